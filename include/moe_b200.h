@@ -1,0 +1,226 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) MoE / QMoE hot path.
+ *
+ * The library libmoe_b200.so implements the com.microsoft MoE and QMoE contrib
+ * operators (opset 1) as hand-written CUDA for sm_100a.  Every entry point takes
+ * plain pointers and sizes, returns a status code and never throws; the message of
+ * the last failure on the calling thread is available from moe_b200_last_error().
+ *
+ * Mapping to the reference plugin (MooreThreads/onnxruntime-musa, paths relative to
+ * its root):
+ *   - the per-op kernel object (create / compute / release) replaces what
+ *     ONNX_OPERATOR_VERSIONED_KERNEL_EX registers and OpKernelBase<Derived> runs
+ *     (musa/ep/src/kernels/utils.h:144-223, kernels/shared_inc/kernel_base.h:33-97);
+ *   - the runtime block replaces the MUSA runtime calls behind device discovery,
+ *     the allocator, the sync stream and data transfer
+ *     (musa/ep/src/ep_factory.cc:389-455, ep_allocator.h:86-278,
+ *      ep_stream.cc:30-185, ep_data_transfer.cc:108-227).
+ * Status codes are the numeric values of OrtErrorCode so a plugin can pass them to
+ * OrtApi::CreateStatus unchanged; element types are ONNX TensorProto codes.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+/* Status codes (values of OrtErrorCode). */
+enum {
+  MOE_B200_OK = 0,
+  MOE_B200_FAIL = 1,
+  MOE_B200_INVALID_ARGUMENT = 2,
+  MOE_B200_NOT_IMPLEMENTED = 9,
+  MOE_B200_EP_FAIL = 11
+};
+
+/* Element types (ONNX TensorProto.DataType). */
+enum {
+  MOE_B200_FLOAT = 1,
+  MOE_B200_UINT8 = 2,
+  MOE_B200_INT32 = 6,
+  MOE_B200_FLOAT16 = 10,
+  MOE_B200_BFLOAT16 = 16
+};
+
+/* activation_type attribute values. */
+enum {
+  MOE_B200_ACT_RELU = 0,
+  MOE_B200_ACT_GELU = 1,
+  MOE_B200_ACT_SILU = 2,
+  MOE_B200_ACT_IDENTITY = 3,
+  MOE_B200_ACT_SWIGLU = 4
+};
+
+/* Attributes of one MoE / QMoE node (the com.microsoft schema's attribute set). */
+typedef struct moe_b200_attrs {
+  int32_t activation_type;          /* MOE_B200_ACT_* */
+  int32_t k;                        /* experts per token */
+  int32_t normalize_routing_weights;
+  int32_t use_sparse_mixer;         /* must be 0 */
+  int32_t swiglu_fusion;            /* 0: fc3 is the linear half; 1 interleaved; 2 halves */
+  float swiglu_limit;               /* +inf disables clamping */
+  float activation_alpha;
+  float activation_beta;
+  int32_t expert_weight_bits;       /* 0 for MoE; 4 or 8 for QMoE */
+  int32_t block_size;               /* QMoE: 0 = one scale per output row */
+} moe_b200_attrs;
+
+/* Shapes of one call.  Weights are [num_experts, N, K], K contiguous. */
+typedef struct moe_b200_problem {
+  int64_t num_rows;        /* T: tokens (rows of input) */
+  int64_t hidden_size;     /* H */
+  int64_t inter_size;      /* I: width of the activation fed to fc2 */
+  int64_t num_experts;     /* E */
+  int32_t dtype;           /* element type of input/router/output (and MoE weights) */
+  int32_t has_fc3;
+  moe_b200_attrs attrs;
+} moe_b200_problem;
+
+/* Device pointers of one call; unused optional inputs are NULL. */
+typedef struct moe_b200_tensors {
+  const void* input;         /* [T, H] */
+  const void* router_probs;  /* [T, E] router logits */
+  const void* fc1_weights;   /* MoE: [E, I or 2I, H]; QMoE: uint8 packed */
+  const void* fc1_scales;    /* QMoE only */
+  const void* fc1_bias;      /* [E, I or 2I] */
+  const void* fc2_weights;   /* [E, H, I] */
+  const void* fc2_scales;
+  const void* fc2_bias;      /* [E, H] */
+  const void* fc3_weights;   /* [E, I, H] */
+  const void* fc3_scales;
+  const void* fc3_bias;      /* [E, I] */
+  void* output;              /* [T, H] */
+} moe_b200_tensors;
+
+/* A tensor as the kernel context presents it (Ort::ConstValue analog). */
+typedef struct moe_b200_tensor_ref {
+  const void* data;   /* device pointer; NULL for an absent optional input */
+  int32_t elem_type;  /* MOE_B200_* element type */
+  int32_t rank;
+  int64_t dims[4];
+} moe_b200_tensor_ref;
+
+typedef struct moe_b200_kernel moe_b200_kernel;
+
+/* ---------------------------------------------------------------- library */
+
+int moe_b200_abi_version(void);
+
+/* Message of the last non-OK status returned on this thread ("" if none). */
+const char* moe_b200_last_error(void);
+
+/* ------------------------------------------------------- operator kernels */
+
+/* Creates the kernel object for one node.  op_type is "MoE" or "QMoE"; attributes
+ * come as name/value strings with the schema's names and defaults.  Replaces the
+ * create lambda of ONNX_OPERATOR_VERSIONED_KERNEL_EX (musa/ep/src/kernels/utils.h:160-207)
+ * and OpKernelBase::CreateKernelImpl (kernels/shared_inc/kernel_base.h:36-43). */
+int moe_b200_kernel_create(const char* op_type, int32_t num_attrs,
+                           const char* const* attr_names,
+                           const char* const* attr_values,
+                           moe_b200_kernel** kernel);
+
+/* Runs the node on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * inputs[] follows the schema's input order; absent optional inputs have
+ * data == NULL.  The output tensor is caller-allocated with the input's shape.
+ * Workspace comes from a per-kernel, per-stream cache (stream-ordered
+ * allocation).  Replaces OpKernelBase::ComputeImpl (kernel_base.h:45-84). */
+int moe_b200_kernel_compute(moe_b200_kernel* kernel, int32_t num_inputs,
+                            const moe_b200_tensor_ref* inputs,
+                            moe_b200_tensor_ref* output, void* stream);
+
+/* Frees the kernel and its cached workspaces.  Replaces
+ * OpKernelBase::ReleaseImpl (kernel_base.h:86-89). */
+int moe_b200_kernel_release(moe_b200_kernel* kernel);
+
+/* ------------------------------------------------ explicit-workspace path */
+
+/* Bytes of device workspace that moe_b200_forward needs for this problem.
+ * Replaces the scratch sizing before AllocateDeviceMemoryOnStream
+ * (musa/ep/src/kernels/shared_inc/kernel_memory.h:241-252). */
+int moe_b200_workspace_size(const moe_b200_problem* problem, size_t* bytes);
+
+/* One MoE (expert_weight_bits == 0) or QMoE layer call on device pointers with a
+ * caller-owned workspace (256-byte aligned, >= moe_b200_workspace_size).  Enqueues
+ * work on `stream` only: no host synchronisation, no allocation. */
+int moe_b200_forward(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* moe_b200_forward plus per-stage device times: stage_ms[0..6] receive the CUDA
+ * event time of route, plan (scan + permutation), gather, QMoE dequantisation,
+ * fc1(+fc3) GEMM, fc2 GEMM and combine, measured on `stream`.  Synchronises the
+ * stream.  A measurement aid; it has no counterpart in the reference. */
+int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                           void* workspace, size_t workspace_bytes, void* stream,
+                           float* stage_ms, int32_t num_stages);
+
+/* ------------------------------------------------------ hot-path stages */
+
+/* Router: softmax + top-k (+ renormalisation) of every row of router_probs
+ * [T, E] (dtype FLOAT/FLOAT16/BFLOAT16).  expert_idx int32 [T, k],
+ * route_weight float [T, k].  Analog of the reference's Softmax + TopK
+ * (musa/ep/src/kernels/math/softmax_impl.mu:49, topk_impl.mu:46-65). */
+int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
+                   int64_t num_experts, int32_t k, int32_t normalize_routing_weights,
+                   int32_t* expert_idx, float* route_weight, void* stream);
+
+/* Dispatch plan for expert_idx [T, k]: expert_offsets int32 [E+1] (exclusive
+ * scan of the counts), permuted_pos int32 [T*k] (position of routed row t*k+j)
+ * and permuted_src int32 [T*k] (inverse).  Order: expert, then token, then slot.
+ * `workspace` must hold moe_b200_permute_workspace_size() bytes. */
+size_t moe_b200_permute_workspace_size(int64_t num_rows, int32_t k,
+                                       int64_t num_experts);
+int moe_b200_permute(const int32_t* expert_idx, int64_t num_rows, int32_t k,
+                     int64_t num_experts, int32_t* expert_offsets,
+                     int32_t* permuted_pos, int32_t* permuted_src,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------ runtime (CUDA retarget) */
+
+typedef struct moe_b200_device_props {
+  char name[256];
+  uint32_t vendor_id;        /* 0x10DE */
+  int32_t device_id;
+  int32_t sm_count;
+  int32_t cc_major, cc_minor;
+  uint64_t total_memory;
+  int32_t pci_bus_id;
+} moe_b200_device_props;
+
+/* Device discovery (musa/ep/src/ep_factory.cc:389-455). */
+int moe_b200_device_count(int32_t* count);
+int moe_b200_device_props_get(int32_t device_id, moe_b200_device_props* props);
+int moe_b200_set_device(int32_t device_id);
+
+/* Allocator (musa/ep/src/ep_allocator.h:86-321). */
+int moe_b200_alloc(size_t bytes, void** ptr);
+int moe_b200_free(void* ptr);
+int moe_b200_alloc_pinned(size_t bytes, void** ptr);
+int moe_b200_free_pinned(void* ptr);
+
+/* Sync stream and notification (musa/ep/src/ep_stream.cc:30-185). */
+int moe_b200_stream_create(void** stream);
+int moe_b200_stream_destroy(void* stream);
+int moe_b200_stream_synchronize(void* stream);
+int moe_b200_notification_create(void** event);
+int moe_b200_notification_activate(void* event, void* stream);   /* record */
+int moe_b200_notification_wait(void* event, void* stream);       /* stream wait */
+int moe_b200_notification_synchronize(void* event);              /* host wait */
+int moe_b200_notification_destroy(void* event);
+
+/* Data transfer (musa/ep/src/ep_data_transfer.cc:108-227).  kind: 1 = H2D,
+ * 2 = D2H, 3 = D2D.  D2H synchronises `stream` before returning. */
+int moe_b200_copy(void* dst, const void* src, size_t bytes, int32_t kind,
+                  void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* MOE_B200_H_ */

@@ -1,0 +1,436 @@
+// Grouped expert GEMM on the 5th-generation tensor cores (tcgen05) for sm_100a.
+//
+// One persistent CTA per SM walks a device-side tile list (expert, n-tile, m-tile)
+// built from the per-expert row offsets, so no host round trip is needed between
+// routing and the GEMM.  Per CTA, warp-specialised:
+//   warp 0      TMA producer: A tile 128x64 (permuted activations) and B tile
+//               256x64 (one expert's weight rows) per stage, 128-byte swizzle.
+//   warp 1      MMA issuer: tcgen05.mma kind::f16, M=128 N=256 K=16, fp32
+//               accumulator in TMEM; two accumulators (2 x 256 columns) so the
+//               epilogue of tile i overlaps the mainloop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld of its 32-lane quarter, bias + activation
+//               (gated: act(g) * u, where columns 0..127 hold the gate tile and
+//               128..255 the linear tile of the same 128 output columns), and a
+//               store of the 16-bit result rows.  Rows of the tile that belong to
+//               the next expert are computed but never stored.
+// Reference analog: muDNN MatMul / muBLAS GemmStridedBatched plus GemmPostKernel
+// (musa/ep/src/kernels/math/matmul.cc:239-332, shared_inc/blas_utils.h:237-262,
+//  math/gemm_post_kernels.mu:27-53), which this single kernel replaces.
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+#include "moe_kernels.h"
+
+namespace moe {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;  // MMA N (gated: 128 gate + 128 linear)
+constexpr int BK = 64;   // one 128-byte swizzle atom of 16-bit elements
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int B_HALF = B_BYTES / 2;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES =
+    1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + 64 * 8 /*barriers*/ +
+    2 * (kMaxExperts + 1) * 4;
+
+struct TcParams {
+  const int32_t* offsets;
+  const int32_t* tiles128;
+  int E;
+  int K;
+  int N;            // output columns
+  int n_tiles;      // per expert
+  int gated;
+  int b1_g, b3_g;   // interleave coordinates
+  int b1_noff, b3_noff;
+  const void* bias1;
+  const void* bias3;
+  int bias_stride;
+  int64_t bias_e_stride;
+  ActParams ap;
+  void* out;
+  int64_t ldo;
+  int* err;
+};
+
+__device__ __forceinline__ void decode_tile(int L, const int32_t* s_tiles, int E, int n_tiles,
+                                            int& e, int& m, int& n) {
+  // Largest e with s_tiles[e] * n_tiles <= L.
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_tiles[mid] * n_tiles <= L) lo = mid; else hi = mid - 1;
+  }
+  e = lo;
+  const int local = L - s_tiles[e] * n_tiles;
+  const int mt = s_tiles[e + 1] - s_tiles[e];
+  n = local / mt;  // m fastest: the m-tiles of one weight tile run back to back (L2 reuse)
+  m = local - n * mt;
+}
+
+template <typename T>
+__device__ __forceinline__ float bias_val(const void* bias, int e, int n, const TcParams& p) {
+  if (bias == nullptr) return 0.f;
+  return to_f(static_cast<const T*>(bias)[e * p.bias_e_stride +
+                                          static_cast<int64_t>(n) * p.bias_stride]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store16(T* dst, const float (&v)[16], int valid_cols) {
+  if (valid_cols >= 16) {
+    uint4 o0, o1;
+    uint32_t* w0 = reinterpret_cast<uint32_t*>(&o0);
+    uint32_t* w1 = reinterpret_cast<uint32_t*>(&o1);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      w0[q] = pack2<T>(v[2 * q], v[2 * q + 1]);
+      w1[q] = pack2<T>(v[8 + 2 * q], v[8 + 2 * q + 1]);
+    }
+    reinterpret_cast<uint4*>(dst)[0] = o0;
+    reinterpret_cast<uint4*>(dst)[1] = o1;
+  } else {
+    for (int q = 0; q < valid_cols; ++q) dst[q] = from_f<T>(v[q]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS, 1)
+tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b1,
+                       const __grid_constant__ CUtensorMap map_b3, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint64_t* done = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_tiles = reinterpret_cast<int32_t*>(bars + 64);
+  int32_t* s_offs = s_tiles + (kMaxExperts + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = p.E;
+
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_tiles[i] = p.tiles128[i];
+    s_offs[i] = p.offsets[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b1);
+    if (p.gated) tma_prefetch_desc(&map_b3);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = s_tiles[E] * p.n_tiles;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int L = blockIdx.x; L < total && !*abort_flag; L += gridDim.x) {
+        int e, m, n;
+        decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
+        const int row0 = s_offs[e] + m * BM;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            atomicExch(p.err, kErrTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          const int kc = kb * BK;
+          tma_load_2d(a_dst, &map_a, &full[stage], kc, row0);
+          if (p.gated) {
+            const int n0 = n * (BN / 2);
+            tma_load_4d(b_dst, &map_b1, &full[stage], kc, p.b1_g, n0 + p.b1_noff, e);
+            tma_load_4d(b_dst + B_HALF, &map_b3, &full[stage], kc, p.b3_g, n0 + p.b3_noff, e);
+          } else {
+            const int n0 = n * BN;
+            tma_load_4d(b_dst, &map_b1, &full[stage], kc, p.b1_g, n0 + p.b1_noff, e);
+            tma_load_4d(b_dst + B_HALF, &map_b1, &full[stage], kc, p.b1_g,
+                        n0 + BN / 2 + p.b1_noff, e);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      const uint32_t idesc = idesc_f16(kFmt, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      for (int L = blockIdx.x; L < total && !*abort_flag; L += gridDim.x, ++i) {
+        const int acc = i & 1;
+        const uint32_t acc_phase = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+          atomicExch(p.err, kErrTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            atomicExch(p.err, kErrTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = smem_desc_k_sw128(a_addr + kk * 32);
+            const uint64_t bd = smem_desc_k_sw128(b_addr + kk * 32);
+            tc_mma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+      }
+      // All MMAs of this CTA have retired once `done` completes.
+      tc_commit(done);
+      mbar_wait(done, 0);
+    }
+  } else {
+    // ----------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r_in_tile = q * 32 + lane;
+    T* out = static_cast<T*>(p.out);
+    int i = 0;
+    for (int L = blockIdx.x; L < total && !*abort_flag; L += gridDim.x, ++i) {
+      const int acc = i & 1;
+      const uint32_t acc_phase = (i >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase)) {
+        atomicExch(p.err, kErrTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int e, m, n;
+      decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
+      const int row = s_offs[e] + m * BM + r_in_tile;
+      const bool valid = row < s_offs[e + 1];
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      T* orow = out + static_cast<int64_t>(row) * p.ldo;
+      if (p.gated) {
+        const int n0 = n * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 16) {
+          float g[16], u[16];
+          tmem_ld16(taddr + c, g);
+          tmem_ld16(taddr + BN / 2 + c, u);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (valid && col < p.N) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int cj = min(col + j, p.N - 1);
+              v[j] = act_gated(p.ap, g[j] + bias_val<T>(p.bias1, e, cj, p),
+                               u[j] + bias_val<T>(p.bias3, e, cj, p));
+            }
+            store16<T>(orow + col, v, p.N - col);
+          }
+        }
+      } else {
+        const int n0 = n * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float a[16];
+          tmem_ld16(taddr + c, a);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (valid && col < p.N) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int cj = min(col + j, p.N - 1);
+              v[j] = act_single(p.ap.act, a[j] + bias_val<T>(p.bias1, e, cj, p));
+            }
+            store16<T>(orow + col, v, p.N - col);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+CUtensorMapDataType tma_dtype(int dt) {
+  return dt == kDtBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// A: [rows, K] row-major, box 128 rows x 64 columns.
+bool make_map_a(CUtensorMap* m, int dt, const void* ptr, int64_t rows, int K) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  cuuint32_t box[2] = {BK, BM};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, tma_dtype(dt), 2, const_cast<void*>(ptr), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+// B: weights of all experts viewed as [E][Nrows/G][G][K], box 1 x 128 x 1 x 64.
+bool make_map_b(CUtensorMap* m, int dt, const GemmOperandB& b, int K, int E) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t rows_g = static_cast<cuuint64_t>(b.n_rows / b.G);
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(b.G), rows_g,
+                        static_cast<cuuint64_t>(E)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(K) * 2,
+                           static_cast<cuuint64_t>(K) * 2 * b.G,
+                           static_cast<cuuint64_t>(K) * 2 * b.n_rows};
+  cuuint32_t box[4] = {BK, 1, BN / 2, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return enc(m, tma_dtype(dt), 4, const_cast<void*>(b.ptr), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <typename T>
+cudaError_t launch_t(const GemmArgs& g, int num_sms, cudaStream_t s) {
+  CUtensorMap ma, mb1, mb3;
+  if (!make_map_a(&ma, g.dtype, g.a, g.rows, g.K)) return cudaErrorInvalidValue;
+  if (!make_map_b(&mb1, g.dtype, g.b1, g.K, g.E)) return cudaErrorInvalidValue;
+  if (g.gated) {
+    if (!make_map_b(&mb3, g.dtype, g.b3, g.K, g.E)) return cudaErrorInvalidValue;
+  } else {
+    mb3 = mb1;
+  }
+  TcParams p;
+  p.offsets = g.offsets;
+  p.tiles128 = g.tiles128;
+  p.E = g.E;
+  p.K = g.K;
+  p.N = g.N;
+  p.gated = g.gated ? 1 : 0;
+  p.n_tiles = g.gated ? (g.N + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN;
+  p.b1_g = g.b1.g;
+  p.b3_g = g.b3.g;
+  p.b1_noff = g.b1.n_off;
+  p.b3_noff = g.b3.n_off;
+  p.bias1 = g.bias1;
+  p.bias3 = g.bias3;
+  p.bias_stride = g.bias_stride;
+  p.bias_e_stride = g.bias_e_stride;
+  p.ap = g.ap;
+  p.out = g.out;
+  p.ldo = g.ldo;
+  p.err = g.err;
+  static bool attr_set = false;  // benign race: the attribute call is idempotent
+  if (!attr_set) {
+    cudaError_t st = cudaFuncSetAttribute(tc_grouped_gemm_kernel<T>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          SMEM_BYTES);
+    if (st != cudaSuccess) return st;
+    attr_set = true;
+  }
+  // The real tile count lives on the device; an upper bound sizes the grid.
+  const int64_t ub_m = (g.rows + BM - 1) / BM + g.E;
+  const int64_t ub = ub_m * p.n_tiles;
+  const int grid = static_cast<int>(std::min<int64_t>(ub, num_sms));
+  tc_grouped_gemm_kernel<T><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb1, mb3, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_supported(const GemmArgs& g) {
+  if (g.dtype != kDtF16 && g.dtype != kDtBF16) return false;
+  if (g.K % 8 != 0 || g.K <= 0) return false;
+  if (g.ldo % 8 != 0) return false;
+  if (g.E > kMaxExperts) return false;
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!aligned(g.a) || !aligned(g.b1.ptr) || !aligned(g.out)) return false;
+  if (g.gated && !aligned(g.b3.ptr)) return false;
+  return get_encode_fn() != nullptr;
+}
+
+cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
+  if (g.rows == 0 || g.N == 0) return cudaSuccess;
+  if (g.dtype == kDtF16) return launch_t<__half>(g, num_sms, s);
+  if (g.dtype == kDtBF16) return launch_t<__nv_bfloat16>(g, num_sms, s);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace moe

@@ -1,0 +1,458 @@
+// Host side of libmoe_b200: problem validation, workspace planning, the launch
+// sequence of one MoE / QMoE layer call, the per-node kernel object and the thin
+// CUDA runtime layer that stands in for the reference's MUSA runtime plumbing.
+//
+// Call sequence of one layer (all on the caller's stream, no host sync):
+//   route       softmax/top-k per row + per-chunk expert histogram
+//   plan        per-expert offsets (exclusive scan), GEMM tile prefixes, stable
+//               permutation (expert, token, slot)
+//   gather      x rows -> expert-contiguous activations Xp
+//   fc1(+fc3)   grouped GEMM, activation fused in the epilogue  -> act [R, I]
+//   fc2         grouped GEMM, bias fused                          -> Y [R, H] (aliases Xp)
+//   combine     out[t] = sum_j w[t, j] * Y[pos[t, j]]
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "moe_kernels.h"
+#include "qmoe.h"
+
+using namespace moe;
+
+// ------------------------------------------------------------------ errors
+namespace {
+
+thread_local std::string g_last_error;
+
+}  // namespace
+
+int moe::set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+namespace {
+
+template <typename... A>
+int fail(int code, const char* fmt, A... args) {
+  return moe::set_error(code, fmt, args...);
+}
+int fail(int code, const char* msg) { return moe::set_error(code, "%s", msg); }
+
+int cuda_fail(cudaError_t st, const char* what) {
+  return fail(MOE_B200_EP_FAIL, "%s: %s", what, cudaGetErrorString(st));
+}
+
+#define MOE_CUDA_CHECK(expr, what)                   \
+  do {                                               \
+    cudaError_t _st = (expr);                        \
+    if (_st != cudaSuccess) return cuda_fail(_st, what); \
+  } while (0)
+
+bool env_flag(const char* name) {
+  const char* v = std::getenv(name);
+  return v != nullptr && v[0] != '\0' && std::strcmp(v, "0") != 0;
+}
+
+int device_sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (counts[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = n > 0 ? n : 148;
+  }
+  return counts[dev];
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+bool is_float_type(int dt) {
+  return dt == MOE_B200_FLOAT || dt == MOE_B200_FLOAT16 || dt == MOE_B200_BFLOAT16;
+}
+
+// ------------------------------------------------------------ workspace plan
+struct WsLayout {
+  size_t idx, w, chunk_counts, chunk_base, offsets, tiles128, tiles64, pos, src, err;
+  size_t xp, act, qmoe, total;
+};
+
+bool swiglu_fused(const moe_b200_problem& p) {
+  return p.attrs.activation_type == MOE_B200_ACT_SWIGLU && p.attrs.swiglu_fusion != 0;
+}
+
+WsLayout plan_workspace(const moe_b200_problem& p) {
+  WsLayout L{};
+  const int64_t T = p.num_rows, E = p.num_experts, k = p.attrs.k;
+  const int64_t R = T * k;
+  const int64_t chunks = num_route_chunks(T);
+  const size_t es = static_cast<size_t>(dtype_bytes(p.dtype));
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
+  L.idx = take(R * 4);
+  L.w = take(R * 4);
+  L.chunk_counts = take(std::max<int64_t>(chunks, 1) * E * 4);
+  L.chunk_base = take(std::max<int64_t>(chunks, 1) * E * 4);
+  L.offsets = take((E + 1) * 4);
+  L.tiles128 = take((E + 1) * 4);
+  L.tiles64 = take((E + 1) * 4);
+  L.pos = take(R * 4);
+  L.src = take(R * 4);
+  L.err = take(16);
+  L.xp = take(R * p.hidden_size * es);   // gathered input, later fc2 output
+  L.act = take(R * p.inter_size * es);
+  L.qmoe = take(qmoe_workspace_bytes(p));
+  L.total = o;
+  return L;
+}
+
+int validate_problem(const moe_b200_problem* p) {
+  if (p == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "problem is NULL");
+  if (!is_float_type(p->dtype))
+    return fail(MOE_B200_NOT_IMPLEMENTED, "unsupported element type %d", p->dtype);
+  if (p->num_rows < 0 || p->hidden_size <= 0 || p->inter_size <= 0 || p->num_experts <= 0)
+    return fail(MOE_B200_INVALID_ARGUMENT,
+                "invalid shape: num_rows=%lld hidden=%lld inter=%lld experts=%lld",
+                (long long)p->num_rows, (long long)p->hidden_size, (long long)p->inter_size,
+                (long long)p->num_experts);
+  if (p->num_experts > kMaxExperts)
+    return fail(MOE_B200_NOT_IMPLEMENTED, "num_experts=%lld exceeds %d",
+                (long long)p->num_experts, kMaxExperts);
+  const auto& a = p->attrs;
+  if (a.k < 1 || a.k > p->num_experts || a.k > kMaxK)
+    return fail(MOE_B200_INVALID_ARGUMENT, "k=%d must be in [1, min(num_experts, %d)]", a.k,
+                kMaxK);
+  if (a.activation_type < MOE_B200_ACT_RELU || a.activation_type > MOE_B200_ACT_SWIGLU)
+    return fail(MOE_B200_INVALID_ARGUMENT, "invalid activation_type %d", a.activation_type);
+  if (a.use_sparse_mixer != 0)
+    return fail(MOE_B200_NOT_IMPLEMENTED, "use_sparse_mixer=1 is not supported");
+  if (a.swiglu_fusion < 0 || a.swiglu_fusion > 2)
+    return fail(MOE_B200_INVALID_ARGUMENT, "swiglu_fusion=%d must be 0, 1 or 2", a.swiglu_fusion);
+  if (a.activation_type == MOE_B200_ACT_SWIGLU && a.swiglu_fusion == 0 && !p->has_fc3)
+    return fail(MOE_B200_INVALID_ARGUMENT,
+                "activation_type=swiglu with swiglu_fusion=0 needs fc3 weights");
+  if (a.swiglu_fusion != 0 && p->has_fc3)
+    return fail(MOE_B200_INVALID_ARGUMENT, "fused swiglu (swiglu_fusion=%d) excludes fc3",
+                a.swiglu_fusion);
+  if (a.expert_weight_bits != 0 && a.expert_weight_bits != 4 && a.expert_weight_bits != 8)
+    return fail(MOE_B200_INVALID_ARGUMENT, "expert_weight_bits=%d must be 4 or 8",
+                a.expert_weight_bits);
+  if (a.expert_weight_bits != 0) {
+    if (p->dtype == MOE_B200_FLOAT)
+      return fail(MOE_B200_NOT_IMPLEMENTED, "QMoE with float32 activations is not supported");
+    if (a.block_size != 0 && (a.block_size < 16 || (a.block_size & (a.block_size - 1)) != 0))
+      return fail(MOE_B200_INVALID_ARGUMENT,
+                  "block_size=%d must be 0 or a power of two >= 16", a.block_size);
+    if (a.expert_weight_bits == 4 && ((p->hidden_size | p->inter_size) & 1))
+      return fail(MOE_B200_INVALID_ARGUMENT, "4-bit weights need even hidden and inter sizes");
+  }
+  const int64_t R = p->num_rows * a.k;
+  if (R > (int64_t)1 << 30)
+    return fail(MOE_B200_INVALID_ARGUMENT, "num_rows * k = %lld is too large", (long long)R);
+  return MOE_B200_OK;
+}
+
+ActParams act_params(const moe_b200_attrs& a) {
+  ActParams ap;
+  ap.act = a.activation_type;
+  ap.alpha = a.activation_alpha;
+  ap.beta = a.activation_beta;
+  ap.limit = a.swiglu_limit;
+  return ap;
+}
+
+// fc1 (+fc3) pass description for MoE weights of element type p.dtype (or the
+// dequantised copies of QMoE weights).
+GemmArgs fc1_args(const moe_b200_problem& p, const void* w1, const void* b1, const void* w3,
+                  const void* b3) {
+  const int I = static_cast<int>(p.inter_size);
+  const int H = static_cast<int>(p.hidden_size);
+  GemmArgs g{};
+  g.dtype = p.dtype;
+  g.K = H;
+  g.N = I;
+  g.E = static_cast<int>(p.num_experts);
+  g.ap = act_params(p.attrs);
+  g.bias_stride = 1;
+  if (p.has_fc3) {
+    g.gated = true;
+    g.b1 = {w1, 0, 1, 0, I};
+    g.b3 = {w3, 0, 1, 0, I};
+    g.bias1 = b1;
+    g.bias3 = b3;
+    g.bias_e_stride = I;
+  } else if (swiglu_fused(p)) {
+    const size_t es = dtype_bytes(p.dtype);
+    g.gated = true;
+    g.bias_e_stride = 2 * I;
+    if (p.attrs.swiglu_fusion == 1) {
+      g.b1 = {w1, 0, 2, 0, 2 * I};
+      g.b3 = {w1, 1, 2, 0, 2 * I};
+      g.bias1 = b1;
+      g.bias3 = b1 ? static_cast<const uint8_t*>(b1) + es : nullptr;
+      g.bias_stride = 2;
+    } else {
+      g.b1 = {w1, 0, 1, 0, 2 * I};
+      g.b3 = {w1, 0, 1, I, 2 * I};
+      g.bias1 = b1;
+      g.bias3 = b1 ? static_cast<const uint8_t*>(b1) + es * I : nullptr;
+    }
+  } else {
+    g.gated = false;
+    g.b1 = {w1, 0, 1, 0, I};
+    g.bias1 = b1;
+    g.bias_e_stride = I;
+  }
+  return g;
+}
+
+GemmArgs fc2_args(const moe_b200_problem& p, const void* w2, const void* b2) {
+  const int I = static_cast<int>(p.inter_size);
+  const int H = static_cast<int>(p.hidden_size);
+  GemmArgs g{};
+  g.dtype = p.dtype;
+  g.K = I;
+  g.N = H;
+  g.E = static_cast<int>(p.num_experts);
+  g.gated = false;
+  g.b1 = {w2, 0, 1, 0, H};
+  g.bias1 = b2;
+  g.bias_stride = 1;
+  g.bias_e_stride = H;
+  g.ap = ActParams{kIdentity, 1.f, 0.f, INFINITY};
+  return g;
+}
+
+cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
+  if (!env_flag("MOE_B200_FORCE_SIMT") && tc_supported(g))
+    return launch_gemm_tc(g, device_sm_count(), s);
+  return launch_gemm_simt(g, s);
+}
+
+// Stage boundaries recorded when `ev` is non-NULL (kNumStages + 1 events).
+enum Stage { kStRoute = 0, kStPlan, kStGather, kStDequant, kStFc1, kStFc2, kStCombine, kNumStages };
+
+int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
+                 size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev = nullptr) {
+  auto mark = [&](int i) { if (ev) cudaEventRecord(ev[i], s); };
+  const WsLayout L = plan_workspace(p);
+  if (ws_bytes < L.total)
+    return fail(MOE_B200_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than %zu",
+                ws_bytes, L.total);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+    return fail(MOE_B200_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  if (t.input == nullptr || t.router_probs == nullptr || t.output == nullptr ||
+      t.fc1_weights == nullptr || t.fc2_weights == nullptr)
+    return fail(MOE_B200_INVALID_ARGUMENT, "input, router_probs, fc1/fc2 weights and output "
+                                           "must be non-NULL");
+  if (p.has_fc3 && t.fc3_weights == nullptr)
+    return fail(MOE_B200_INVALID_ARGUMENT, "has_fc3 is set but fc3_weights is NULL");
+  const int T = static_cast<int>(p.num_rows);
+  const int E = static_cast<int>(p.num_experts);
+  const int k = p.attrs.k;
+  const int H = static_cast<int>(p.hidden_size);
+  const int I = static_cast<int>(p.inter_size);
+  const int64_t R = static_cast<int64_t>(T) * k;
+  if (T == 0) return MOE_B200_OK;
+
+  auto* idx = reinterpret_cast<int32_t*>(ws + L.idx);
+  auto* w = reinterpret_cast<float*>(ws + L.w);
+  auto* cc = reinterpret_cast<int32_t*>(ws + L.chunk_counts);
+  auto* cb = reinterpret_cast<int32_t*>(ws + L.chunk_base);
+  auto* offs = reinterpret_cast<int32_t*>(ws + L.offsets);
+  auto* t128 = reinterpret_cast<int32_t*>(ws + L.tiles128);
+  auto* t64 = reinterpret_cast<int32_t*>(ws + L.tiles64);
+  auto* pos = reinterpret_cast<int32_t*>(ws + L.pos);
+  auto* src = reinterpret_cast<int32_t*>(ws + L.src);
+  auto* err = reinterpret_cast<int*>(ws + L.err);
+  void* xp = ws + L.xp;
+  void* act = ws + L.act;
+
+  MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, sizeof(int), s), "clear error word");
+  mark(kStRoute);
+  MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
+                              p.attrs.normalize_routing_weights, idx, w, cc, s),
+                 "route");
+  mark(kStPlan);
+  MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, pos, src, s), "plan");
+  const size_t es = dtype_bytes(p.dtype);
+  mark(kStGather);
+  MOE_CUDA_CHECK(launch_gather(t.input, static_cast<int64_t>(H) * es, k, src, R, xp, s),
+                 "gather");
+
+  const void* w1 = t.fc1_weights;
+  const void* w2 = t.fc2_weights;
+  const void* w3 = t.fc3_weights;
+  mark(kStDequant);
+  if (p.attrs.expert_weight_bits != 0) {
+    // QMoE: dequantise the weights of every expert into the workspace, then run the
+    // same grouped GEMMs.  (Small-T decode takes the weight-streaming path instead.)
+    QmoeDequantOut dq;
+    int st = qmoe_dequantize(p, t, ws + L.qmoe, offs, &dq, s);
+    if (st != MOE_B200_OK) return st;
+    w1 = dq.w1;
+    w2 = dq.w2;
+    w3 = dq.w3;
+  }
+
+  GemmArgs g1 = fc1_args(p, w1, t.fc1_bias, w3, t.fc3_bias);
+  g1.a = xp;
+  g1.rows = R;
+  g1.offsets = offs;
+  g1.tiles128 = t128;
+  g1.tiles64 = t64;
+  g1.out = act;
+  g1.ldo = I;
+  g1.err = err;
+  mark(kStFc1);
+  MOE_CUDA_CHECK(run_gemm(g1, s), "fc1 grouped GEMM");
+
+  GemmArgs g2 = fc2_args(p, w2, t.fc2_bias);
+  g2.a = act;
+  g2.rows = R;
+  g2.offsets = offs;
+  g2.tiles128 = t128;
+  g2.tiles64 = t64;
+  g2.out = xp;  // Y aliases the gathered input, dead after fc1
+  g2.ldo = H;
+  g2.err = err;
+  mark(kStFc2);
+  MOE_CUDA_CHECK(run_gemm(g2, s), "fc2 grouped GEMM");
+
+  mark(kStCombine);
+  MOE_CUDA_CHECK(launch_combine(p.dtype, xp, pos, w, T, k, H, t.output, s), "combine");
+  mark(kNumStages);
+
+  if (env_flag("MOE_B200_TRACE_SYNC")) {
+    MOE_CUDA_CHECK(cudaStreamSynchronize(s), "stream synchronize");
+    int herr = 0;
+    MOE_CUDA_CHECK(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+    if (herr != 0) return fail(MOE_B200_EP_FAIL, "device error code %d", herr);
+  }
+  return MOE_B200_OK;
+}
+
+}  // namespace
+
+// ==================================================================== C ABI
+extern "C" {
+
+int moe_b200_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+const char* moe_b200_last_error(void) { return g_last_error.c_str(); }
+
+int moe_b200_workspace_size(const moe_b200_problem* problem, size_t* bytes) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  if (bytes == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "bytes is NULL");
+  *bytes = plan_workspace(*problem).total;
+  return MOE_B200_OK;
+}
+
+int moe_b200_forward(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  if (t == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "tensors is NULL");
+  return forward_impl(*problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                           void* workspace, size_t workspace_bytes, void* stream,
+                           float* stage_ms, int32_t num_stages) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  if (t == nullptr || stage_ms == nullptr || num_stages < kNumStages)
+    return fail(MOE_B200_INVALID_ARGUMENT, "tensors/stage_ms NULL or num_stages < %d", kNumStages);
+  cudaEvent_t ev[kNumStages + 1];
+  for (int i = 0; i <= kNumStages; ++i) MOE_CUDA_CHECK(cudaEventCreate(&ev[i]), "cudaEventCreate");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = forward_impl(*problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes, s, ev);
+  if (st == MOE_B200_OK && problem->num_rows > 0) {
+    cudaError_t ce = cudaEventSynchronize(ev[kNumStages]);
+    for (int i = 0; i < kNumStages && ce == cudaSuccess; ++i)
+      ce = cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]);
+    if (ce != cudaSuccess) st = cuda_fail(ce, "stage timing");
+  } else if (st == MOE_B200_OK) {
+    for (int i = 0; i < kNumStages; ++i) stage_ms[i] = 0.f;
+  }
+  for (int i = 0; i <= kNumStages; ++i) cudaEventDestroy(ev[i]);
+  return st;
+}
+
+int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
+                   int64_t num_experts, int32_t k, int32_t normalize_routing_weights,
+                   int32_t* expert_idx, float* route_weight, void* stream) {
+  if (!is_float_type(dtype)) return fail(MOE_B200_NOT_IMPLEMENTED, "unsupported dtype %d", dtype);
+  if (num_experts < 1 || num_experts > kMaxExperts || k < 1 || k > num_experts || k > kMaxK ||
+      num_rows < 0)
+    return fail(MOE_B200_INVALID_ARGUMENT, "invalid routing shape");
+  if (num_rows == 0) return MOE_B200_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* cc = nullptr;
+  // The histogram of this standalone call is not needed; give it a scratch buffer.
+  const size_t bytes = static_cast<size_t>(num_route_chunks(num_rows)) * num_experts * 4;
+  MOE_CUDA_CHECK(cudaMallocAsync(reinterpret_cast<void**>(&cc), bytes, s), "alloc");
+  cudaError_t e = launch_route(dtype, router_probs, static_cast<int>(num_rows),
+                               static_cast<int>(num_experts), k, normalize_routing_weights,
+                               expert_idx, route_weight, cc, s);
+  cudaFreeAsync(cc, s);
+  if (e != cudaSuccess) return cuda_fail(e, "route");
+  return MOE_B200_OK;
+}
+
+size_t moe_b200_permute_workspace_size(int64_t num_rows, int32_t k, int64_t num_experts) {
+  (void)k;
+  const size_t chunks = std::max<int64_t>(num_route_chunks(num_rows), 1);
+  return align_up(chunks * num_experts * 4, 256) * 2 + align_up((num_experts + 1) * 4, 256) * 2 +
+         256;
+}
+
+int moe_b200_permute(const int32_t* expert_idx, int64_t num_rows, int32_t k,
+                     int64_t num_experts, int32_t* expert_offsets, int32_t* permuted_pos,
+                     int32_t* permuted_src, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  if (num_experts < 1 || num_experts > kMaxExperts || k < 1 || num_rows < 0)
+    return fail(MOE_B200_INVALID_ARGUMENT, "invalid permutation shape");
+  if (workspace_bytes < moe_b200_permute_workspace_size(num_rows, k, num_experts))
+    return fail(MOE_B200_INVALID_ARGUMENT, "permute workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t chunks = std::max<int64_t>(num_route_chunks(num_rows), 1);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t cbytes = align_up(chunks * num_experts * 4, 256);
+  const size_t tbytes = align_up((num_experts + 1) * 4, 256);
+  auto* cc = reinterpret_cast<int32_t*>(ws);
+  auto* cb = reinterpret_cast<int32_t*>(ws + cbytes);
+  auto* t128 = reinterpret_cast<int32_t*>(ws + 2 * cbytes);
+  auto* t64 = reinterpret_cast<int32_t*>(ws + 2 * cbytes + tbytes);
+  auto* err = reinterpret_cast<int*>(ws + 2 * cbytes + 2 * tbytes);
+  const int T = static_cast<int>(num_rows), E = static_cast<int>(num_experts);
+  MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, sizeof(int), s), "clear error word");
+  if (T == 0) MOE_CUDA_CHECK(cudaMemsetAsync(cc, 0, cbytes, s), "clear counts");
+  MOE_CUDA_CHECK(launch_histogram(expert_idx, T, k, E, cc, err, s), "histogram");
+  MOE_CUDA_CHECK(launch_plan(expert_idx, T, k, E, cc, cb, expert_offsets, t128, t64,
+                             permuted_pos, permuted_src, s),
+                 "plan");
+  int herr = 0;
+  MOE_CUDA_CHECK(cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s),
+                 "read error word");
+  MOE_CUDA_CHECK(cudaStreamSynchronize(s), "stream synchronize");
+  if (herr == kErrBadExpert) return fail(MOE_B200_INVALID_ARGUMENT, "expert index out of range");
+  return MOE_B200_OK;
+}
+
+}  // extern "C"

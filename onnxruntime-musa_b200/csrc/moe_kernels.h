@@ -1,0 +1,83 @@
+// Internal launch interface between the host planner (moe_api.cu) and the device
+// kernels.  Not part of the public C ABI.
+#pragma once
+
+#include "common.cuh"
+
+namespace moe {
+
+// Element type ids (ONNX TensorProto codes, as in the C ABI).
+constexpr int kDtF32 = 1;
+constexpr int kDtU8 = 2;
+constexpr int kDtF16 = 10;
+constexpr int kDtBF16 = 16;
+
+// Records `fmt` as this thread's last error message (read by moe_b200_last_error)
+// and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+inline int dtype_bytes(int dt) { return dt == kDtF32 ? 4 : (dt == kDtU8 ? 1 : 2); }
+
+// Routing chunk: rows handled by one CTA of the router / permutation kernels.
+constexpr int kRouteThreads = 256;
+constexpr int kRouteChunk = 256;
+inline int num_route_chunks(int64_t rows) {
+  return static_cast<int>((rows + kRouteChunk - 1) / kRouteChunk);
+}
+constexpr int kMaxExperts = 256;
+constexpr int kMaxK = 32;
+
+cudaError_t launch_route(int dtype, const void* logits, int T, int E, int k, int normalize,
+                         int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s);
+cudaError_t launch_histogram(const int32_t* idx, int T, int k, int E, int32_t* chunk_counts,
+                             int* err, cudaStream_t s);
+cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* chunk_counts,
+                        int32_t* chunk_base, int32_t* offsets, int32_t* tiles128,
+                        int32_t* tiles64, int32_t* pos, int32_t* src, cudaStream_t s);
+cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
+                          int64_t rows, void* xp, cudaStream_t s);
+cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
+                           int T, int k, int H, void* out, cudaStream_t s);
+
+// One grouped GEMM pass over all experts:
+//   out[r, n] = epilogue( sum_k A[r, k] * B1[e(r), n, k] [, sum_k A[r, k] * B3[e(r), n, k]] )
+// for every permuted row r of expert e (rows offsets[e] .. offsets[e+1]).
+// B matrices are addressed as [E][Nrows][G][K] with element (e, n, g, k) at
+//   b + e*b_e_stride + (n*G + g)*K + k, so an interleaved fused fc1 (G=2) selects its
+// gate (g=0) and linear (g=1) rows by g; a split fc1 selects halves by n offset.
+struct GemmOperandB {
+  const void* ptr;     // weights of all experts
+  int g;               // interleave selector (0 or 1)
+  int G;               // interleave factor (1 or 2)
+  int n_off;           // row offset (split fc1: I for the linear half)
+  int n_rows;          // rows of one expert's matrix (as stored: N*G + ...)
+};
+
+struct GemmArgs {
+  int dtype;                   // element type of A, B and out
+  const void* a;               // [R, K] permuted activations
+  int64_t rows;                // R
+  int K;
+  int N;                       // output columns
+  bool gated;                  // two B operands combined by act_gated
+  GemmOperandB b1, b3;         // b3 used when gated
+  const int32_t* offsets;      // [E+1]
+  const int32_t* tiles128;     // [E+1] prefix of ceil(count/128)
+  const int32_t* tiles64;      // [E+1] prefix of ceil(count/64)
+  int E;
+  const void* bias1;           // element (e, n) at bias1[e*bias_e_stride + n*bias_stride]
+  const void* bias3;
+  int bias_stride;
+  int64_t bias_e_stride;
+  ActParams ap;                // plain: act applied to (acc + bias1); kIdentity for fc2
+  void* out;                   // [R, N]
+  int64_t ldo;
+  int* err;
+};
+
+cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);
+// tcgen05 path; requires dtype f16/bf16, K % 8 == 0.
+bool tc_supported(const GemmArgs& g);
+cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s);
+
+}  // namespace moe

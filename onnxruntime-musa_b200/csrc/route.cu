@@ -1,0 +1,351 @@
+// Router (softmax + top-k + renormalisation), dispatch plan (per-expert histogram,
+// exclusive scan, stable permutation) and the row gather into expert-contiguous
+// order.  All integer results are deterministic: no atomic slot claiming.
+//
+// Reference analogs (MooreThreads/onnxruntime-musa):
+//   softmax  musa/ep/src/kernels/math/softmax_impl.mu:49-84 (fp32 accumulation)
+//   top-k    musa/ep/src/kernels/math/topk_impl.mu:46-65 (ties -> lower index)
+//   scan     musa/ep/src/kernels/math/cumsum_impl.mu:17 (replaced by a two-level scan)
+//   gather   musa/ep/src/kernels/tensor/gather_impl.mu:18
+#include "moe_kernels.h"
+
+namespace moe {
+
+__device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// ------------------------------------------------------------------------ router
+// One warp per row; lane l holds logits l, l+32, ...  Selection compares fp32
+// values, ties to the lower index.  NaN logits are read as -inf.
+template <typename T, int kPerLane>
+__global__ void __launch_bounds__(kRouteThreads)
+route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int normalize,
+             int32_t* __restrict__ expert_idx, float* __restrict__ route_w,
+             int32_t* __restrict__ chunk_counts) {
+  extern __shared__ int32_t s_counts[];  // [E]
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_counts[e] = 0;
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int row0 = blockIdx.x * kRouteChunk;
+  const int row_end = min(row0 + kRouteChunk, num_rows);
+  for (int t = row0 + warp; t < row_end; t += kRouteThreads / 32) {
+    float v[kPerLane];
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int e = lane + 32 * j;
+      float x = -INFINITY;
+      if (e < E) {
+        x = to_f(logits[static_cast<int64_t>(t) * E + e]);
+        if (x != x) x = -INFINITY;
+      }
+      v[j] = x;
+    }
+    // Row max and softmax denominator (fixed butterfly order: deterministic).
+    float m = v[0];
+#pragma unroll
+    for (int j = 1; j < kPerLane; ++j) m = fmaxf(m, v[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j)
+      if (lane + 32 * j < E) s += expf(v[j] - m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+
+    uint32_t taken = 0;  // bit j: v[j] already selected
+    float top_val = 0.f, sel_sum = 0.f, my_val = 0.f;
+    int my_idx = 0;
+    for (int r = 0; r < k; ++r) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < kPerLane; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E && !(taken & (1u << j)) && (v[j] > bv || (v[j] == bv && e < bi))) {
+          bv = v[j];
+          bi = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      if (r == 0) top_val = bv;
+      const float ex = normalize ? expf(bv - top_val) : expf(bv - m);
+      sel_sum += ex;
+      if (lane == r) { my_val = ex; my_idx = bi; }
+    }
+    if (lane < k) {
+      const float w = normalize ? my_val / sel_sum : my_val / s;
+      expert_idx[static_cast<int64_t>(t) * k + lane] = my_idx;
+      route_w[static_cast<int64_t>(t) * k + lane] = w;
+      atomicAdd(&s_counts[my_idx], 1);
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    chunk_counts[static_cast<int64_t>(blockIdx.x) * E + e] = s_counts[e];
+}
+
+// ---------------------------------------------------------- histogram (external)
+// Per-chunk histogram of an existing expert_idx (used when routing is supplied).
+__global__ void __launch_bounds__(kRouteThreads)
+histogram_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, int E,
+                 int32_t* __restrict__ chunk_counts, int* __restrict__ err) {
+  extern __shared__ int32_t s_counts[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_counts[e] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk * k;
+  const int64_t end = imin64(base + static_cast<int64_t>(kRouteChunk) * k,
+                                   static_cast<int64_t>(num_rows) * k);
+  for (int64_t i = base + threadIdx.x; i < end; i += blockDim.x) {
+    const int e = expert_idx[i];
+    if (e < 0 || e >= E) { atomicExch(err, kErrBadExpert); continue; }
+    atomicAdd(&s_counts[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    chunk_counts[static_cast<int64_t>(blockIdx.x) * E + e] = s_counts[e];
+}
+
+// ---------------------------------------------------------------------- scan
+// Single CTA.  Column scan over chunks per expert (chunk_base), then an exclusive
+// scan over experts (expert_offsets) and the prefix of 128-row and 64-row tile
+// counts used by the grouped-GEMM schedulers.
+__global__ void __launch_bounds__(1024)
+scan_kernel(const int32_t* __restrict__ chunk_counts, int num_chunks, int E,
+            int32_t* __restrict__ chunk_base, int32_t* __restrict__ expert_offsets,
+            int32_t* __restrict__ tiles128, int32_t* __restrict__ tiles64) {
+  extern __shared__ int32_t s_tot[];  // [3][E]
+  int32_t* s_cnt = s_tot;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int32_t run = 0;
+    for (int c = 0; c < num_chunks; ++c) {
+      const int64_t i = static_cast<int64_t>(c) * E + e;
+      chunk_base[i] = run;
+      run += chunk_counts[i];
+    }
+    s_cnt[e] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t o = 0, t128 = 0, t64 = 0;
+    for (int e = 0; e < E; ++e) {
+      expert_offsets[e] = o;
+      tiles128[e] = t128;
+      tiles64[e] = t64;
+      const int32_t c = s_cnt[e];
+      o += c;
+      t128 += (c + 127) / 128;
+      t64 += (c + 63) / 64;
+    }
+    expert_offsets[E] = o;
+    tiles128[E] = t128;
+    tiles64[E] = t64;
+  }
+}
+
+// ------------------------------------------------------------------ permutation
+// One CTA per routing chunk.  Entries are ranked within their expert in
+// (token, slot) order: __match_any_sync gives the rank inside a warp, a per-warp
+// count table the rank across warps, and a running per-expert counter the rank
+// across the groups of the chunk.
+__global__ void __launch_bounds__(kRouteThreads)
+permute_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, int E,
+               const int32_t* __restrict__ expert_offsets,
+               const int32_t* __restrict__ chunk_base, int32_t* __restrict__ permuted_pos,
+               int32_t* __restrict__ permuted_src) {
+  extern __shared__ int32_t smem[];
+  constexpr int kWarps = kRouteThreads / 32;
+  int32_t* s_warp = smem;               // [kWarps][E]
+  int32_t* s_run = smem + kWarps * E;   // [E]
+  int32_t* s_base = s_run + E;          // [E]
+  for (int i = threadIdx.x; i < kWarps * E; i += blockDim.x) s_warp[i] = 0;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    s_run[e] = 0;
+    s_base[e] = expert_offsets[e] + chunk_base[static_cast<int64_t>(blockIdx.x) * E + e];
+  }
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk * k;
+  const int64_t end = imin64(base + static_cast<int64_t>(kRouteChunk) * k,
+                                   static_cast<int64_t>(num_rows) * k);
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  for (int64_t g = base; g < end; g += kRouteThreads) {
+    const int64_t i = g + threadIdx.x;
+    const bool valid = i < end;
+    int e = valid ? expert_idx[i] : -1;
+    if (e >= E || e < -1) e = -1;  // out-of-range ids were flagged by the router/histogram
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    const int lane_rank = __popc(peers & lt_mask);
+    const bool leader = (peers & lt_mask) == 0;
+    if (e >= 0 && leader) s_warp[warp * E + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int r = s_run[e] + lane_rank;
+      for (int w = 0; w < warp; ++w) r += s_warp[w * E + e];
+      const int32_t p = s_base[e] + r;
+      permuted_pos[i] = p;
+      permuted_src[p] = static_cast<int32_t>(i);
+    }
+    __syncthreads();
+    for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
+      int add = 0;
+      for (int w = 0; w < kWarps; ++w) { add += s_warp[w * E + ee]; s_warp[w * E + ee] = 0; }
+      s_run[ee] += add;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------------ gather
+// Xp[p, :] = x[permuted_src[p] / k, :].  One warp per permuted row, 16-byte
+// vectors when the row is 16-byte aligned.
+__global__ void __launch_bounds__(256)
+gather_rows_kernel(const uint8_t* __restrict__ x, int64_t row_bytes, int k,
+                   const int32_t* __restrict__ permuted_src, int64_t num_perm_rows,
+                   uint8_t* __restrict__ xp) {
+  const int lane = threadIdx.x & 31;
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (p >= num_perm_rows) return;
+  const int64_t t = permuted_src[p] / k;
+  const uint8_t* src = x + t * row_bytes;
+  uint8_t* dst = xp + p * row_bytes;
+  if ((row_bytes & 15) == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    for (int64_t i = lane; i < row_bytes / 16; i += 32) d4[i] = __ldg(s4 + i);
+  } else {
+    for (int64_t i = lane; i < row_bytes; i += 32) dst[i] = src[i];
+  }
+}
+
+// ------------------------------------------------------------------------ combine
+// out[t, :] = sum_j w[t, j] * Y[pos[t, j], :], fp32 accumulation in slot order.
+template <typename T>
+__global__ void __launch_bounds__(256)
+combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ permuted_pos,
+               const float* __restrict__ route_w, int num_rows, int k, int H,
+               T* __restrict__ out) {
+  const int t = blockIdx.x;
+  if (t >= num_rows) return;
+  const int32_t* pos = permuted_pos + static_cast<int64_t>(t) * k;
+  const float* w = route_w + static_cast<int64_t>(t) * k;
+  if constexpr (sizeof(T) == 2) {
+    if ((H & 7) == 0) {
+      for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < k; ++j) {
+          const uint4 v = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(pos[j]) * H + c);
+          const T* e = reinterpret_cast<const T*>(&v);
+          const float wj = w[j];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] += wj * to_f(e[q]);
+        }
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ow[q] = pack2<T>(acc[2 * q], acc[2 * q + 1]);
+        *reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * H + c) = o;
+      }
+      return;
+    }
+  }
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc += w[j] * to_f(y[static_cast<int64_t>(pos[j]) * H + c]);
+    out[static_cast<int64_t>(t) * H + c] = from_f<T>(acc);
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+template <typename T>
+static cudaError_t launch_route_t(const void* logits, int T_, int E, int k, int normalize,
+                                  int32_t* idx, float* w, int32_t* chunk_counts,
+                                  cudaStream_t s) {
+  const int chunks = num_route_chunks(T_);
+  const size_t sm = static_cast<size_t>(E) * sizeof(int32_t);
+  const T* l = static_cast<const T*>(logits);
+  const int per_lane = (E + 31) / 32;
+  if (per_lane <= 1)
+    route_kernel<T, 1><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+  else if (per_lane <= 2)
+    route_kernel<T, 2><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+  else if (per_lane <= 4)
+    route_kernel<T, 4><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+  else
+    route_kernel<T, 8><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route(int dtype, const void* logits, int T_, int E, int k, int normalize,
+                         int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s) {
+  if (T_ == 0) return cudaSuccess;
+  switch (dtype) {
+    case kDtF32: return launch_route_t<float>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
+    case kDtF16: return launch_route_t<__half>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
+    case kDtBF16: return launch_route_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_histogram(const int32_t* idx, int T_, int k, int E, int32_t* chunk_counts,
+                             int* err, cudaStream_t s) {
+  if (T_ == 0) return cudaSuccess;
+  histogram_kernel<<<num_route_chunks(T_), kRouteThreads, E * sizeof(int32_t), s>>>(
+      idx, T_, k, E, chunk_counts, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_plan(const int32_t* idx, int T_, int k, int E, const int32_t* chunk_counts,
+                        int32_t* chunk_base, int32_t* offsets, int32_t* tiles128,
+                        int32_t* tiles64, int32_t* pos, int32_t* src, cudaStream_t s) {
+  const int chunks = num_route_chunks(T_);
+  scan_kernel<<<1, 1024, 3 * E * sizeof(int32_t), s>>>(chunk_counts, chunks, E, chunk_base,
+                                                       offsets, tiles128, tiles64);
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess || T_ == 0) return st;
+  const size_t sm = (static_cast<size_t>(kRouteThreads / 32) + 2) * E * sizeof(int32_t);
+  permute_kernel<<<chunks, kRouteThreads, sm, s>>>(idx, T_, k, E, offsets, chunk_base, pos, src);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
+                          int64_t rows, void* xp, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const int64_t blocks = (rows + 7) / 8;
+  gather_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+      static_cast<const uint8_t*>(x), row_bytes, k, src, rows, static_cast<uint8_t*>(xp));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
+                           int T_, int k, int H, void* out, cudaStream_t s) {
+  if (T_ == 0) return cudaSuccess;
+  switch (dtype) {
+    case kDtF32:
+      combine_kernel<float><<<T_, 256, 0, s>>>(static_cast<const float*>(y), pos, w, T_, k, H,
+                                               static_cast<float*>(out));
+      break;
+    case kDtF16:
+      combine_kernel<__half><<<T_, 256, 0, s>>>(static_cast<const __half*>(y), pos, w, T_, k, H,
+                                                static_cast<__half*>(out));
+      break;
+    case kDtBF16:
+      combine_kernel<__nv_bfloat16><<<T_, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(y), pos,
+                                                       w, T_, k, H,
+                                                       static_cast<__nv_bfloat16*>(out));
+      break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,107 @@
+"""CPU tests of the C ABI boundary: the library loads, exports exactly the symbols the
+public header declares, and its host-side logic (attribute parsing, validation,
+workspace planning, provider options) behaves like the reference plugin's."""
+
+import math
+import pathlib
+import re
+import subprocess
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "moe_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(moe_b200_\w+)\(", text, re.M))
+
+
+def test_header_symbols_exported(pkg):
+    L = pkg.lib()
+    decl = declared_symbols()
+    assert len(decl) >= 25
+    for name in decl:
+        assert hasattr(L, name), name
+    assert decl == set(pkg.SIGNATURES), "ctypes signatures out of sync with the header"
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.get_library_path()],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    assert exported == decl, f"unexpected exports: {exported ^ decl}"
+
+
+def test_abi_version(pkg):
+    assert pkg.lib().moe_b200_abi_version() == 1
+
+
+def test_kernel_create_attributes(pkg):
+    op = pkg.MoE(activation_type="silu", k=2, normalize_routing_weights=1)
+    op.release()
+    op = pkg.QMoE(activation_type="swiglu", k=2, expert_weight_bits=8, block_size=0,
+                  swiglu_fusion=1, swiglu_limit=7.0, activation_alpha=1.702, activation_beta=1.0)
+    op.release()
+    with pytest.raises(pkg.InvalidArgument, match="activation_type"):
+        pkg.MoE(activation_type="tanh")
+    with pytest.raises(pkg.InvalidArgument, match="unknown attribute"):
+        pkg.MoE(activation_type="relu", foo=1)
+    with pytest.raises(pkg.InvalidArgument, match="k=0"):
+        pkg.MoE(k=0)
+    with pytest.raises(pkg.InvalidArgument, match="not an integer"):
+        pkg.MoE(k="two")
+    with pytest.raises(pkg.InvalidArgument, match="expert_weight_bits"):
+        pkg.QMoE(expert_weight_bits=3)
+    with pytest.raises(pkg.InvalidArgument, match="QMoE attribute"):
+        pkg.MoE(expert_weight_bits=4)
+
+
+def test_workspace_planning(pkg):
+    p = pkg.make_problem(4096, 4096, 14336, 8, pkg.FLOAT16, has_fc3=True,
+                         activation_type="silu", k=2, normalize_routing_weights=1)
+    ws = pkg.workspace_size(p)
+    R = 4096 * 2
+    # gathered input + activation dominate: R*H*2 + R*I*2
+    assert R * 4096 * 2 + R * 14336 * 2 <= ws < R * 4096 * 2 + R * 14336 * 2 + (1 << 22)
+    q = pkg.make_problem(64, 4096, 14336, 8, pkg.FLOAT16, has_fc3=True, activation_type="silu",
+                         k=2, expert_weight_bits=4, block_size=128)
+    assert pkg.workspace_size(q) > 0
+
+
+@pytest.mark.parametrize("kw,exc,msg", [
+    (dict(k=9), "InvalidArgument", "k=9"),
+    (dict(use_sparse_mixer=1), "NotImplementedByEP", "sparse_mixer"),
+    (dict(activation_type="swiglu"), "InvalidArgument", "needs fc3"),
+    (dict(activation_type="swiglu", swiglu_fusion=3), "InvalidArgument", "swiglu_fusion"),
+    (dict(expert_weight_bits=4, block_size=24), "InvalidArgument", "block_size"),
+])
+def test_problem_validation(pkg, kw, exc, msg):
+    base = dict(k=2, activation_type="silu")
+    base.update(kw)
+    p = pkg.make_problem(16, 64, 64, 8, pkg.FLOAT16, **base)
+    with pytest.raises(getattr(pkg, exc), match=msg):
+        pkg.workspace_size(p)
+
+
+def test_no_device_is_zero_devices(pkg):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("host has a GPU")
+    assert pkg.get_ep_devices() == []
+
+
+def test_provider_options(pkg):
+    assert pkg.make_provider_options() == {"device_id": "0", "do_copy_in_default_stream": "1"}
+    o = pkg.make_provider_options(device_id=3, user_compute_stream=12345)
+    assert o["has_user_compute_stream"] == "1" and o["user_compute_stream"] == "12345"
+    assert o["use_ep_level_unified_stream"] == "1"
+    o = pkg.make_provider_options(use_ep_level_unified_stream=False, ep_world_size=4, ep_rank=1)
+    assert o["use_ep_level_unified_stream"] == "0" and o["ep_world_size"] == "4"
+    with pytest.raises(ValueError):
+        pkg.make_provider_options(device_id=-1)
+    with pytest.raises(ValueError):
+        pkg.make_provider_options(user_compute_stream=0)
+    with pytest.raises(TypeError):
+        pkg.make_provider_options(do_copy_in_default_stream=1)
+    with pytest.raises(ValueError):
+        pkg.make_provider_options(ep_world_size=2, ep_rank=2)
+    assert pkg.get_ep_names() == [pkg.get_ep_name()] == ["B200MoEExecutionProvider"]

@@ -1,0 +1,198 @@
+"""GPU parity of the full MoE / QMoE layer through the C ABI against the oracle."""
+
+import math
+import os
+import pathlib
+
+import numpy as np
+import pytest
+
+from gpu_util import TOL, as_np, load_golden, moe_input_list, moe_inputs_on, to_dev, torch_dtype
+
+pytestmark = pytest.mark.gpu
+GOLDEN = pathlib.Path(__file__).parent / "golden"
+
+
+def run_moe(pkg, d, attrs, out=None):
+    op = pkg.MoE(**attrs)
+    try:
+        return op(moe_input_list(d), out=out)
+    finally:
+        op.release()
+
+
+def oracle_out(orc, h, attrs):
+    return orc.moe(h["x"], h["router_probs"], h["fc1_w"], h["fc1_b"], h["fc2_w"], h["fc2_b"],
+                   h["fc3_w"], h["fc3_b"], **attrs)
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("*.npz")), ids=lambda p: p.stem)
+def test_golden_fixtures(pkg, orc, dev, path):
+    import torch
+    d, meta = load_golden(path)
+    dt = torch_dtype(meta["dtype"])
+    get = lambda n: to_dev(d[n], dev) if n in d.files else None
+    if meta["op"] == "MoE":
+        op = pkg.MoE(**meta["attrs"])
+        out = op([get("x"), get("router_probs"), get("fc1_w"), get("fc1_b"), get("fc2_w"),
+                  get("fc2_b"), get("fc3_w"), get("fc3_b")])
+    else:
+        op = pkg.QMoE(**meta["attrs"])
+        out = op([get("x"), get("router_probs"), get("fc1_q"), get("fc1_scales"), None,
+                  get("fc2_q"), get("fc2_scales"), None, get("fc3_q"), get("fc3_scales"), None])
+    op.release()
+    assert out.dtype == dt
+    np.testing.assert_allclose(as_np(out), d["output"], **TOL[meta["dtype"]])
+    idx, _ = pkg.route(get("router_probs"), meta["attrs"]["k"],
+                       meta["attrs"]["normalize_routing_weights"])
+    np.testing.assert_array_equal(idx.cpu().numpy(), d["expert_idx"])
+
+
+def test_config1_fp32_silu_bias(pkg, orc, dev):
+    """fp32, T=256, H=512, I=1024, E=8, k=2, silu, fc1/fc2 bias."""
+    inp = orc.make_moe_inputs(T=256, H=512, I=1024, E=8, k=2, act="silu", gated=False,
+                              dtype="float32", bias=True, normalize=1, seed=20261201)
+    d, h = moe_inputs_on(dev, inp, "float32")
+    out = run_moe(pkg, d, inp["attrs"])
+    np.testing.assert_allclose(as_np(out), oracle_out(orc, h, inp["attrs"]), **TOL["float32"])
+
+
+CASES = [
+    # (T, H, I, E, k, act, gated, bias, normalize, extra)
+    (64, 256, 384, 8, 2, "silu", True, False, 1, {}),
+    (200, 512, 256, 16, 4, "gelu", False, True, 0, {}),
+    (129, 256, 512, 8, 2, "relu", True, True, 1, {}),
+    (77, 128, 256, 4, 1, "identity", False, True, 0, {}),
+    (300, 256, 1024, 64, 8, "silu", True, False, 1, {}),
+    (1, 256, 256, 8, 2, "silu", True, False, 1, {}),
+    (3, 136, 200, 8, 2, "silu", True, True, 1, {}),        # N, K not multiples of 64
+]
+
+
+@pytest.mark.parametrize("dtype_name", ["float16", "bfloat16"])
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"T{c[0]}H{c[1]}I{c[2]}E{c[3]}k{c[4]}{c[5]}")
+def test_moe_half(pkg, orc, dev, dtype_name, case):
+    T, H, I, E, k, act, gated, bias, norm, extra = case
+    inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act=act, gated=gated, dtype="float32",
+                              bias=bias, normalize=norm, seed=T * 7 + E)
+    d, h = moe_inputs_on(dev, inp, dtype_name)
+    attrs = dict(inp["attrs"], **extra)
+    out = run_moe(pkg, d, attrs)
+    np.testing.assert_allclose(as_np(out), oracle_out(orc, h, attrs), **TOL[dtype_name])
+
+
+@pytest.mark.parametrize("fusion", [0, 1, 2])
+@pytest.mark.parametrize("dtype_name", ["float16", "float32"])
+def test_swiglu_variants(pkg, orc, dev, fusion, dtype_name):
+    import torch
+    T, H, I, E, k = 96, 256, 192, 8, 2
+    inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act="swiglu", gated=True,
+                              dtype="float32", bias=True, normalize=1, seed=fusion + 40)
+    w1, w3, b1, b3 = inp["fc1_w"], inp["fc3_w"], inp["fc1_b"], inp["fc3_b"]
+    if fusion == 1:
+        W = np.empty((E, 2 * I, H), np.float32); W[:, 0::2] = w1; W[:, 1::2] = w3
+        B = np.empty((E, 2 * I), np.float32); B[:, 0::2] = b1; B[:, 1::2] = b3
+        inp.update(fc1_w=W, fc1_b=B, fc3_w=None, fc3_b=None)
+    elif fusion == 2:
+        inp.update(fc1_w=np.concatenate([w1, w3], 1), fc1_b=np.concatenate([b1, b3], 1),
+                   fc3_w=None, fc3_b=None)
+    d, h = moe_inputs_on(dev, inp, dtype_name)
+    attrs = dict(activation_type="swiglu", k=k, normalize_routing_weights=1,
+                 swiglu_fusion=fusion, activation_alpha=1.702, activation_beta=1.0,
+                 swiglu_limit=0.5)
+    out = run_moe(pkg, d, attrs)
+    np.testing.assert_allclose(as_np(out), oracle_out(orc, h, attrs), **TOL[dtype_name])
+
+
+def test_input_3d_and_empty(pkg, orc, dev):
+    import torch
+    inp = orc.make_moe_inputs(T=48, H=128, I=128, E=8, k=2, act="silu", gated=True,
+                              dtype="float16", bias=False, seed=5)
+    d, h = moe_inputs_on(dev, inp, "float16")
+    d3 = dict(d, x=d["x"].view(4, 12, 128))
+    out = run_moe(pkg, d3, inp["attrs"])
+    assert out.shape == (4, 12, 128)
+    np.testing.assert_allclose(as_np(out).reshape(48, 128), oracle_out(orc, h, inp["attrs"]),
+                               **TOL["float16"])
+    d0 = dict(d, x=d["x"][:0], router_probs=d["router_probs"][:0])
+    out0 = run_moe(pkg, d0, inp["attrs"])
+    assert out0.shape == (0, 128)
+
+
+def test_shape_errors(pkg, orc, dev):
+    import torch
+    inp = orc.make_moe_inputs(T=8, H=64, I=64, E=4, k=2, act="silu", gated=False,
+                              dtype="float16", seed=6)
+    d, _ = moe_inputs_on(dev, inp, "float16")
+    op = pkg.MoE(activation_type="silu", k=2)
+    bad = moe_input_list(d)
+    bad[2] = d["fc1_w"][:, :32].contiguous()
+    with pytest.raises(pkg.InvalidArgument, match="fc1_experts_weights"):
+        op(bad)
+    bad = moe_input_list(d)
+    bad[1] = d["router_probs"][:4].contiguous()
+    with pytest.raises(pkg.InvalidArgument, match="router_probs"):
+        op(bad)
+    bad = moe_input_list(d)
+    bad[4] = d["fc2_w"].float()
+    with pytest.raises(pkg.InvalidArgument, match="fc2_experts_weights"):
+        op(bad)
+    op.release()
+    op = pkg.MoE(activation_type="silu", k=5)
+    with pytest.raises(pkg.InvalidArgument, match="k=5"):
+        op(moe_input_list(d))
+    op.release()
+
+
+def test_tensor_core_path_matches_ffma_path(pkg, orc, dev):
+    """The tcgen05 GEMMs and the FFMA GEMMs give the same layer output."""
+    import torch
+    inp = orc.make_moe_inputs(T=512, H=1024, I=768, E=8, k=2, act="silu", gated=True,
+                              dtype="float32", seed=9)
+    d, h = moe_inputs_on(dev, inp, "bfloat16")
+    tc = run_moe(pkg, d, inp["attrs"])
+    os.environ["MOE_B200_FORCE_SIMT"] = "1"
+    try:
+        simt = run_moe(pkg, d, inp["attrs"])
+    finally:
+        del os.environ["MOE_B200_FORCE_SIMT"]
+    ref = oracle_out(orc, h, inp["attrs"])
+    np.testing.assert_allclose(as_np(tc), ref, **TOL["bfloat16"])
+    np.testing.assert_allclose(as_np(simt), ref, **TOL["bfloat16"])
+
+
+def _torch_rows_reference(pkg, orc, d, rows, attrs):
+    """fp32 PyTorch reference of the layer for a subset of rows (the layer is row-wise
+    independent given each row's routing)."""
+    import torch
+    x = d["x"][rows].float()
+    lg = d["router_probs"][rows].float().cpu().numpy()
+    idx, w = orc.route(lg, attrs["k"], attrs["normalize_routing_weights"])
+    out = torch.zeros_like(x)
+    for i in range(len(rows)):
+        for j in range(attrs["k"]):
+            e = int(idx[i, j])
+            g = x[i] @ d["fc1_w"][e].float().T
+            u = x[i] @ d["fc3_w"][e].float().T
+            a = torch.nn.functional.silu(g) * u
+            out[i] += float(w[i, j]) * (a @ d["fc2_w"][e].float().T)
+    return out.double().cpu().numpy()
+
+
+def test_config2_mixtral_full_size(pkg, orc, dev):
+    """BASELINE configs[1] at full size: Mixtral-shaped fp16 layer, T=4096."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(20261202)
+    T, H, I, E = 4096, 4096, 14336, 8
+    d = dict(x=torch.randn(T, H, device=dev, generator=g).half(),
+             router_probs=torch.randn(T, E, device=dev, generator=g).half(),
+             fc1_w=(torch.randn(E, I, H, device=dev, generator=g) * 0.02).half(), fc1_b=None,
+             fc2_w=(torch.randn(E, H, I, device=dev, generator=g) * 0.02).half(), fc2_b=None,
+             fc3_w=(torch.randn(E, I, H, device=dev, generator=g) * 0.02).half(), fc3_b=None)
+    attrs = dict(activation_type="silu", k=2, normalize_routing_weights=1)
+    out1 = run_moe(pkg, d, attrs)
+    out2 = run_moe(pkg, d, attrs)
+    assert torch.equal(out1, out2), "layer output is not deterministic"
+    rows = torch.tensor([0, 1, 777, 2048, 4095] + list(range(1000, 1027)), device=dev)
+    ref = _torch_rows_reference(pkg, orc, d, rows, attrs)
+    np.testing.assert_allclose(as_np(out1[rows]), ref, **TOL["float16"])
