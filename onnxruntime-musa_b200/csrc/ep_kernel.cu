@@ -168,8 +168,17 @@ int moe_b200_kernel_compute(moe_b200_kernel* kern, int32_t num_inputs,
   if (num_inputs < (q ? 7 : 5) || num_inputs > max_inputs)
     return (efail(MOE_B200_INVALID_ARGUMENT, "%s takes %d..%d inputs, got %d",
                         q ? "QMoE" : "MoE", q ? 7 : 5, max_inputs, num_inputs));
+  // An input is present when it has data or is a zero-size tensor (whose data
+  // pointer may legitimately be NULL); absent optional inputs have rank 0, no data.
+  auto present = [&](const moe_b200_tensor_ref& t) {
+    if (t.data != nullptr) return true;
+    if (t.rank <= 0 || t.rank > 4) return false;
+    for (int d = 0; d < t.rank; ++d)
+      if (t.dims[d] == 0) return true;
+    return false;
+  };
   auto get = [&](int i) -> const moe_b200_tensor_ref* {
-    if (i < 0 || i >= num_inputs || in[i].data == nullptr) return nullptr;
+    if (i < 0 || i >= num_inputs || !present(in[i])) return nullptr;
     return &in[i];
   };
   if (q) {
@@ -246,7 +255,7 @@ int moe_b200_kernel_compute(moe_b200_kernel* kern, int32_t num_inputs,
     if (st == MOE_B200_OK && w3) st = check_scales(kFc3S, I, H, "fc3_scales");
     if (st != MOE_B200_OK) return (st);
   }
-  if (output->data == nullptr || output->elem_type != dt || output->rank != x->rank)
+  if (!present(*output) || output->elem_type != dt || output->rank != x->rank)
     return (efail(MOE_B200_INVALID_ARGUMENT, "output must match the input's type and rank"));
   for (int i = 0; i < x->rank; ++i)
     if (output->dims[i] != x->dims[i])

@@ -254,10 +254,10 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
                 ws_bytes, L.total);
   if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)
     return fail(MOE_B200_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
-  if (t.input == nullptr || t.router_probs == nullptr || t.output == nullptr ||
-      t.fc1_weights == nullptr || t.fc2_weights == nullptr)
-    return fail(MOE_B200_INVALID_ARGUMENT, "input, router_probs, fc1/fc2 weights and output "
-                                           "must be non-NULL");
+  if (t.fc1_weights == nullptr || t.fc2_weights == nullptr)
+    return fail(MOE_B200_INVALID_ARGUMENT, "fc1/fc2 weights must be non-NULL");
+  if (p.num_rows > 0 && (t.input == nullptr || t.router_probs == nullptr || t.output == nullptr))
+    return fail(MOE_B200_INVALID_ARGUMENT, "input, router_probs and output must be non-NULL");
   if (p.has_fc3 && t.fc3_weights == nullptr)
     return fail(MOE_B200_INVALID_ARGUMENT, "has_fc3 is set but fc3_weights is NULL");
   const int T = static_cast<int>(p.num_rows);
