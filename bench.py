@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 A "step" is one com.microsoft MoE layer call over one batch of synthetic tokens:
-BASELINE configs[1] (Mixtral-8x7B-shaped fp16 layer: T=4096, H=4096, I=14336,
+benchmark config 2 of 5 (Mixtral-8x7B-shaped fp16 layer: T=4096, H=4096, I=14336,
 E=8, k=2, SwiGLU via fc3, no bias).  Inputs x, logits ~ N(0,1), weights ~ N(0, 0.02),
 generated on the device from a fixed seed (no dataset is involved).
 

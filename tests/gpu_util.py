@@ -4,7 +4,7 @@ import json
 
 import numpy as np
 
-# Output tolerances: fp32 rtol 1e-4 (atol chosen here: 1e-6);
+# Output tolerances of the parity bar: fp32 rtol 1e-4 (atol chosen here: 1e-6);
 # fp16 / bf16 rtol 2e-2, atol 2e-3.
 TOL = {"float32": dict(rtol=1e-4, atol=1e-6), "float16": dict(rtol=2e-2, atol=2e-3),
        "bfloat16": dict(rtol=2e-2, atol=2e-3)}

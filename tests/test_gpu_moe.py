@@ -49,7 +49,7 @@ def test_golden_fixtures(pkg, orc, dev, path):
 
 
 def test_config1_fp32_silu_bias(pkg, orc, dev):
-    """fp32, T=256, H=512, I=1024, E=8, k=2, silu, fc1/fc2 bias."""
+    """Benchmark config 1: fp32, T=256, H=512, I=1024, E=8, k=2, silu, fc1/fc2 bias."""
     inp = orc.make_moe_inputs(T=256, H=512, I=1024, E=8, k=2, act="silu", gated=False,
                               dtype="float32", bias=True, normalize=1, seed=20261201)
     d, h = moe_inputs_on(dev, inp, "float32")
@@ -180,7 +180,7 @@ def _torch_rows_reference(pkg, orc, d, rows, attrs):
 
 
 def test_config2_mixtral_full_size(pkg, orc, dev):
-    """BASELINE configs[1] at full size: Mixtral-shaped fp16 layer, T=4096."""
+    """Benchmark config 2 at full size: Mixtral-shaped fp16 layer, T=4096."""
     import torch
     g = torch.Generator(device=dev).manual_seed(20261202)
     T, H, I, E = 4096, 4096, 14336, 8
