@@ -42,7 +42,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer tokens/s"
 UNIT = "tokens/s"
 CFG = dict(T=4096, H=4096, I=14336, E=8, k=2)
-WORKLOAD = "configs[1]: Mixtral-8x7B-shaped com.microsoft.MoE fp16, T=4096 H=4096 I=14336 E=8 k=2 SwiGLU(fc3)"
+WORKLOAD = ("configs[1]: Mixtral-8x7B-shaped com.microsoft.MoE fp16, T={T} H=4096 I=14336 E=8 k=2 "
+            "SwiGLU(fc3)")
 # DRAM bytes (read + write) of one fc1(+fc3) GEMM launch from the ncu capture
 # summarised in profiles/; None until a capture exists.
 FC1_TRAFFIC_BYTES = None
@@ -267,7 +268,7 @@ def bench_ours(args, rank, world, dev):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,1) tokens/logits, N(0,0.02) weights; random init)",
-        "config": {"workload": WORKLOAD, "global_batch": T * world, "tokens_per_gpu": T,
+        "config": {"workload": WORKLOAD.format(T=T), "global_batch": T * world, "tokens_per_gpu": T,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (2.8 GB of weights per step)"},
         "e2e": e2e, "roofline": roof,
@@ -300,7 +301,7 @@ def bench_reference(args, rank, world):
     return {"metric": METRIC, "value": round(v, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "impl": "reference", "dtype": "f32",
-            "config": {"workload": WORKLOAD, "engine": "C restatement of the CPU path"},
+            "config": {"workload": WORKLOAD.format(T=T), "engine": "C restatement of the CPU path"},
             "cpu_baseline": base,
             "e2e": {"value": round(v, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -313,10 +314,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--tokens", type=int, default=CFG["T"],
+                    help="tokens per GPU (default: the config's 4096; smaller for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     import torch
+    CFG["T"] = args.tokens
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -170,6 +170,18 @@ int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
                    int64_t num_experts, int32_t k, int32_t normalize_routing_weights,
                    int32_t* expert_idx, float* route_weight, void* stream);
 
+/* moe_b200_route without any device allocation, for callers that cannot allocate
+ * where they route (memory planned up front, or owned by an arena that only hands
+ * out inputs and outputs).  No counterpart in the reference.  Same arguments and
+ * results as moe_b200_route; its scratch is a static 256 KiB device array, so
+ * ceil(num_rows / 256) * num_experts must be <= 65536 (else INVALID_ARGUMENT).
+ * All calls on a device share that array: calls overlapping on the GPU race.  The
+ * first call on a device looks up the array's address; make it before any stream
+ * capture. */
+int moe_b200_route_noalloc(const void* router_probs, int32_t dtype, int64_t num_rows,
+                           int64_t num_experts, int32_t k, int32_t normalize_routing_weights,
+                           int32_t* expert_idx, float* route_weight, void* stream);
+
 /* Dispatch plan for expert_idx [T, k]: expert_offsets int32 [E+1] (exclusive
  * scan of the counts), permuted_pos int32 [T*k] (position of routed row t*k+j)
  * and permuted_src int32 [T*k] (inverse).  Order: expert, then token, then slot.

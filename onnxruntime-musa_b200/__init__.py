@@ -113,6 +113,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "moe_b200_forward_timed": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                               _VP, _SZ, _VP, _PF, _I32]),
     "moe_b200_route": (ctypes.c_int, [_VP, _I32, _I64, _I64, _I32, _I32, _VP, _VP, _VP]),
+    "moe_b200_route_noalloc": (ctypes.c_int, [_VP, _I32, _I64, _I64, _I32, _I32, _VP, _VP, _VP]),
     "moe_b200_permute_workspace_size": (_SZ, [_I64, _I32, _I64]),
     "moe_b200_permute": (ctypes.c_int, [_VP, _I64, _I32, _I64, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "moe_b200_device_count": (ctypes.c_int, [_PI32]),
