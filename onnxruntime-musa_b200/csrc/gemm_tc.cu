@@ -8,7 +8,8 @@
 //   warp 1      MMA issuer: tcgen05.mma kind::f16, M=128 N=256 K=16, fp32
 //               accumulator in TMEM; two accumulators (2 x 256 columns) so the
 //               epilogue of tile i overlaps the mainloop of tile i+1.
-//   warps 2..5  epilogue: tcgen05.ld of its 32-lane quarter, bias + activation
+//   warps 2..9  epilogue (two warps per 32-lane TMEM quarter, each taking half the
+//               columns): tcgen05.ld of its lane quarter, bias + activation
 //               (gated: act(g) * u, where columns 0..127 hold the gate tile and
 //               128..255 the linear tile of the same 128 output columns), and a
 //               store of the 16-bit result rows.  Rows of the tile that belong to
@@ -33,7 +34,8 @@ constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int B_HALF = B_BYTES / 2;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;      // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int EPI_WARPS = 8;      // two warps per TMEM lane quarter, splitting the columns
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES =
     1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + 64 * 8 /*barriers*/ +
@@ -41,7 +43,7 @@ constexpr int SMEM_BYTES =
 
 struct TcParams {
   const int32_t* offsets;
-  const int32_t* tiles128;
+  const int32_t* tiles;   // prefix of per-expert m-tile counts (128 or 256 rows per tile)
   int E;
   int K;
   int N;            // output columns
@@ -95,8 +97,92 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int valid_
     reinterpret_cast<uint4*>(dst)[0] = o0;
     reinterpret_cast<uint4*>(dst)[1] = o1;
   } else {
-    for (int q = 0; q < valid_cols; ++q) dst[q] = from_f<T>(v[q]);
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+      if (q < valid_cols) dst[q] = from_f<T>(v[q]);
   }
+}
+
+// Fast-math activations for the 16-bit epilogue (inputs and outputs are fp16/bf16,
+// so the few-ulp error of the approximate exp and reciprocal is far below the
+// output rounding).
+__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+
+__device__ __forceinline__ float fast_act_single(int act, float x) {
+  switch (act) {
+    case kRelu: return fmaxf(x, 0.0f);
+    case kGelu: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    case kSilu: return x * fast_sigmoid(x);
+    default: return x;
+  }
+}
+
+__device__ __forceinline__ float fast_act_gated(const ActParams& p, float g, float u) {
+  if (p.act == kSwiglu) {
+    g = fminf(g, p.limit);
+    u = fminf(fmaxf(u, -p.limit), p.limit);
+    return g * fast_sigmoid(p.alpha * g) * (u + p.beta);
+  }
+  return fast_act_single(p.act, g) * u;
+}
+
+// Epilogue of one accumulator tile for the calling warp's 32 TMEM lanes (one output
+// row per thread), accumulator columns [c0, c1).  Gated: columns [0,128) hold the gate
+// and [128,256) the linear half of output columns n0..n0+127 (c ranges over the gate
+// columns); plain: columns [0,256) are outputs n0..n0+255.
+template <typename T>
+__device__ __forceinline__ void epilogue_rows(const TcParams& p, uint32_t taddr, int row,
+                                              bool valid, int e, int n0, int c0, int c1) {
+  T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+  const bool has_b1 = p.bias1 != nullptr, has_b3 = p.bias3 != nullptr;
+  if (p.gated) {
+#pragma unroll 1
+    for (int c = c0; c < c1; c += 16) {
+      float g[16], u[16];
+      tmem_ld16(taddr + c, g);
+      tmem_ld16(taddr + BN / 2 + c, u);
+      tmem_ld_wait();
+      const int col = n0 + c;
+      if (valid && col < p.N) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int cj = min(col + j, p.N - 1);
+          const float gb = has_b1 ? g[j] + bias_val<T>(p.bias1, e, cj, p) : g[j];
+          const float ub = has_b3 ? u[j] + bias_val<T>(p.bias3, e, cj, p) : u[j];
+          v[j] = fast_act_gated(p.ap, gb, ub);
+        }
+        store16<T>(orow + col, v, p.N - col);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = c0; c < c1; c += 16) {
+      float a[16];
+      tmem_ld16(taddr + c, a);
+      tmem_ld_wait();
+      const int col = n0 + c;
+      if (valid && col < p.N) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int cj = min(col + j, p.N - 1);
+          const float ab = has_b1 ? a[j] + bias_val<T>(p.bias1, e, cj, p) : a[j];
+          v[j] = fast_act_single(p.ap.act, ab);
+        }
+        store16<T>(orow + col, v, p.N - col);
+      }
+    }
+  }
+}
+
+// Column range of epilogue warp `w` (2..9): warps 2..5 take the first half of the
+// tile's columns, warps 6..9 the second half.
+__device__ __forceinline__ void epi_cols(const TcParams& p, int warp, int& c0, int& c1) {
+  const int width = p.gated ? BN / 2 : BN;
+  const int half = width / 2;
+  c0 = warp < 6 ? 0 : half;
+  c1 = c0 + half;
 }
 
 template <typename T>
@@ -125,7 +211,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
   const int E = p.E;
 
   for (int i = threadIdx.x; i <= E; i += blockDim.x) {
-    s_tiles[i] = p.tiles128[i];
+    s_tiles[i] = p.tiles[i];
     s_offs[i] = p.offsets[i];
   }
   if (threadIdx.x == 0) {
@@ -135,7 +221,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], EPI_WARPS);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -241,7 +327,8 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
     // ----------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int r_in_tile = q * 32 + lane;
-    T* out = static_cast<T*>(p.out);
+    int ec0, ec1;
+    epi_cols(p, warp, ec0, ec1);
     int i = 0;
     for (int L = blockIdx.x; L < total && !*abort_flag; L += gridDim.x, ++i) {
       const int acc = i & 1;
@@ -257,46 +344,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
       const int row = s_offs[e] + m * BM + r_in_tile;
       const bool valid = row < s_offs[e + 1];
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      T* orow = out + static_cast<int64_t>(row) * p.ldo;
-      if (p.gated) {
-        const int n0 = n * (BN / 2);
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 16) {
-          float g[16], u[16];
-          tmem_ld16(taddr + c, g);
-          tmem_ld16(taddr + BN / 2 + c, u);
-          tmem_ld_wait();
-          const int col = n0 + c;
-          if (valid && col < p.N) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int cj = min(col + j, p.N - 1);
-              v[j] = act_gated(p.ap, g[j] + bias_val<T>(p.bias1, e, cj, p),
-                               u[j] + bias_val<T>(p.bias3, e, cj, p));
-            }
-            store16<T>(orow + col, v, p.N - col);
-          }
-        }
-      } else {
-        const int n0 = n * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          float a[16];
-          tmem_ld16(taddr + c, a);
-          tmem_ld_wait();
-          const int col = n0 + c;
-          if (valid && col < p.N) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int cj = min(col + j, p.N - 1);
-              v[j] = act_single(p.ap.act, a[j] + bias_val<T>(p.bias1, e, cj, p));
-            }
-            store16<T>(orow + col, v, p.N - col);
-          }
-        }
-      }
+      epilogue_rows<T>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -308,6 +356,201 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2): a cluster of 2 CTAs on 2 SMs computes a
+// 256x256 tile with M=256 MMAs issued by the leader CTA.  Each CTA stages its own
+// 128 rows of A and its own 128 rows of B (gate rows in CTA 0 and linear rows in CTA 1
+// when gated), so per SM the operand traffic per MMA is half that of the single-CTA
+// kernel.  Both CTAs' TMA loads complete on the leader's `full` barrier (which expects
+// the bytes of both); MMA completion is committed to the barriers of both CTAs.  No
+// TMA load is multicast.  Accumulators: 128 lanes x 256 columns per CTA, double
+// buffered; each CTA's epilogue drains its own rows and then arrives on the leader's
+// `tempty` barrier (16 arrivals: 8 warps x 2 CTAs).
+constexpr int P_BM = 256;         // rows per pair tile
+constexpr int P_STAGES = 6;
+constexpr int P_STAGE_BYTES = A_BYTES + B_HALF;  // per CTA: 128x64 of A + 128x64 of B
+constexpr int P_SMEM_BYTES =
+    1024 + P_STAGES * P_STAGE_BYTES + 64 * 8 + 2 * (kMaxExperts + 1) * 4;
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                            const __grid_constant__ CUtensorMap map_b1,
+                            const __grid_constant__ CUtensorMap map_b3, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + P_STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + P_STAGES * B_HALF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + P_STAGES;
+  uint64_t* tfull = bars + 2 * P_STAGES;
+  uint64_t* tempty = bars + 2 * P_STAGES + 2;
+  uint64_t* done = bars + 2 * P_STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_tiles = reinterpret_cast<int32_t*>(bars + 64);
+  int32_t* s_offs = s_tiles + (kMaxExperts + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = p.E;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_tiles[i] = p.tiles[i];
+    s_offs[i] = p.offsets[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b1);
+    if (p.gated) tma_prefetch_desc(&map_b3);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = s_tiles[E] * p.n_tiles;
+  const int nk = (p.K + BK - 1) / BK;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int L = pair; L < total && !*abort_flag; L += npairs) {
+        int e, m, n;
+        decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
+        const int row0 = s_offs[e] + m * P_BM + static_cast<int>(rank) * BM;
+        const CUtensorMap* bmap = (p.gated && rank == 1) ? &map_b3 : &map_b1;
+        int bg, brow;
+        if (p.gated) {
+          bg = rank == 1 ? p.b3_g : p.b1_g;
+          brow = n * (BN / 2) + (rank == 1 ? p.b3_noff : p.b1_noff);
+        } else {
+          bg = p.b1_g;
+          brow = n * BN + static_cast<int>(rank) * (BN / 2) + p.b1_noff;
+        }
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            atomicExch(p.err, kErrTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          const int kc = kb * BK;
+          tma_load_2d_pair(sA + stage * A_BYTES, &map_a, full_leader, kc, row0);
+          tma_load_4d_pair(sB + stage * B_HALF, bmap, full_leader, kc, bg, brow, e);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------- MMA issuer (leader CTA only)
+    if (lane == 0 && leader) {
+      constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      const uint32_t idesc = idesc_f16(kFmt, P_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      for (int L = pair; L < total && !*abort_flag; L += npairs, ++i) {
+        const int acc = i & 1;
+        const uint32_t acc_phase = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+          atomicExch(p.err, kErrTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            atomicExch(p.err, kErrTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_HALF);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            tc_mma_f16_pair(d_tmem, smem_desc_k_sw128(a_addr + kk * 32),
+                            smem_desc_k_sw128(b_addr + kk * 32), idesc,
+                            (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_pair(&tfull[acc], 0x3);
+      }
+      tc_commit_pair(done, 0x1);
+      mbar_wait(done, 0);
+    }
+  } else {
+    // ----------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r_in_tile = static_cast<int>(rank) * BM + q * 32 + lane;
+    int ec0, ec1;
+    epi_cols(p, warp, ec0, ec1);
+    int i = 0;
+    for (int L = pair; L < total && !*abort_flag; L += npairs, ++i) {
+      const int acc = i & 1;
+      const uint32_t acc_phase = (i >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase)) {
+        atomicExch(p.err, kErrTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int e, m, n;
+      decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
+      const int row = s_offs[e] + m * P_BM + r_in_tile;
+      const bool valid = row < s_offs[e + 1];
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      epilogue_rows<T>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal it or read its smem
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -368,7 +611,7 @@ bool make_map_b(CUtensorMap* m, int dt, const GemmOperandB& b, int K, int E) {
 }
 
 template <typename T>
-cudaError_t launch_t(const GemmArgs& g, int num_sms, cudaStream_t s) {
+cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) {
   CUtensorMap ma, mb1, mb3;
   if (!make_map_a(&ma, g.dtype, g.a, g.rows, g.K)) return cudaErrorInvalidValue;
   if (!make_map_b(&mb1, g.dtype, g.b1, g.K, g.E)) return cudaErrorInvalidValue;
@@ -379,7 +622,7 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, cudaStream_t s) {
   }
   TcParams p;
   p.offsets = g.offsets;
-  p.tiles128 = g.tiles128;
+  p.tiles = pair ? g.tiles256 : g.tiles128;
   p.E = g.E;
   p.K = g.K;
   p.N = g.N;
@@ -397,19 +640,29 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.out = g.out;
   p.ldo = g.ldo;
   p.err = g.err;
-  static bool attr_set = false;  // benign race: the attribute call is idempotent
-  if (!attr_set) {
-    cudaError_t st = cudaFuncSetAttribute(tc_grouped_gemm_kernel<T>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          SMEM_BYTES);
+  // The attribute call is idempotent; a race between first callers is benign.
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[pair]) {
+    cudaError_t st = pair ? cudaFuncSetAttribute(tc_pair_grouped_gemm_kernel<T>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 P_SMEM_BYTES)
+                          : cudaFuncSetAttribute(tc_grouped_gemm_kernel<T>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 SMEM_BYTES);
     if (st != cudaSuccess) return st;
-    attr_set = true;
+    attr_set[pair] = true;
   }
   // The real tile count lives on the device; an upper bound sizes the grid.
-  const int64_t ub_m = (g.rows + BM - 1) / BM + g.E;
-  const int64_t ub = ub_m * p.n_tiles;
-  const int grid = static_cast<int>(std::min<int64_t>(ub, num_sms));
-  tc_grouped_gemm_kernel<T><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb1, mb3, p);
+  const int rows_per_tile = pair ? P_BM : BM;
+  const int64_t ub = ((g.rows + rows_per_tile - 1) / rows_per_tile + g.E) * p.n_tiles;
+  if (pair) {
+    const int64_t pairs = std::min<int64_t>(ub, num_sms / 2);
+    tc_pair_grouped_gemm_kernel<T><<<static_cast<int>(2 * pairs), THREADS, P_SMEM_BYTES, s>>>(
+        ma, mb1, mb3, p);
+  } else {
+    const int grid = static_cast<int>(std::min<int64_t>(ub, num_sms));
+    tc_grouped_gemm_kernel<T><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb1, mb3, p);
+  }
   return cudaGetLastError();
 }
 
@@ -426,10 +679,12 @@ bool tc_supported(const GemmArgs& g) {
   return get_encode_fn() != nullptr;
 }
 
-cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
+cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, int mode, cudaStream_t s) {
   if (g.rows == 0 || g.N == 0) return cudaSuccess;
-  if (g.dtype == kDtF16) return launch_t<__half>(g, num_sms, s);
-  if (g.dtype == kDtBF16) return launch_t<__nv_bfloat16>(g, num_sms, s);
+  // mode 0: choose (CTA pairs when experts average >= 256 rows), 1: single CTA, 2: pairs.
+  const bool pair = mode == 2 || (mode == 0 && g.rows >= 256 * static_cast<int64_t>(g.E));
+  if (g.dtype == kDtF16) return launch_t<__half>(g, num_sms, pair, s);
+  if (g.dtype == kDtBF16) return launch_t<__nv_bfloat16>(g, num_sms, pair, s);
   return cudaErrorInvalidValue;
 }
 

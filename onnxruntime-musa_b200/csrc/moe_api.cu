@@ -86,7 +86,7 @@ bool is_float_type(int dt) {
 
 // ------------------------------------------------------------ workspace plan
 struct WsLayout {
-  size_t idx, w, chunk_counts, chunk_base, offsets, tiles128, tiles64, pos, src, err;
+  size_t idx, w, chunk_counts, chunk_base, offsets, tiles128, tiles64, tiles256, pos, src, err;
   size_t xp, act, qmoe, total;
 };
 
@@ -109,6 +109,7 @@ WsLayout plan_workspace(const moe_b200_problem& p) {
   L.offsets = take((E + 1) * 4);
   L.tiles128 = take((E + 1) * 4);
   L.tiles64 = take((E + 1) * 4);
+  L.tiles256 = take((E + 1) * 4);
   L.pos = take(R * 4);
   L.src = take(R * 4);
   L.err = take(16);
@@ -236,9 +237,14 @@ GemmArgs fc2_args(const moe_b200_problem& p, const void* w2, const void* b2) {
   return g;
 }
 
+// MOE_B200_FORCE_SIMT=1 selects the FFMA GEMMs; MOE_B200_TC_MODE=1|2 forces the
+// single-CTA or CTA-pair tensor-core kernel (used by tests to cover both).
 cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
-  if (!env_flag("MOE_B200_FORCE_SIMT") && tc_supported(g))
-    return launch_gemm_tc(g, device_sm_count(), s);
+  if (!env_flag("MOE_B200_FORCE_SIMT") && tc_supported(g)) {
+    const char* m = std::getenv("MOE_B200_TC_MODE");
+    const int mode = m ? std::atoi(m) : 0;
+    return launch_gemm_tc(g, device_sm_count(), mode, s);
+  }
   return launch_gemm_simt(g, s);
 }
 
@@ -275,6 +281,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   auto* offs = reinterpret_cast<int32_t*>(ws + L.offsets);
   auto* t128 = reinterpret_cast<int32_t*>(ws + L.tiles128);
   auto* t64 = reinterpret_cast<int32_t*>(ws + L.tiles64);
+  auto* t256 = reinterpret_cast<int32_t*>(ws + L.tiles256);
   auto* pos = reinterpret_cast<int32_t*>(ws + L.pos);
   auto* src = reinterpret_cast<int32_t*>(ws + L.src);
   auto* err = reinterpret_cast<int*>(ws + L.err);
@@ -287,7 +294,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
                               p.attrs.normalize_routing_weights, idx, w, cc, s),
                  "route");
   mark(kStPlan);
-  MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, pos, src, s), "plan");
+  MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s), "plan");
   const size_t es = dtype_bytes(p.dtype);
   mark(kStGather);
   MOE_CUDA_CHECK(launch_gather(t.input, static_cast<int64_t>(H) * es, k, src, R, xp, s),
@@ -314,6 +321,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g1.offsets = offs;
   g1.tiles128 = t128;
   g1.tiles64 = t64;
+  g1.tiles256 = t256;
   g1.out = act;
   g1.ldo = I;
   g1.err = err;
@@ -326,6 +334,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g2.offsets = offs;
   g2.tiles128 = t128;
   g2.tiles64 = t64;
+  g2.tiles256 = t256;
   g2.out = xp;  // Y aliases the gathered input, dead after fc1
   g2.ldo = H;
   g2.err = err;
@@ -418,7 +427,7 @@ int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
 size_t moe_b200_permute_workspace_size(int64_t num_rows, int32_t k, int64_t num_experts) {
   (void)k;
   const size_t chunks = std::max<int64_t>(num_route_chunks(num_rows), 1);
-  return align_up(chunks * num_experts * 4, 256) * 2 + align_up((num_experts + 1) * 4, 256) * 2 +
+  return align_up(chunks * num_experts * 4, 256) * 2 + align_up((num_experts + 1) * 4, 256) * 3 +
          256;
 }
 
@@ -439,12 +448,13 @@ int moe_b200_permute(const int32_t* expert_idx, int64_t num_rows, int32_t k,
   auto* cb = reinterpret_cast<int32_t*>(ws + cbytes);
   auto* t128 = reinterpret_cast<int32_t*>(ws + 2 * cbytes);
   auto* t64 = reinterpret_cast<int32_t*>(ws + 2 * cbytes + tbytes);
-  auto* err = reinterpret_cast<int*>(ws + 2 * cbytes + 2 * tbytes);
+  auto* t256 = reinterpret_cast<int32_t*>(ws + 2 * cbytes + 2 * tbytes);
+  auto* err = reinterpret_cast<int*>(ws + 2 * cbytes + 3 * tbytes);
   const int T = static_cast<int>(num_rows), E = static_cast<int>(num_experts);
   MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, sizeof(int), s), "clear error word");
   if (T == 0) MOE_CUDA_CHECK(cudaMemsetAsync(cc, 0, cbytes, s), "clear counts");
   MOE_CUDA_CHECK(launch_histogram(expert_idx, T, k, E, cc, err, s), "histogram");
-  MOE_CUDA_CHECK(launch_plan(expert_idx, T, k, E, cc, cb, expert_offsets, t128, t64,
+  MOE_CUDA_CHECK(launch_plan(expert_idx, T, k, E, cc, cb, expert_offsets, t128, t64, t256,
                              permuted_pos, permuted_src, s),
                  "plan");
   int herr = 0;

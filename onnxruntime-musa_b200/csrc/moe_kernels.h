@@ -33,7 +33,8 @@ cudaError_t launch_histogram(const int32_t* idx, int T, int k, int E, int32_t* c
                              int* err, cudaStream_t s);
 cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* chunk_counts,
                         int32_t* chunk_base, int32_t* offsets, int32_t* tiles128,
-                        int32_t* tiles64, int32_t* pos, int32_t* src, cudaStream_t s);
+                        int32_t* tiles64, int32_t* tiles256, int32_t* pos, int32_t* src,
+                        cudaStream_t s);
 cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
                           int64_t rows, void* xp, cudaStream_t s);
 cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
@@ -64,6 +65,7 @@ struct GemmArgs {
   const int32_t* offsets;      // [E+1]
   const int32_t* tiles128;     // [E+1] prefix of ceil(count/128)
   const int32_t* tiles64;      // [E+1] prefix of ceil(count/64)
+  const int32_t* tiles256;     // [E+1] prefix of ceil(count/256)
   int E;
   const void* bias1;           // element (e, n) at bias1[e*bias_e_stride + n*bias_stride]
   const void* bias3;
@@ -78,6 +80,7 @@ struct GemmArgs {
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);
 // tcgen05 path; requires dtype f16/bf16, K % 8 == 0.
 bool tc_supported(const GemmArgs& g);
-cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s);
+// mode: 0 = choose, 1 = single-CTA kernel, 2 = CTA-pair (cta_group::2) kernel.
+cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, int mode, cudaStream_t s);
 
 }  // namespace moe

@@ -120,9 +120,9 @@ histogram_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, in
 __global__ void __launch_bounds__(1024)
 scan_kernel(const int32_t* __restrict__ chunk_counts, int num_chunks, int E,
             int32_t* __restrict__ chunk_base, int32_t* __restrict__ expert_offsets,
-            int32_t* __restrict__ tiles128, int32_t* __restrict__ tiles64) {
-  extern __shared__ int32_t s_tot[];  // [3][E]
-  int32_t* s_cnt = s_tot;
+            int32_t* __restrict__ tiles128, int32_t* __restrict__ tiles64,
+            int32_t* __restrict__ tiles256) {
+  extern __shared__ int32_t s_cnt[];  // [E]
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int32_t run = 0;
     for (int c = 0; c < num_chunks; ++c) {
@@ -134,19 +134,22 @@ scan_kernel(const int32_t* __restrict__ chunk_counts, int num_chunks, int E,
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int32_t o = 0, t128 = 0, t64 = 0;
+    int32_t o = 0, t128 = 0, t64 = 0, t256 = 0;
     for (int e = 0; e < E; ++e) {
       expert_offsets[e] = o;
       tiles128[e] = t128;
       tiles64[e] = t64;
+      tiles256[e] = t256;
       const int32_t c = s_cnt[e];
       o += c;
       t128 += (c + 127) / 128;
       t64 += (c + 63) / 64;
+      t256 += (c + 255) / 256;
     }
     expert_offsets[E] = o;
     tiles128[E] = t128;
     tiles64[E] = t64;
+    tiles256[E] = t256;
   }
 }
 
@@ -306,10 +309,11 @@ cudaError_t launch_histogram(const int32_t* idx, int T_, int k, int E, int32_t* 
 
 cudaError_t launch_plan(const int32_t* idx, int T_, int k, int E, const int32_t* chunk_counts,
                         int32_t* chunk_base, int32_t* offsets, int32_t* tiles128,
-                        int32_t* tiles64, int32_t* pos, int32_t* src, cudaStream_t s) {
+                        int32_t* tiles64, int32_t* tiles256, int32_t* pos, int32_t* src,
+                        cudaStream_t s) {
   const int chunks = num_route_chunks(T_);
-  scan_kernel<<<1, 1024, 3 * E * sizeof(int32_t), s>>>(chunk_counts, chunks, E, chunk_base,
-                                                       offsets, tiles128, tiles64);
+  scan_kernel<<<1, 1024, E * sizeof(int32_t), s>>>(chunk_counts, chunks, E, chunk_base,
+                                                   offsets, tiles128, tiles64, tiles256);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess || T_ == 0) return st;
   const size_t sm = (static_cast<size_t>(kRouteThreads / 32) + 2) * E * sizeof(int32_t);

@@ -196,3 +196,29 @@ def test_config2_mixtral_full_size(pkg, orc, dev):
     rows = torch.tensor([0, 1, 777, 2048, 4095] + list(range(1000, 1027)), device=dev)
     ref = _torch_rows_reference(pkg, orc, d, rows, attrs)
     np.testing.assert_allclose(as_np(out1[rows]), ref, **TOL["float16"])
+
+
+TC_CASES = [
+    # (T, H, I, E, k, act, gated, bias, dtype)
+    (300, 256, 384, 8, 2, "silu", True, False, "float16"),
+    (1000, 512, 256, 16, 4, "gelu", False, True, "bfloat16"),
+    (5, 128, 128, 64, 8, "silu", True, True, "float16"),       # most experts empty
+    (700, 256, 520, 4, 1, "relu", True, False, "bfloat16"),    # N tail, one expert per row
+    (2048, 1024, 768, 8, 2, "silu", True, False, "float16"),
+]
+
+
+@pytest.mark.parametrize("mode", ["1", "2"], ids=["single_cta", "cta_pair"])
+@pytest.mark.parametrize("case", TC_CASES, ids=lambda c: f"T{c[0]}H{c[1]}I{c[2]}E{c[3]}k{c[4]}{c[5]}")
+def test_tensor_core_kernels(pkg, orc, dev, mode, case):
+    """Both tcgen05 kernels (one CTA per tile, and CTA pairs with cta_group::2)."""
+    T, H, I, E, k, act, gated, bias, dtype_name = case
+    inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act=act, gated=gated, dtype="float32",
+                              bias=bias, normalize=1, seed=T + E + int(mode))
+    d, h = moe_inputs_on(dev, inp, dtype_name)
+    os.environ["MOE_B200_TC_MODE"] = mode
+    try:
+        out = run_moe(pkg, d, inp["attrs"])
+    finally:
+        del os.environ["MOE_B200_TC_MODE"]
+    np.testing.assert_allclose(as_np(out), oracle_out(orc, h, inp["attrs"]), **TOL[dtype_name])
