@@ -45,8 +45,8 @@ CFG = dict(T=4096, H=4096, I=14336, E=8, k=2)
 WORKLOAD = ("configs[1]: Mixtral-8x7B-shaped com.microsoft.MoE fp16, T={T} H=4096 I=14336 E=8 k=2 "
             "SwiGLU(fc3)")
 # DRAM bytes (read + write) of one fc1(+fc3) GEMM launch from the ncu capture
-# summarised in profiles/; None until a capture exists.
-FC1_TRAFFIC_BYTES = None
+# summarised in profiles/ (fc1 pass, dram__bytes_read.sum + dram__bytes_write.sum).
+FC1_TRAFFIC_BYTES = 2_488_566_000  # profiles/tc_pair_grouped_gemm_c2.md
 
 
 def peaks():
@@ -253,7 +253,7 @@ def bench_ours(args, rank, world, dev):
     fc1_flops, fc2_flops = alg_flops()
     fc1_s = stage_ms["fc1"] / 1e3
     achieved = fc1_flops / fc1_s / 1e12
-    roof = {"bound": "tensor", "kernel": "tc_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)",
+    roof = {"bound": "tensor", "kernel": "tc_pair_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)",
             "achieved": round(achieved, 1), "peak": peak_burst, "unit": "TFLOP/s",
             "frac": round(achieved / peak_burst, 4),
             "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)",
