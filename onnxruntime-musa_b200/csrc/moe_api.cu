@@ -304,6 +304,16 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   const void* w2 = t.fc2_weights;
   const void* w3 = t.fc3_weights;
   mark(kStDequant);
+  if (qmoe_use_decode(p)) {
+    // Decode-sized QMoE: stream the packed weights of the touched experts once.
+    mark(kStFc1);
+    int st = qmoe_decode_forward(p, t, xp, act, offs, pos, w, ws + L.qmoe, s);
+    if (st != MOE_B200_OK) return st;
+    mark(kStFc2);
+    mark(kStCombine);
+    mark(kNumStages);
+    return MOE_B200_OK;
+  }
   if (p.attrs.expert_weight_bits != 0) {
     // QMoE: dequantise the weights of every expert into the workspace, then run the
     // same grouped GEMMs.  (Small-T decode takes the weight-streaming path instead.)

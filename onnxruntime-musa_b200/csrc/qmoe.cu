@@ -1,6 +1,10 @@
 // QMoE dequantisation kernels.  HBM-bound byte work: each thread turns 8 codes
 // (4 bytes of int4 or 8 bytes of int8) into one 16-byte vector of fp16/bf16.
+#include <algorithm>
+#include <cstdlib>
+
 #include "qmoe.h"
+#include "qmoe_decode.h"
 
 namespace moe {
 
@@ -95,15 +99,121 @@ cudaError_t dequant(int dtype, const void* q, const void* scales, int64_t rows, 
   return cudaErrorInvalidValue;
 }
 
+}  // namespace
+
 int64_t fc1_rows(const moe_b200_problem& p) {
   const bool fused = p.attrs.activation_type == MOE_B200_ACT_SWIGLU && p.attrs.swiglu_fusion != 0;
   return fused ? 2 * p.inter_size : p.inter_size;
 }
 
+bool qmoe_use_decode(const moe_b200_problem& p) {
+  if (p.attrs.expert_weight_bits == 0) return false;
+  if (std::getenv("MOE_B200_QMOE_NO_DECODE") != nullptr) return false;
+  return p.num_rows * p.attrs.k <= kQmoeDecodeMaxRows &&
+         qmoe_decode_supported(p.dtype, p.attrs.expert_weight_bits, p.attrs.block_size,
+                               p.hidden_size, p.inter_size);
+}
+
+namespace {
+// K splits of the fc2 pass: enough warps to keep HBM busy when few experts are touched.
+int fc2_splits(const moe_b200_problem& p) {
+  const int64_t touched = std::min<int64_t>(p.num_experts, p.num_rows * p.attrs.k);
+  const int64_t warps = (p.hidden_size / 16) * std::max<int64_t>(touched, 1);
+  int s = static_cast<int>((8192 + warps - 1) / warps);
+  const int chunks = static_cast<int>(p.inter_size / 128);
+  return std::max(1, std::min({s, kQmoeMaxSplits, chunks}));
+}
 }  // namespace
+
+int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, const void* xp,
+                        void* act, const int32_t* offsets, const int32_t* pos, const float* w,
+                        uint8_t* ws, cudaStream_t s) {
+  if (t.fc1_scales == nullptr || t.fc2_scales == nullptr || (p.has_fc3 && t.fc3_scales == nullptr))
+    return set_error(MOE_B200_INVALID_ARGUMENT, "QMoE scales are required");
+  const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
+  const int64_t R = p.num_rows * p.attrs.k;
+  const bool fused = p.attrs.activation_type == MOE_B200_ACT_SWIGLU && p.attrs.swiglu_fusion != 0;
+  const int N1 = static_cast<int>(fc1_rows(p));
+  const auto* s1 = static_cast<const __half*>(t.fc1_scales);
+  QDecodeArgs a{};
+  a.x = static_cast<const __half*>(xp);
+  a.rows = R;
+  a.K = static_cast<int>(H);
+  a.N = static_cast<int>(I);
+  a.E = static_cast<int>(E);
+  a.offsets = offsets;
+  a.bits = p.attrs.expert_weight_bits;
+  a.block_size = p.attrs.block_size;
+  a.ap = ActParams{p.attrs.activation_type, p.attrs.activation_alpha, p.attrs.activation_beta,
+                   p.attrs.swiglu_limit};
+  a.bias_stride = 1;
+  a.bias_e_stride = I;
+  const uint8_t* q1 = static_cast<const uint8_t*>(t.fc1_weights);
+  if (p.has_fc3) {
+    a.gated = true;
+    a.b1 = QOperand{q1, s1, 0, 1, 0, static_cast<int>(I)};
+    a.b3 = QOperand{static_cast<const uint8_t*>(t.fc3_weights),
+                    static_cast<const __half*>(t.fc3_scales), 0, 1, 0, static_cast<int>(I)};
+    a.bias1 = t.fc1_bias;
+    a.bias3 = t.fc3_bias;
+  } else if (fused) {
+    a.gated = true;
+    a.bias_e_stride = 2 * I;
+    if (p.attrs.swiglu_fusion == 1) {
+      a.b1 = QOperand{q1, s1, 0, 2, 0, N1};
+      a.b3 = QOperand{q1, s1, 1, 2, 0, N1};
+      a.bias1 = t.fc1_bias;
+      a.bias3 = t.fc1_bias ? static_cast<const __half*>(t.fc1_bias) + 1 : nullptr;
+      a.bias_stride = 2;
+    } else {
+      a.b1 = QOperand{q1, s1, 0, 1, 0, N1};
+      a.b3 = QOperand{q1, s1, 0, 1, static_cast<int>(I), N1};
+      a.bias1 = t.fc1_bias;
+      a.bias3 = t.fc1_bias ? static_cast<const __half*>(t.fc1_bias) + I : nullptr;
+    }
+  } else {
+    a.gated = false;
+    a.b1 = QOperand{q1, s1, 0, 1, 0, static_cast<int>(I)};
+    a.bias1 = t.fc1_bias;
+  }
+  a.out = static_cast<__half*>(act);
+  a.ldo = I;
+  a.splits = 1;
+  cudaError_t st = launch_qmoe_decode(a, static_cast<int>(E), s);
+  if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "QMoE fc1 decode: %s", cudaGetErrorString(st));
+
+  QDecodeArgs b{};
+  b.x = static_cast<const __half*>(act);
+  b.rows = R;
+  b.K = static_cast<int>(I);
+  b.N = static_cast<int>(H);
+  b.E = static_cast<int>(E);
+  b.offsets = offsets;
+  b.bits = p.attrs.expert_weight_bits;
+  b.block_size = p.attrs.block_size;
+  b.gated = false;
+  b.b1 = QOperand{static_cast<const uint8_t*>(t.fc2_weights),
+                  static_cast<const __half*>(t.fc2_scales), 0, 1, 0, static_cast<int>(H)};
+  b.ap = ActParams{kIdentity, 1.f, 0.f, INFINITY};
+  b.bias1 = t.fc2_bias;
+  b.bias_stride = 1;
+  b.bias_e_stride = H;
+  b.out_partial = reinterpret_cast<float*>(ws);
+  b.ldo = H;
+  b.splits = fc2_splits(p);
+  st = launch_qmoe_decode(b, static_cast<int>(E), s);
+  if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "QMoE fc2 decode: %s", cudaGetErrorString(st));
+  st = launch_combine_partials(b.out_partial, b.splits, R, pos, w, static_cast<int>(p.num_rows),
+                               p.attrs.k, static_cast<int>(H), t.output, s);
+  if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "QMoE combine: %s", cudaGetErrorString(st));
+  return MOE_B200_OK;
+}
 
 size_t qmoe_workspace_bytes(const moe_b200_problem& p) {
   if (p.attrs.expert_weight_bits == 0) return 0;
+  if (qmoe_use_decode(p))
+    return align256(static_cast<size_t>(kQmoeMaxSplits) * p.num_rows * p.attrs.k *
+                    p.hidden_size * sizeof(float));
   const size_t es = dtype_bytes(p.dtype);
   const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
   size_t b = align256(E * fc1_rows(p) * H * es) + align256(E * H * I * es);

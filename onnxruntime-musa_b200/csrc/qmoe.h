@@ -14,8 +14,20 @@ struct QmoeDequantOut {
   const void* w3;
 };
 
-// Workspace bytes for the dequantised weight copies (0 for MoE problems).
+// Rows of one expert's fc1 weights (2*inter for fused swiglu, else inter).
+int64_t fc1_rows(const moe_b200_problem& p);
+
+// True when this QMoE call takes the weight-streaming decode kernels.
+bool qmoe_use_decode(const moe_b200_problem& p);
+
+// Workspace bytes of the QMoE path: fp32 partial sums (decode) or the dequantised
+// weight copies (larger calls); 0 for MoE problems.
 size_t qmoe_workspace_bytes(const moe_b200_problem& p);
+
+// Decode path: fc1 (+fc3) and fc2 from the packed weights, then the combine.
+int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, const void* xp,
+                        void* act, const int32_t* offsets, const int32_t* pos, const float* w,
+                        uint8_t* ws, cudaStream_t s);
 
 // Dequantises fc1/fc2(/fc3) of every expert into `ws` in element type p.dtype.
 int qmoe_dequantize(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,

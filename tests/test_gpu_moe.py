@@ -222,3 +222,83 @@ def test_tensor_core_kernels(pkg, orc, dev, mode, case):
     finally:
         del os.environ["MOE_B200_TC_MODE"]
     np.testing.assert_allclose(as_np(out), oracle_out(orc, h, inp["attrs"]), **TOL[dtype_name])
+
+
+def _qmoe_run(pkg, dev, q, attrs, fc3=True):
+    get = lambda n: to_dev(q[n], dev) if q.get(n) is not None else None
+    op = pkg.QMoE(**attrs)
+    try:
+        return op([get("x"), get("router_probs"), get("fc1_q"), get("fc1_scales"), get("fc1_b"),
+                   get("fc2_q"), get("fc2_scales"), get("fc2_b"),
+                   get("fc3_q") if fc3 else None, get("fc3_scales") if fc3 else None,
+                   get("fc3_b") if fc3 else None])
+    finally:
+        op.release()
+
+
+QMOE_DECODE_CASES = [
+    # (T, H, I, E, k, bits, block_size)
+    (1, 512, 384, 8, 2, 4, 128),
+    (8, 512, 384, 8, 2, 4, 128),
+    (32, 256, 512, 8, 2, 4, 32),
+    (64, 512, 256, 8, 2, 8, 0),
+    (17, 384, 640, 16, 2, 8, 64),
+    (3, 256, 256, 64, 8, 4, 0),
+]
+
+
+@pytest.mark.parametrize("case", QMOE_DECODE_CASES, ids=lambda c: f"T{c[0]}H{c[1]}I{c[2]}E{c[3]}k{c[4]}b{c[5]}bs{c[6]}")
+def test_qmoe_decode_path(pkg, orc, dev, case):
+    """Weight-streaming decode kernels against the oracle and the dequantise+GEMM path."""
+    T, H, I, E, k, bits, bs = case
+    # Scales keep the outputs near unit scale, where the fp16 tolerances are meaningful.
+    mu = -5.0 if bits == 4 else -8.5
+    q = orc.make_qmoe_inputs(T=T, H=H, I=I, E=E, k=k, bits=bits, block_size=bs,
+                             scale_mu=mu, scale_sigma=0.3, seed=T * 13 + bits)
+    attrs = dict(q["attrs"], k=k)
+    out = _qmoe_run(pkg, dev, q, attrs)
+    ref = orc.qmoe(q["x"], q["router_probs"], q["fc1_q"], q["fc1_scales"], None, q["fc2_q"],
+                   q["fc2_scales"], None, q["fc3_q"], q["fc3_scales"], None, **attrs)
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+    os.environ["MOE_B200_QMOE_NO_DECODE"] = "1"
+    try:
+        out2 = _qmoe_run(pkg, dev, q, attrs)
+    finally:
+        del os.environ["MOE_B200_QMOE_NO_DECODE"]
+    np.testing.assert_allclose(as_np(out2), ref, **TOL["float16"])
+
+
+@pytest.mark.parametrize("variant", ["plain_gelu_bias", "swiglu_interleaved", "swiglu_halves"])
+def test_qmoe_decode_variants(pkg, orc, dev, variant):
+    T, H, I, E, k, bits, bs = 6, 256, 256, 8, 2, 4, 64
+    rng = np.random.default_rng(77)
+    q = orc.make_qmoe_inputs(T=T, H=H, I=I, E=E, k=k, bits=bits, block_size=bs,
+                             scale_mu=-4.0, scale_sigma=0.3, seed=78)
+    attrs = dict(q["attrs"], k=k)
+    fc3 = True
+    if variant == "plain_gelu_bias":
+        attrs["activation_type"] = "gelu"
+        fc3 = False
+        q["fc1_b"] = (rng.standard_normal((E, I)) * 0.05).astype(np.float16)
+        q["fc2_b"] = (rng.standard_normal((E, H)) * 0.05).astype(np.float16)
+    else:
+        fusion = 1 if variant == "swiglu_interleaved" else 2
+        attrs.update(activation_type="swiglu", swiglu_fusion=fusion, activation_alpha=1.702,
+                     activation_beta=1.0, swiglu_limit=7.0)
+        if fusion == 1:
+            W = np.empty((E, 2 * I, H // 2), np.uint8); W[:, 0::2] = q["fc1_q"]; W[:, 1::2] = q["fc3_q"]
+            S = np.empty((E, 2 * I) + q["fc1_scales"].shape[2:], np.float16)
+            S[:, 0::2] = q["fc1_scales"]; S[:, 1::2] = q["fc3_scales"]
+        else:
+            W = np.concatenate([q["fc1_q"], q["fc3_q"]], 1)
+            S = np.concatenate([q["fc1_scales"], q["fc3_scales"]], 1)
+        q["fc1_q"], q["fc1_scales"] = W, S
+        q["fc1_b"] = (rng.standard_normal((E, 2 * I)) * 0.05).astype(np.float16)
+        fc3 = False
+    out = _qmoe_run(pkg, dev, q, attrs, fc3=fc3)
+    W1 = orc.dequantize(q["fc1_q"], q["fc1_scales"], bits, bs, H)
+    W2 = orc.dequantize(q["fc2_q"], q["fc2_scales"], bits, bs, I)
+    W3 = orc.dequantize(q["fc3_q"], q["fc3_scales"], bits, bs, H) if fc3 else None
+    ref = orc.moe(q["x"], q["router_probs"], W1, q.get("fc1_b"), W2, q.get("fc2_b"), W3, None,
+                  **{kk: v for kk, v in attrs.items() if kk not in ("expert_weight_bits", "block_size")})
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
