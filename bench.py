@@ -1,20 +1,25 @@
 """MoE-layer throughput benchmark of the B200 MoE execution provider.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c1|c2|c3|c4|c5] [--tokens T[,T...]] [--no-cpu]
 
-A "step" is one com.microsoft MoE layer call over one batch of synthetic tokens:
-benchmark config 2 of 5 (Mixtral-8x7B-shaped fp16 layer: T=4096, H=4096, I=14336,
-E=8, k=2, SwiGLU via fc3, no bias).  Inputs x, logits ~ N(0,1), weights ~ N(0, 0.02),
-generated on the device from a fixed seed (no dataset is involved).
+A "step" is one com.microsoft MoE / QMoE layer call over one batch of synthetic tokens.
+The default workload is benchmark config 2 of 5, the Mixtral-8x7B-shaped fp16 layer
+(T=4096, H=4096, I=14336, E=8, k=2, SwiGLU via fc3, no bias); the other configs are
+measured with --config for the kernel notes.  Inputs are generated on the device from
+fixed seeds with the configs' distributions (no dataset is involved): x, logits ~ N(0,1),
+weights ~ N(0, 0.02), biases ~ N(0, 0.01), int codes uniform with lognormal scales, and
+for config 4 a Zipf(1.1) per-expert logit bias rescaled to [0, 3].
 
 * ``value``: tokens/s with inputs resident in HBM, K timed steps bracketed by a
-  barrier + synchronize, CUDA events on the launching stream, max over ranks.
-  The weights (2.8 GB) exceed the 126 MB L2, so no explicit flush is needed.
+  barrier + synchronize, CUDA events on the launching stream, max over ranks.  Every
+  config except the small fp32 one streams more than the 126 MB L2 per step.
 * ``e2e``: the same metric through the kernel-object API (the call the plugin makes)
   with the step's input and router logits copied from pinned host memory and the
   output read back to host memory inside the timed region.
-* ``roofline``: the fc1(+fc3) grouped GEMM (the dominant kernel), its algorithmic
-  FLOPs per launch / its CUDA-event duration against the measured bf16/fp16 peak.
+* ``roofline``: the dominant kernel, its algorithmic FLOPs (tensor-bound configs) or
+  bytes (weight-streaming QMoE decode) per launch over its CUDA-event duration,
+  against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the C restatement of the CPU path (oracle/moe_oracle.c, "port")
   on a bounded sample of the same layer on the host cores.
 * ``--impl reference``: the same CPU restatement timed as the reference arm (the
@@ -41,20 +46,42 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-layer tokens/s"
 UNIT = "tokens/s"
-CFG = dict(T=4096, H=4096, I=14336, E=8, k=2)
-WORKLOAD = ("configs[1]: Mixtral-8x7B-shaped com.microsoft.MoE fp16, T={T} H=4096 I=14336 E=8 k=2 "
-            "SwiGLU(fc3)")
-# DRAM bytes (read + write) of one fc1(+fc3) GEMM launch from the ncu capture
-# summarised in profiles/ (fc1 pass, dram__bytes_read.sum + dram__bytes_write.sum).
-FC1_TRAFFIC_BYTES = 2_488_566_000  # profiles/tc_pair_grouped_gemm_c2.md
+
+CONFIGS = {
+    "c1": dict(kind="moe", T=256, H=512, I=1024, E=8, k=2, act="silu", gated=False,
+               dtype="float32", bias=True,
+               desc="configs[0]: com.microsoft.MoE fp32, T={T} H=512 I=1024 E=8 k=2 silu, "
+                    "fc1/fc2 bias"),
+    "c2": dict(kind="moe", T=4096, H=4096, I=14336, E=8, k=2, act="silu", gated=True,
+               dtype="float16", bias=False,
+               desc="configs[1]: Mixtral-8x7B-shaped com.microsoft.MoE fp16, T={T} H=4096 "
+                    "I=14336 E=8 k=2 SwiGLU(fc3)"),
+    "c3": dict(kind="qmoe", T=1, H=4096, I=14336, E=8, k=2, bits=4, block=128, mu=-5.0,
+               sigma=0.3,
+               desc="configs[2]: QMoE int4 block 128, fp16, Mixtral shape, T={T} E=8 k=2 "
+                    "SwiGLU(fc3)"),
+    "c4": dict(kind="moe", T=16384, H=2048, I=768, E=64, k=8, act="silu", gated=True,
+               dtype="float16", bias=False, zipf=True,
+               desc="configs[3]: fine-grained com.microsoft.MoE fp16, T={T} H=2048 I=768 "
+                    "E=64 k=8 SwiGLU, Zipf expert bias"),
+    "c5": dict(kind="qmoe", T=64, H=4096, I=6400, E=16, k=2, bits=8, block=0, mu=-6.0,
+               sigma=0.25,
+               desc="configs[4]: QMoE int8 per-row scales, fp16, T={T} H=4096 I=6400 E=16 "
+                    "k=2 SwiGLU(fc3)"),
+}
+
+# DRAM bytes (read + write) of one fc1(+fc3) launch of the default workload from the ncu
+# capture summarised in profiles/tc_pair_grouped_gemm_c2.md.
+FC1_TRAFFIC_BYTES = 2_488_566_000
 
 
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return d["bf16_tflops"], d.get("bf16_tflops_sustained"), d["hbm_gbs"], "measured"
-    return 1590.0, 1400.0, 6650.0, "fallback"
+        return dict(tflops=d["bf16_tflops"], tflops_sus=d.get("bf16_tflops_sustained"),
+                    hbm=d["hbm_gbs"], src="measured")
+    return dict(tflops=1590.0, tflops_sus=1400.0, hbm=6650.0, src="fallback")
 
 
 class ClockSampler:
@@ -67,12 +94,13 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.rows = []
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -87,8 +115,6 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.rows = [l.split(", ") for l in out.strip().splitlines() if l.strip()]
-        else:
-            self.rows = []
 
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
@@ -106,31 +132,103 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_layer(dev, seed):
+# ----------------------------------------------------------------- synthetic layer
+def make_layer(cfg, dev, seed):
+    """Device tensors of one layer with the config's distributions."""
     import torch
     g = torch.Generator(device=dev).manual_seed(seed)
-    T, H, I, E = CFG["T"], CFG["H"], CFG["I"], CFG["E"]
-    return dict(
-        x=torch.randn(T, H, device=dev, generator=g).half(),
-        router_probs=torch.randn(T, E, device=dev, generator=g).half(),
-        fc1_w=(torch.randn(E, I, H, device=dev, generator=g) * 0.02).half(),
-        fc2_w=(torch.randn(E, H, I, device=dev, generator=g) * 0.02).half(),
-        fc3_w=(torch.randn(E, I, H, device=dev, generator=g) * 0.02).half())
+    T, H, I, E = cfg["T"], cfg["H"], cfg["I"], cfg["E"]
+    rn = lambda *s: torch.randn(*s, device=dev, generator=g)
+    if cfg["kind"] == "moe":
+        dt = getattr(torch, cfg["dtype"])
+        logits = rn(T, E)
+        if cfg.get("zipf"):
+            import numpy as np
+            z = np.random.default_rng(seed).zipf(1.1, E).astype(np.float64)
+            span = z.max() - z.min()
+            bias_e = 3.0 * (z - z.min()) / span if span > 0 else np.zeros(E)
+            logits = logits + torch.tensor(bias_e, device=dev, dtype=torch.float32)[None, :]
+        return dict(x=rn(T, H).to(dt), router_probs=logits.to(dt),
+                    fc1_w=(rn(E, I, H) * 0.02).to(dt), fc2_w=(rn(E, H, I) * 0.02).to(dt),
+                    fc3_w=(rn(E, I, H) * 0.02).to(dt) if cfg["gated"] else None,
+                    fc1_b=(rn(E, I) * 0.01).to(dt) if cfg.get("bias") else None,
+                    fc2_b=(rn(E, H) * 0.01).to(dt) if cfg.get("bias") else None)
+    bits, bs = cfg["bits"], cfg["block"]
+    lo, hi = (-8, 7) if bits == 4 else (-127, 127)
+
+    def weights(N, K):
+        codes = torch.randint(lo, hi + 1, (E, N, K), device=dev, generator=g, dtype=torch.int16)
+        if bits == 4:
+            q = (codes + 8).to(torch.uint8)
+            packed = (q[..., 0::2] | (q[..., 1::2] << 4)).contiguous()
+        else:
+            packed = (codes + 128).to(torch.uint8)
+        del codes
+        shape = (E, N, (K + bs - 1) // bs) if bs else (E, N)
+        sc = torch.exp(cfg["mu"] + cfg["sigma"] * torch.randn(*shape, device=dev, generator=g))
+        return packed, sc.half()
+
+    q1, s1 = weights(I, H)
+    q3, s3 = weights(I, H)
+    q2, s2 = weights(H, I)
+    return dict(x=rn(T, H).half(), router_probs=rn(T, E).half(), fc1_q=q1, fc1_s=s1, fc2_q=q2,
+                fc2_s=s2, fc3_q=q3, fc3_s=s3)
 
 
-def alg_flops():
-    c = CFG
-    fc1 = c["T"] * c["k"] * 2 * 2 * c["H"] * c["I"]   # fc1 + fc3
-    fc2 = c["T"] * c["k"] * 2 * c["H"] * c["I"]
-    return fc1, fc2
+def problem_and_tensors(pkg, cfg, L, out):
+    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    if cfg["kind"] == "moe":
+        dt = {"float32": pkg.FLOAT, "float16": pkg.FLOAT16, "bfloat16": pkg.BFLOAT16}[cfg["dtype"]]
+        prob = pkg.make_problem(T, H, I, E, dt, has_fc3=cfg["gated"], activation_type=cfg["act"],
+                                k=k, normalize_routing_weights=1)
+        tens = dict(input=L["x"], router_probs=L["router_probs"], fc1_weights=L["fc1_w"],
+                    fc1_bias=L["fc1_b"], fc2_weights=L["fc2_w"], fc2_bias=L["fc2_b"],
+                    fc3_weights=L["fc3_w"], output=out)
+        inputs = [L["x"], L["router_probs"], L["fc1_w"], L["fc1_b"], L["fc2_w"], L["fc2_b"],
+                  L["fc3_w"], None]
+        op_attrs = dict(activation_type=cfg["act"], k=k, normalize_routing_weights=1)
+        return prob, tens, inputs, op_attrs, "MoE"
+    prob = pkg.make_problem(T, H, I, E, pkg.FLOAT16, has_fc3=True, activation_type="silu", k=k,
+                            normalize_routing_weights=1, expert_weight_bits=cfg["bits"],
+                            block_size=cfg["block"])
+    tens = dict(input=L["x"], router_probs=L["router_probs"], fc1_weights=L["fc1_q"],
+                fc1_scales=L["fc1_s"], fc2_weights=L["fc2_q"], fc2_scales=L["fc2_s"],
+                fc3_weights=L["fc3_q"], fc3_scales=L["fc3_s"], output=out)
+    inputs = [L["x"], L["router_probs"], L["fc1_q"], L["fc1_s"], None, L["fc2_q"], L["fc2_s"],
+              None, L["fc3_q"], L["fc3_s"], None]
+    op_attrs = dict(activation_type="silu", k=k, normalize_routing_weights=1,
+                    expert_weight_bits=cfg["bits"], block_size=cfg["block"])
+    return prob, tens, inputs, op_attrs, "QMoE"
+
+
+def algorithmic(cfg, L, pkg):
+    """FLOPs and bytes of one layer call (bytes over the experts this routing touches)."""
+    import torch
+    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    n_mat = 3 if (cfg["kind"] == "qmoe" or cfg["gated"]) else 2
+    flops_fc1 = T * k * 2 * (n_mat - 1) * H * I
+    flops_fc2 = T * k * 2 * H * I
+    idx, _ = pkg.route(L["router_probs"], k, 1)
+    touched = int(torch.unique(idx).numel())
+    if cfg["kind"] == "moe":
+        es = 4 if cfg["dtype"] == "float32" else 2
+        per_expert = n_mat * H * I * es
+        act_es = es
+    else:
+        per_w = H * I * cfg["bits"] // 8
+        nb_h = (H + cfg["block"] - 1) // cfg["block"] if cfg["block"] else 1
+        nb_i = (I + cfg["block"] - 1) // cfg["block"] if cfg["block"] else 1
+        per_expert = 3 * per_w + (2 * I * nb_h + H * nb_i) * 2
+        act_es = 2
+    io = T * H * act_es * 2 + T * E * act_es
+    return dict(flops=flops_fc1 + flops_fc2, flops_fc1=flops_fc1, flops_fc2=flops_fc2,
+                bytes=touched * per_expert + io, touched=touched,
+                bytes_fc1=touched * per_expert * (n_mat - 1) / n_mat,
+                bytes_fc2=touched * per_expert / n_mat)
 
 
 # ------------------------------------------------------------------ CPU baseline
-def cpu_baseline(layer, budget_s=12.0):
-    """The C restatement (oracle/moe_oracle.c) on a bounded token sample of the layer,
-    all host cores.  Weights are handed over as fp32 copies (prepacked once, outside
-    the timed call)."""
-    import numpy as np
+def _oracle_lib():
     so = ROOT / "oracle" / "_build" / "libmoe_oracle.so"
     if not so.exists():
         subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], check=True)
@@ -139,48 +237,61 @@ def cpu_baseline(layer, budget_s=12.0):
     L.oracle_moe.argtypes = [ctypes.c_int64] * 4 + [ctypes.c_int] * 4 + [ctypes.c_float] * 3 + \
         [ctypes.c_int] * 2 + [ctypes.c_void_p] * 12
     L.oracle_get_threads.restype = ctypes.c_int
-    cores = L.oracle_get_threads()
-    f = lambda t: np.ascontiguousarray(t.float().cpu().numpy())
-    w1, w2, w3 = f(layer["fc1_w"]), f(layer["fc2_w"]), f(layer["fc3_w"])
-    x_all, lg_all = f(layer["x"]), f(layer["router_probs"])
-    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    return L
+
+
+def cpu_baseline(cfg, L, budget_s=12.0):
+    """The C restatement (oracle/moe_oracle.c) on a bounded token sample of the layer, all
+    host cores.  MoE weights are handed over as fp32 copies (prepacked once, outside the
+    timed call); QMoE weights stay packed and are dequantised inside the call."""
+    import numpy as np
+    lib = _oracle_lib()
+    cores = lib.oracle_get_threads()
+    f = lambda t: None if t is None else np.ascontiguousarray(t.float().cpu().numpy())
+    u8 = lambda t: np.ascontiguousarray(t.cpu().numpy())
+    P = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+    x_all, lg_all = f(L["x"]), f(L["router_probs"])
+    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    if cfg["kind"] == "moe":
+        w1, w2, w3, b1, b2 = f(L["fc1_w"]), f(L["fc2_w"]), f(L["fc3_w"]), f(L["fc1_b"]), f(L["fc2_b"])
+        act = {"silu": 2, "gelu": 1, "relu": 0, "identity": 3}[cfg["act"]]
+        bits = bs = 0
+        s1 = s2 = s3 = None
+    else:
+        w1, w2, w3 = u8(L["fc1_q"]), u8(L["fc2_q"]), u8(L["fc3_q"])
+        s1, s2, s3 = f(L["fc1_s"]), f(L["fc2_s"]), f(L["fc3_s"])
+        b1 = b2 = None
+        act, bits, bs = 2, cfg["bits"], cfg["block"]
 
     def run(n):
         x, lg = np.ascontiguousarray(x_all[:n]), np.ascontiguousarray(lg_all[:n])
         out = np.zeros_like(x)
         t0 = time.perf_counter()
-        rc = L.oracle_moe(n, CFG["H"], CFG["I"], CFG["E"], CFG["k"], 1, 2, 0, 1.0, 0.0,
-                          math.inf, 0, 0, P(x), P(lg), P(w1), None, None, P(w2), None, None,
-                          P(w3), None, None, P(out))
-        dt = time.perf_counter() - t0
+        rc = lib.oracle_moe(n, H, I, E, k, 1, act, 0, 1.0, 0.0, math.inf, bits, bs, P(x), P(lg),
+                            P(w1), P(s1), P(b1), P(w2), P(s2), P(b2), P(w3), P(s3), None, P(out))
         if rc != 0:
             raise RuntimeError("oracle_moe failed")
-        return dt
+        return time.perf_counter() - t0
 
-    n = 32
+    n = min(T, 32)
     dt = run(n)
-    n2 = int(min(CFG["T"], max(n, n * budget_s / max(dt, 1e-3) * 0.8)))
+    n2 = int(min(T, max(n, n * budget_s / max(dt, 1e-3) * 0.8)))
     if n2 > n:
         n, dt = n2, run(n2)
     return {"value": n / dt, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n} of {CFG['T']} tokens of the same layer (all 8 experts, fp32 "
-                      f"weights), one call, {dt:.2f} s"}
+            "sample": f"{n} of {T} tokens of the same layer, one call, {dt:.2f} s"}
 
 
 # ------------------------------------------------------------------ our arm
-def bench_ours(args, rank, world, dev):
+def bench_ours(args, cfg, rank, world, dev):
     import torch
     import __graft_entry__ as ge
     pkg = ge.load_package()
-    layer = make_layer(dev, 20261202 + rank)
-    T, H, I, E, k = CFG["T"], CFG["H"], CFG["I"], CFG["E"], CFG["k"]
-    prob = pkg.make_problem(T, H, I, E, pkg.FLOAT16, has_fc3=True, activation_type="silu",
-                            k=k, normalize_routing_weights=1)
+    L = make_layer(cfg, dev, 20261202 + rank)
+    T = cfg["T"]
+    out = torch.empty_like(L["x"])
+    prob, tens, inputs, op_attrs, op_type = problem_and_tensors(pkg, cfg, L, out)
     ws = torch.empty(pkg.workspace_size(prob), dtype=torch.uint8, device=dev)
-    out = torch.empty_like(layer["x"])
-    tens = dict(input=layer["x"], router_probs=layer["router_probs"],
-                fc1_weights=layer["fc1_w"], fc2_weights=layer["fc2_w"],
-                fc3_weights=layer["fc3_w"], output=out)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -194,24 +305,27 @@ def bench_ours(args, rank, world, dev):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident throughput
-    for _ in range(args.warmup):
-        pkg.forward(prob, tens, ws, stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            pkg.forward(prob, tens, ws, stream)
-        ev1.record(stream)
+    def timed(step, steps):
+        for _ in range(args.warmup):
+            step()
         torch.cuda.synchronize(dev)
-    barrier()
-    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / steps
+
+    # ---- device-resident throughput
+    with ClockSampler(dev.index) as clk:
+        ms = timed(lambda: pkg.forward(prob, tens, ws, stream), args.steps)
     value = world * T / (ms / 1e3)
 
-    # ---- per-stage CUDA-event times (dominant kernel)
+    # ---- per-stage CUDA-event times
     stage = {s: [] for s in pkg.STAGES}
     for _ in range(max(3, min(args.steps, 10))):
         for s, v in pkg.forward_timed(prob, tens, ws, stream).items():
@@ -219,89 +333,96 @@ def bench_ours(args, rank, world, dev):
     stage_ms = {s: statistics.median(v) for s, v in stage.items()}
 
     # ---- end to end through the kernel object with host buffers
-    op = pkg.MoE(activation_type="silu", k=k, normalize_routing_weights=1)
-    hx = layer["x"].cpu().pin_memory()
-    hl = layer["router_probs"].cpu().pin_memory()
+    op = (pkg.QMoE if op_type == "QMoE" else pkg.MoE)(**op_attrs)
+    hx, hl = L["x"].cpu().pin_memory(), L["router_probs"].cpu().pin_memory()
     hout = torch.empty_like(hx).pin_memory()
-    dx, dl = torch.empty_like(layer["x"]), torch.empty_like(layer["router_probs"])
-    inputs = [dx, dl, layer["fc1_w"], None, layer["fc2_w"], None, layer["fc3_w"], None]
+    dx, dl = torch.empty_like(L["x"]), torch.empty_like(L["router_probs"])
+    e2e_inputs = [dx, dl] + inputs[2:]
 
     def e2e_step():
         dx.copy_(hx, non_blocking=True)
         dl.copy_(hl, non_blocking=True)
-        op(inputs, out=out, stream=stream)
+        op(e2e_inputs, out=out, stream=stream)
         hout.copy_(out, non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier()
-    torch.cuda.synchronize(dev)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    ev1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    e2e_ms = timed(e2e_step, args.steps)
     op.release()
+    es = hx.element_size()
     e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
-           "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 2,
-           "d2h_bytes_per_step": hout.numel() * 2}
+           "h2d_bytes_per_step": hx.numel() * es + hl.numel() * es,
+           "d2h_bytes_per_step": hout.numel() * es}
 
-    peak_burst, peak_sus, _, peak_src = peaks()
-    fc1_flops, fc2_flops = alg_flops()
-    fc1_s = stage_ms["fc1"] / 1e3
-    achieved = fc1_flops / fc1_s / 1e12
-    roof = {"bound": "tensor", "kernel": "tc_pair_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)",
-            "achieved": round(achieved, 1), "peak": peak_burst, "unit": "TFLOP/s",
-            "frac": round(achieved / peak_burst, 4),
-            "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)",
-            "frac_of_sustained": round(achieved / peak_sus, 4) if peak_sus else None,
-            "traffic": FC1_TRAFFIC_BYTES,
-            "alg_flops_per_launch": fc1_flops,
-            "fc2": {"achieved": round(fc2_flops / (stage_ms["fc2"] / 1e3) / 1e12, 1)},
-            "layer_frac": round((fc1_flops + fc2_flops) / (ms / 1e3) / 1e12 / peak_burst, 4)}
-    launches_per_step = 7  # route, scan, permute, gather, fc1, fc2, combine
+    pk = peaks()
+    alg = algorithmic(cfg, L, pkg)
+    decode = cfg["kind"] == "qmoe" and T * cfg["k"] <= 128
+    if decode:
+        achieved = alg["bytes_fc1"] / (stage_ms["fc1"] / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": "qmoe_decode_kernel (fc1+fc3 pass)",
+                "achieved": round(achieved, 1), "peak": pk["hbm"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm"], 4), "traffic": None,
+                "peak_source": f"{pk['src']} HBM copy (MEASURED_PEAKS.json)",
+                "alg_bytes_per_launch": int(alg["bytes_fc1"]),
+                "fc2": {"achieved": round(alg["bytes_fc2"] / (stage_ms["fc2"] / 1e3) / 1e9, 1)},
+                "experts_touched": alg["touched"],
+                "layer_frac": round((alg["bytes"] / pk["hbm"] / 1e9) / (ms / 1e3), 4)}
+    else:
+        k_name = ("simt_gemm_kernel (FFMA)" if cfg["kind"] == "moe" and cfg["dtype"] == "float32"
+                  else "tc_pair_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)")
+        achieved = alg["flops_fc1"] / (stage_ms["fc1"] / 1e3) / 1e12
+        roof_t = max(alg["flops"] / (pk["tflops"] * 1e12), alg["bytes"] / (pk["hbm"] * 1e9))
+        roof = {"bound": "tensor", "kernel": k_name, "achieved": round(achieved, 1),
+                "peak": pk["tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["tflops"], 4),
+                "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)",
+                "frac_of_sustained": round(achieved / pk["tflops_sus"], 4) if pk["tflops_sus"] else None,
+                "traffic": FC1_TRAFFIC_BYTES if (args.config == "c2" and T == 4096) else None,
+                "alg_flops_per_launch": alg["flops_fc1"],
+                "fc2": {"achieved": round(alg["flops_fc2"] / (stage_ms["fc2"] / 1e3) / 1e12, 1)},
+                "layer_frac": round(roof_t / (ms / 1e3), 4)}
+    # Launches per layer call: route, scan, permute, gather, fc1, fc2, combine; QMoE
+    # prefill adds three dequantisation launches.
+    launches = 10 if (cfg["kind"] == "qmoe" and not decode) else 7
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic (seeded N(0,1) tokens/logits, N(0,0.02) weights; random init)",
-        "config": {"workload": WORKLOAD.format(T=T), "global_batch": T * world, "tokens_per_gpu": T,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if cfg.get("dtype") == "float32" else "f16",
+        "data": "synthetic (seeded, on-device; config distributions; random init)",
+        "config": {"workload": cfg["desc"].format(T=T), "global_batch": T * world,
+                   "tokens_per_gpu": T,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (2.8 GB of weights per step)"},
+                   "l2": "inputs larger than L2 (weights streamed every step)"
+                         if alg["bytes"] > 126e6 else "inputs smaller than L2 (not flushed)"},
         "e2e": e2e, "roofline": roof,
         "stage_ms": {s: round(v, 4) for s, v in stage_ms.items()},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu:
-        result["cpu_baseline"] = cpu_baseline(layer)
+        result["cpu_baseline"] = cpu_baseline(cfg, L)
     return result
 
 
-def bench_reference(args, rank, world):
+def bench_reference(args, cfg, rank, world):
     """Reference arm: the CPU restatement of the path on this host's cores."""
     import torch
     if rank != 0:
         return None
-    dev = torch.device("cuda:0") if torch.cuda.is_available() else torch.device("cpu")
-    layer = make_layer(dev, 20261202) if dev.type == "cuda" else None
-    if layer is None:
+    if not torch.cuda.is_available():
         return {"impl": "reference", "unavailable": "no CUDA device to generate the layer on"}
-    times = []
-    base = None
+    L = make_layer(cfg, torch.device("cuda:0"), 20261202)
+    vals, base = [], None
+    budget = max(2.0, 60.0 / (args.warmup + args.steps))
     for i in range(args.warmup + args.steps):
-        base = cpu_baseline(layer, budget_s=max(2.0, 60.0 / (args.warmup + args.steps)))
+        base = cpu_baseline(cfg, L, budget_s=budget)
         if i >= args.warmup:
-            times.append(base["value"])
-    v = statistics.median(times)
+            vals.append(base["value"])
+    v = statistics.median(vals)
     base["value"] = v
     return {"metric": METRIC, "value": round(v, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "impl": "reference", "dtype": "f32",
-            "config": {"workload": WORKLOAD.format(T=T), "engine": "C restatement of the CPU path"},
+            "config": {"workload": cfg["desc"].format(T=cfg["T"]),
+                       "engine": "C restatement of the CPU path (oracle/moe_oracle.c)"},
             "cpu_baseline": base,
             "e2e": {"value": round(v, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -313,29 +434,33 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--tokens", default=None,
+                    help="tokens per GPU (comma list for a sweep); default: the config's")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--tokens", type=int, default=CFG["T"],
-                    help="tokens per GPU (default: the config's 4096; smaller for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     import torch
-    CFG["T"] = args.tokens
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    base = CONFIGS[args.config]
+    sweep = [int(t) for t in args.tokens.split(",")] if args.tokens else [base["T"]]
     if args.impl == "reference":
-        res = bench_reference(args, rank, world)
-        if res is not None:
-            print(json.dumps(res), flush=True)
+        for T in sweep:
+            res = bench_reference(args, dict(base, T=T), rank, world)
+            if res is not None:
+                print(json.dumps(res), flush=True)
         return
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=dev)
-    res = bench_ours(args, rank, world, dev)
-    if rank == 0:
-        print(json.dumps(res), flush=True)
+    for T in sweep:
+        res = bench_ours(args, dict(base, T=T), rank, world, dev)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
 

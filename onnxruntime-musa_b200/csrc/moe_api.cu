@@ -289,13 +289,36 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   void* act = ws + L.act;
 
   MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, sizeof(int), s), "clear error word");
+  const size_t es = dtype_bytes(p.dtype);
+  if (qmoe_use_decode(p)) {
+    // Decode-sized QMoE: one CTA routes and plans, then the packed weights of the
+    // touched experts are streamed once (token rows are read in place: no gather).
+    mark(kStRoute);
+    MOE_CUDA_CHECK(launch_small_dispatch(p.dtype, t.router_probs, T, E, k,
+                                         p.attrs.normalize_routing_weights, idx, w, offs, pos,
+                                         src, s),
+                   "route");
+    mark(kStPlan);
+    mark(kStGather);
+    mark(kStDequant);
+    mark(kStFc1);
+    int st = qmoe_decode_fc1(p, t, src, act, offs, ws + L.qmoe, s);
+    if (st != MOE_B200_OK) return st;
+    mark(kStFc2);
+    st = qmoe_decode_fc2(p, t, act, offs, ws + L.qmoe, s);
+    if (st != MOE_B200_OK) return st;
+    mark(kStCombine);
+    st = qmoe_decode_combine(p, t, ws + L.qmoe, offs, pos, w, s);
+    if (st != MOE_B200_OK) return st;
+    mark(kNumStages);
+    return MOE_B200_OK;
+  }
   mark(kStRoute);
   MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
                               p.attrs.normalize_routing_weights, idx, w, cc, s),
                  "route");
   mark(kStPlan);
   MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s), "plan");
-  const size_t es = dtype_bytes(p.dtype);
   mark(kStGather);
   MOE_CUDA_CHECK(launch_gather(t.input, static_cast<int64_t>(H) * es, k, src, R, xp, s),
                  "gather");
@@ -304,19 +327,9 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   const void* w2 = t.fc2_weights;
   const void* w3 = t.fc3_weights;
   mark(kStDequant);
-  if (qmoe_use_decode(p)) {
-    // Decode-sized QMoE: stream the packed weights of the touched experts once.
-    mark(kStFc1);
-    int st = qmoe_decode_forward(p, t, xp, act, offs, pos, w, ws + L.qmoe, s);
-    if (st != MOE_B200_OK) return st;
-    mark(kStFc2);
-    mark(kStCombine);
-    mark(kNumStages);
-    return MOE_B200_OK;
-  }
   if (p.attrs.expert_weight_bits != 0) {
-    // QMoE: dequantise the weights of every expert into the workspace, then run the
-    // same grouped GEMMs.  (Small-T decode takes the weight-streaming path instead.)
+    // QMoE prefill: dequantise the weights of every expert into the workspace, then run
+    // the same grouped GEMMs.
     QmoeDequantOut dq;
     int st = qmoe_dequantize(p, t, ws + L.qmoe, offs, &dq, s);
     if (st != MOE_B200_OK) return st;

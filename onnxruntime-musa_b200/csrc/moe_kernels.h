@@ -26,9 +26,16 @@ inline int num_route_chunks(int64_t rows) {
 }
 constexpr int kMaxExperts = 256;
 constexpr int kMaxK = 32;
+// Routed rows (T*k) up to which routing and the dispatch plan run in one CTA.
+constexpr int kSmallDispatchRows = 1024;
 
 cudaError_t launch_route(int dtype, const void* logits, int T, int E, int k, int normalize,
                          int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s);
+// Routing + offsets + permutation of a call with T*k <= kSmallDispatchRows, one CTA
+// (no GEMM tile prefixes: for the decode kernels only).
+cudaError_t launch_small_dispatch(int dtype, const void* logits, int T, int E, int k,
+                                  int normalize, int32_t* idx, float* w, int32_t* offsets,
+                                  int32_t* pos, int32_t* src, cudaStream_t s);
 cudaError_t launch_histogram(const int32_t* idx, int T, int k, int E, int32_t* chunk_counts,
                              int* err, cudaStream_t s);
 cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* chunk_counts,

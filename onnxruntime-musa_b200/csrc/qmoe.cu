@@ -115,19 +115,31 @@ bool qmoe_use_decode(const moe_b200_problem& p) {
 }
 
 namespace {
-// K splits of the fc2 pass: enough warps to keep HBM busy when few experts are touched.
-int fc2_splits(const moe_b200_problem& p) {
+
+// K splits of a decode pass over N output rows of K columns: enough warp tiles
+// (16 rows each) to fill the GPU several times over when few experts are touched.
+int decode_splits(const moe_b200_problem& p, int64_t N, int64_t K) {
   const int64_t touched = std::min<int64_t>(p.num_experts, p.num_rows * p.attrs.k);
-  const int64_t warps = (p.hidden_size / 16) * std::max<int64_t>(touched, 1);
-  int s = static_cast<int>((8192 + warps - 1) / warps);
-  const int chunks = static_cast<int>(p.inter_size / 128);
+  const int64_t tiles = (N + 15) / 16 * std::max<int64_t>(touched, 1);
+  const int64_t target = 148 * 4 * 8;  // 8 waves of 4 warps per SM
+  const int s = static_cast<int>((target + tiles - 1) / tiles);
+  const int chunks = static_cast<int>(K / 128);
   return std::max(1, std::min({s, kQmoeMaxSplits, chunks}));
 }
+int fc1_splits(const moe_b200_problem& p) { return decode_splits(p, p.inter_size, p.hidden_size); }
+int fc2_splits(const moe_b200_problem& p) { return decode_splits(p, p.hidden_size, p.inter_size); }
+
+// Workspace of the decode path: fc1 partials [S1][R][2I] then fc2 partials [S2][R][H].
+size_t fc1_partial_bytes(const moe_b200_problem& p) {
+  const int s1 = fc1_splits(p);
+  if (s1 == 1) return 0;
+  return align256(static_cast<size_t>(s1) * p.num_rows * p.attrs.k * 2 * p.inter_size * sizeof(float));
+}
+
 }  // namespace
 
-int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, const void* xp,
-                        void* act, const int32_t* offsets, const int32_t* pos, const float* w,
-                        uint8_t* ws, cudaStream_t s) {
+int qmoe_decode_fc1(const moe_b200_problem& p, const moe_b200_tensors& t, const int32_t* src,
+                    void* act, const int32_t* offsets, uint8_t* ws, cudaStream_t s) {
   if (t.fc1_scales == nullptr || t.fc2_scales == nullptr || (p.has_fc3 && t.fc3_scales == nullptr))
     return set_error(MOE_B200_INVALID_ARGUMENT, "QMoE scales are required");
   const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
@@ -136,7 +148,9 @@ int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, co
   const int N1 = static_cast<int>(fc1_rows(p));
   const auto* s1 = static_cast<const __half*>(t.fc1_scales);
   QDecodeArgs a{};
-  a.x = static_cast<const __half*>(xp);
+  a.x = static_cast<const __half*>(t.input);  // routed row p reads input row src[p] / k
+  a.src_rows = src;
+  a.k = p.attrs.k;
   a.rows = R;
   a.K = static_cast<int>(H);
   a.N = static_cast<int>(I);
@@ -176,14 +190,28 @@ int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, co
     a.b1 = QOperand{q1, s1, 0, 1, 0, static_cast<int>(I)};
     a.bias1 = t.fc1_bias;
   }
-  a.out = static_cast<__half*>(act);
-  a.ldo = I;
-  a.splits = 1;
+  a.splits = fc1_splits(p);
+  if (a.splits == 1) {
+    a.out = static_cast<__half*>(act);
+    a.ldo = I;
+  } else {
+    a.out_partial = reinterpret_cast<float*>(ws);
+    a.ldo = a.gated ? 2 * I : I;
+  }
   cudaError_t st = launch_qmoe_decode(a, static_cast<int>(E), s);
+  if (st == cudaSuccess && a.splits > 1) st = launch_finalize_fc1(a, static_cast<__half*>(act), s);
   if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "QMoE fc1 decode: %s", cudaGetErrorString(st));
+  return MOE_B200_OK;
+}
 
+int qmoe_decode_fc2(const moe_b200_problem& p, const moe_b200_tensors& t, const void* act,
+                    const int32_t* offsets, uint8_t* ws, cudaStream_t s) {
+  const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
+  const int64_t R = p.num_rows * p.attrs.k;
   QDecodeArgs b{};
   b.x = static_cast<const __half*>(act);
+  b.src_rows = nullptr;
+  b.k = p.attrs.k;
   b.rows = R;
   b.K = static_cast<int>(I);
   b.N = static_cast<int>(H);
@@ -195,16 +223,24 @@ int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, co
   b.b1 = QOperand{static_cast<const uint8_t*>(t.fc2_weights),
                   static_cast<const __half*>(t.fc2_scales), 0, 1, 0, static_cast<int>(H)};
   b.ap = ActParams{kIdentity, 1.f, 0.f, INFINITY};
-  b.bias1 = t.fc2_bias;
   b.bias_stride = 1;
   b.bias_e_stride = H;
-  b.out_partial = reinterpret_cast<float*>(ws);
+  b.out_partial = reinterpret_cast<float*>(ws + fc1_partial_bytes(p));
   b.ldo = H;
   b.splits = fc2_splits(p);
-  st = launch_qmoe_decode(b, static_cast<int>(E), s);
+  cudaError_t st = launch_qmoe_decode(b, static_cast<int>(E), s);
   if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "QMoE fc2 decode: %s", cudaGetErrorString(st));
-  st = launch_combine_partials(b.out_partial, b.splits, R, pos, w, static_cast<int>(p.num_rows),
-                               p.attrs.k, static_cast<int>(H), t.output, s);
+  return MOE_B200_OK;
+}
+
+int qmoe_decode_combine(const moe_b200_problem& p, const moe_b200_tensors& t, const uint8_t* ws,
+                        const int32_t* offsets, const int32_t* pos, const float* w,
+                        cudaStream_t s) {
+  const int64_t R = p.num_rows * p.attrs.k;
+  cudaError_t st = launch_combine_partials(
+      reinterpret_cast<const float*>(ws + fc1_partial_bytes(p)), fc2_splits(p), R, pos, w,
+      static_cast<int>(p.num_rows), p.attrs.k, static_cast<int>(p.hidden_size), offsets,
+      static_cast<int>(p.num_experts), t.fc2_bias, t.output, s);
   if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "QMoE combine: %s", cudaGetErrorString(st));
   return MOE_B200_OK;
 }
@@ -212,8 +248,9 @@ int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, co
 size_t qmoe_workspace_bytes(const moe_b200_problem& p) {
   if (p.attrs.expert_weight_bits == 0) return 0;
   if (qmoe_use_decode(p))
-    return align256(static_cast<size_t>(kQmoeMaxSplits) * p.num_rows * p.attrs.k *
-                    p.hidden_size * sizeof(float));
+    return fc1_partial_bytes(p) +
+           align256(static_cast<size_t>(fc2_splits(p)) * p.num_rows * p.attrs.k * p.hidden_size *
+                    sizeof(float));
   const size_t es = dtype_bytes(p.dtype);
   const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
   size_t b = align256(E * fc1_rows(p) * H * es) + align256(E * H * I * es);

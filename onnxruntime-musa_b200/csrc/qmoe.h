@@ -24,10 +24,16 @@ bool qmoe_use_decode(const moe_b200_problem& p);
 // weight copies (larger calls); 0 for MoE problems.
 size_t qmoe_workspace_bytes(const moe_b200_problem& p);
 
-// Decode path: fc1 (+fc3) and fc2 from the packed weights, then the combine.
-int qmoe_decode_forward(const moe_b200_problem& p, const moe_b200_tensors& t, const void* xp,
-                        void* act, const int32_t* offsets, const int32_t* pos, const float* w,
-                        uint8_t* ws, cudaStream_t s);
+// Decode path, in three steps: fc1 (+fc3) from the packed weights into `act` (token
+// rows read from the layer input through `src`, the inverse permutation), fc2 into
+// fp32 partial sums in `ws`, and the routing-weighted combine of the partials.
+int qmoe_decode_fc1(const moe_b200_problem& p, const moe_b200_tensors& t, const int32_t* src,
+                    void* act, const int32_t* offsets, uint8_t* ws, cudaStream_t s);
+int qmoe_decode_fc2(const moe_b200_problem& p, const moe_b200_tensors& t, const void* act,
+                    const int32_t* offsets, uint8_t* ws, cudaStream_t s);
+int qmoe_decode_combine(const moe_b200_problem& p, const moe_b200_tensors& t, const uint8_t* ws,
+                        const int32_t* offsets, const int32_t* pos, const float* w,
+                        cudaStream_t s);
 
 // Dequantises fc1/fc2(/fc3) of every expert into `ws` in element type p.dtype.
 int qmoe_dequantize(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,

@@ -1,24 +1,35 @@
 // QMoE decode path: weight-streaming grouped GEMM for small routed-row counts.
 //
-// At decode sizes (T*k routed rows in the tens) a QMoE layer is bound by reading
-// the packed weights of the touched experts from HBM.  This kernel streams them once:
-// each warp owns 16 output rows of one expert (16 gate + 16 linear rows when gated),
-// loads their packed int4/int8 codes for a 128-wide K chunk with 16-byte coalesced
-// loads (the next chunk is prefetched into a second register set), dequantises in
-// registers ((q - zero_point) * scale in half2 arithmetic, exact before the scale) and
-// feeds the codes straight into mma.sync m16n8k16 as the A operand, with the expert's
-// routed token rows as the B operand (swap-AB: D[weight row, token]).  Experts with no
-// routed rows launch CTAs that exit immediately, so untouched experts cost no traffic.
+// At decode sizes (T*k routed rows in the tens) a QMoE layer is bound by reading the
+// packed weights of the touched experts from HBM.  This kernel streams them once: each
+// warp owns 16 output rows of one expert (16 gate + 16 linear rows when gated) and
+// walks K in 128-wide chunks.  The codes reach shared memory through a warp-private
+// cp.async ring (4 KB to 14 KB per warp in flight, enough bytes per SM to cover HBM
+// latency), are converted to fp16 in registers and fed to mma.sync m16n8k16 as the A
+// operand, with the expert's routed token rows as the B operand (swap-AB:
+// D[weight row, token]).  Token rows are read in place from the layer input through the
+// inverse permutation, so no gather pass runs.  Experts with no routed rows launch CTAs
+// that exit at once: untouched experts cost no traffic.
 //
-// K permutation: within a 128-wide chunk, thread t (of the 4 sharing a row) holds the
-// 32 consecutive codes [32t, 32t+32).  MMA step j (0..7) uses, for that thread, codes
-// 32t+4j .. 32t+4j+3 in the fragment slots {2t, 2t+1, 2t+8, 2t+9}; the B fragment is
-// gathered with the same mapping (one 8-byte load of 4 consecutive activations), so the
-// products are summed over exactly the same k pairs as an in-order dot product.
+// Scale modes (kScale):
+//   kScaleRow    one scale per output row: the MMA runs on the integer codes (exact in
+//                fp16) and the fp32 sum is scaled once at the end;
+//   kScaleChunk  block scales covering whole 128-wide chunks (block_size >= 128): codes
+//                exact, each chunk's fp32 partial sum is scaled and accumulated;
+//   kScaleElem   smaller blocks: codes are scaled during the fp16 conversion.
 //
-// fc2 (a long K = inter_size) is split over K across CTAs; each split writes fp32
-// partial sums [split][row][col] and the combine kernel adds splits in fixed order,
-// so the result is deterministic.
+// K permutation.  A dot product may take its k terms in any order as long as A and B
+// agree.  Thread t (of the 4 sharing a row) handles the 32 consecutive codes
+// [32t, 32t+32) of a chunk and places 4 of them per MMA step in the fragment slots
+// {2t, 2t+1, 2t+8, 2t+9}; the B fragment is gathered with the same mapping:
+//   * int8, and int4 in kScaleElem: step j takes codes 32t+4j .. 32t+4j+3 in order;
+//   * int4 in the exact modes: word m (codes 8m..8m+7) is split by one shift + mask per
+//     half2 into pairs (c_i, c_{i+4}); steps 2m / 2m+1 take pairs (0,1) / (2,3), and the
+//     activations are permuted to match with prmt.
+//
+// fc2 (long K = inter_size) is split over K across CTAs; each split writes fp32 partial
+// sums [split][row][col] and the combine kernel adds splits in a fixed order, so the
+// result is deterministic.
 #include "qmoe_decode.h"
 
 namespace moe {
@@ -27,6 +38,10 @@ namespace {
 
 constexpr int QD_WARPS = 4;
 constexpr int QD_CHUNK = 128;
+// Stages of the per-warp ring: 8 for int4 and 4 for int8, the same bytes in flight.
+template <int BITS> constexpr int qd_stages() { return BITS == 4 ? 8 : 4; }
+
+enum ScaleMode { kScaleRow = 0, kScaleChunk = 1, kScaleElem = 2 };
 
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                               uint32_t b1) {
@@ -40,80 +55,87 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// Two int4 codes of one byte -> half2 (q_lo - 8, q_hi - 8) * s.  1024 + q is built by
-// placing q in the mantissa of 1024.0h (0x6400); the subtraction is exact.
-__device__ __forceinline__ uint32_t deq4(uint32_t byte, __half2 s2) {
+// 1024 + q for a code q placed in the mantissa of 1024.0h (0x6400); subtracting
+// 1024 + zero_point is exact.
+__device__ __forceinline__ __half2 h2c(uint16_t bits) {
+  return __halves2half2(__ushort_as_half(bits), __ushort_as_half(bits));
+}
+// Codes (lo nibble, hi nibble) of one byte -> (q_lo - 8, q_hi - 8) * s.
+__device__ __forceinline__ uint32_t deq4_scaled(uint32_t byte, __half2 s2) {
   const uint32_t u = (byte & 0xFu) | ((byte & 0xF0u) << 12) | 0x64006400u;
-  const __half2 v = __hsub2(bits_h2(u), __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408)));
-  return h2_bits(__hmul2(v, s2));
+  return h2_bits(__hmul2(__hsub2(bits_h2(u), h2c(0x6408)), s2));
 }
-// Bytes (b0, b1) of a word selected by `sel` -> half2 (b0 - 128, b1 - 128) * s.
-__device__ __forceinline__ uint32_t deq8(uint32_t word, uint32_t sel, __half2 s2) {
-  const uint32_t u = __byte_perm(word, 0x64646464u, sel);
-  const __half2 v = __hsub2(bits_h2(u), __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
-  return h2_bits(__hmul2(v, s2));
+// Nibbles i and i+4 of a word (after shifting it right by 4i) -> (q - 8) exact.
+__device__ __forceinline__ uint32_t deq4_pair(uint32_t shifted) {
+  const uint32_t u = (shifted & 0x000F000Fu) | 0x64006400u;
+  return h2_bits(__hsub2(bits_h2(u), h2c(0x6408)));
 }
-
-// Packed codes of one weight row for one chunk: 64 bytes (int4) or 128 bytes (int8),
-// of which this thread holds 16 or 32.
-template <int BITS> struct Codes { uint4 v[BITS / 4]; };
-
-template <int BITS>
-__device__ __forceinline__ void load_codes(Codes<BITS>& c, const uint8_t* row, int chunk, int t) {
-  const uint4* p = reinterpret_cast<const uint4*>(row + static_cast<int64_t>(chunk) * (QD_CHUNK * BITS / 8) +
-                                                  t * (32 * BITS / 8));
-#pragma unroll
-  for (int i = 0; i < BITS / 4; ++i) c.v[i] = __ldg(p + i);
+// Bytes of a word selected by `sel` -> (b - 128) exact, optionally scaled.
+__device__ __forceinline__ uint32_t deq8(uint32_t word, uint32_t sel) {
+  return h2_bits(__hsub2(bits_h2(__byte_perm(word, 0x64646464u, sel)), h2c(0x6480)));
+}
+__device__ __forceinline__ uint32_t deq8_scaled(uint32_t word, uint32_t sel, __half2 s2) {
+  return h2_bits(__hmul2(bits_h2(deq8(word, sel)), s2));
 }
 
-// A-fragment registers (slots 2t..: codes 32t+4j .. 32t+4j+3) of step j.
-template <int BITS>
-__device__ __forceinline__ void frag(const Codes<BITS>& c, int j, __half2 s2, uint32_t& lo,
-                                     uint32_t& hi) {
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(c.v);
-  if (BITS == 4) {
-    const uint32_t word = w[j >> 1];                 // bytes 2j, 2j+1 live in word j/2
-    const uint32_t sh = (j & 1) * 16;
-    lo = deq4((word >> sh) & 0xFFu, s2);
-    hi = deq4((word >> (sh + 8)) & 0xFFu, s2);
-  } else {
-    const uint32_t word = w[j];                      // bytes 4j .. 4j+3
-    lo = deq8(word, 0x4140u, s2);
-    hi = deq8(word, 0x4342u, s2);
-  }
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-struct RowPtrs {
-  const uint8_t* r0;   // row n0+g
-  const uint8_t* r8;   // row n0+g+8
-  const __half* s0;    // scales of those rows
-  const __half* s8;
-};
-
-__device__ __forceinline__ RowPtrs row_ptrs(const QOperand& b, int e, int n, int N, int K, int bits,
-                                            int nb) {
-  const int na = min(n, N - 1), nb8 = min(n + 8, N - 1);
-  const int64_t row_bytes = static_cast<int64_t>(K) * bits / 8;
-  const int64_t sr0 = static_cast<int64_t>(e) * b.n_rows + static_cast<int64_t>(na + b.n_off) * b.G + b.g;
-  const int64_t sr8 = static_cast<int64_t>(e) * b.n_rows + static_cast<int64_t>(nb8 + b.n_off) * b.G + b.g;
-  RowPtrs r;
-  r.r0 = b.q + sr0 * row_bytes;
-  r.r8 = b.q + sr8 * row_bytes;
-  r.s0 = b.scales + sr0 * nb;
-  r.s8 = b.scales + sr8 * nb;
-  return r;
+// Stored row of output row n (clamped into range) of expert e.
+__device__ __forceinline__ int64_t stored_row(const QOperand& b, int e, int n, int N) {
+  return static_cast<int64_t>(e) * b.n_rows + static_cast<int64_t>(min(n, N - 1) + b.n_off) * b.G +
+         b.g;
 }
 
-template <int BITS, int NG, bool GATED>
+template <int BITS, int NG, bool GATED, int kScale>
 __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_begin, int cnt,
-                                         int tok0, int n0, int c_begin, int c_end, int split) {
+                                         int tok0, int n0, int c_begin, int c_end, int split,
+                                         uint8_t* ring) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int nb = a.block_size ? (a.K + a.block_size - 1) / a.block_size : 1;
   constexpr int NT = GATED ? 2 : 1;
-  RowPtrs rp[NT];
-  rp[0] = row_ptrs(a.b1, e, n0 + g, a.N, a.K, BITS, nb);
-  if (GATED) rp[NT - 1] = row_ptrs(a.b3, e, n0 + g, a.N, a.K, BITS, nb);
+  constexpr int ROW_CHUNK = QD_CHUNK * BITS / 8;  // bytes of one row per chunk
+  constexpr int PPR = ROW_CHUNK / 16;              // 16-byte pieces per row chunk
+  constexpr int STAGE = NT * 16 * ROW_CHUNK;       // bytes per stage of this warp
+  constexpr int PER_LANE = NT * 16 * PPR / 32;     // pieces each lane copies per chunk
+  const int64_t row_bytes = static_cast<int64_t>(a.K) * BITS / 8;
+
+  // Sources of the cp.async pieces of this lane (fixed across chunks).
+  const uint8_t* src[PER_LANE];
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    const int p = lane + 32 * i;
+    const int x = p / (16 * PPR);
+    const int r = (p / PPR) % 16;
+    const QOperand& b = (GATED && x == 1) ? a.b3 : a.b1;
+    src[i] = b.q + stored_row(b, e, n0 + r, a.N) * row_bytes + (p % PPR) * 16;
+  }
+  auto issue = [&](int c, int stage) {
+    uint8_t* dst = ring + stage * STAGE;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i)
+      cp_async16(dst + (lane + 32 * i) * 16, src[i] + static_cast<int64_t>(c) * ROW_CHUNK);
+  };
+
+  // Scale rows of this thread (rows n0+g and n0+g+8 of each tile).
+  const __half* sc0[NT];
+  const __half* sc8[NT];
+#pragma unroll
+  for (int x = 0; x < NT; ++x) {
+    const QOperand& b = (GATED && x == 1) ? a.b3 : a.b1;
+    sc0[x] = b.scales + stored_row(b, e, n0 + g, a.N) * nb;
+    sc8[x] = b.scales + stored_row(b, e, n0 + g + 8, a.N) * nb;
+  }
 
   float acc[NT][NG][4];
 #pragma unroll
@@ -123,63 +145,161 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
 #pragma unroll
       for (int z = 0; z < 4; ++z) acc[x][y][z] = 0.f;
 
-  // Activation row pointers of this thread's B columns (token g of each group).
+  // Activation rows of this thread's B columns (token g of each group).
   const __half* xrow[NG];
   bool tok_ok[NG];
 #pragma unroll
   for (int gi = 0; gi < NG; ++gi) {
     const int tok = tok0 + gi * 8 + g;
     tok_ok[gi] = tok < cnt;
-    xrow[gi] = a.x + static_cast<int64_t>(row_begin + (tok_ok[gi] ? tok : 0)) * a.K + 32 * t;
+    const int64_t prow = row_begin + (tok_ok[gi] ? tok : 0);
+    const int64_t xr = a.src_rows ? a.src_rows[prow] / a.k : prow;
+    xrow[gi] = a.x + xr * a.K + 32 * t;
   }
 
-  Codes<BITS> cur[NT][2], nxt[NT][2];
+  __syncwarp();
 #pragma unroll
-  for (int x = 0; x < NT; ++x) {
-    load_codes<BITS>(cur[x][0], rp[x].r0, c_begin, t);
-    load_codes<BITS>(cur[x][1], rp[x].r8, c_begin, t);
+  for (int st = 0; st < qd_stages<BITS>() - 1; ++st) {
+    if (c_begin + st < c_end) issue(c_begin + st, st);
+    cp_async_commit();
   }
   for (int c = c_begin; c < c_end; ++c) {
-    if (c + 1 < c_end) {
-#pragma unroll
-      for (int x = 0; x < NT; ++x) {
-        load_codes<BITS>(nxt[x][0], rp[x].r0, c + 1, t);
-        load_codes<BITS>(nxt[x][1], rp[x].r8, c + 1, t);
-      }
-    }
-    const int sidx = a.block_size ? (c * QD_CHUNK + 32 * t) / a.block_size : 0;
-    __half2 s0[NT], s8[NT];
+    const int stage = (c - c_begin) % qd_stages<BITS>();
+    cp_async_wait<qd_stages<BITS>() - 2>();
+    __syncwarp();
+    const uint8_t* sb = ring + stage * STAGE;
+    uint4 code[NT][2][BITS / 4];  // [tile][row g / g+8][16-byte words]
 #pragma unroll
     for (int x = 0; x < NT; ++x) {
-      s0[x] = __half2half2(rp[x].s0[sidx]);
-      s8[x] = __half2half2(rp[x].s8[sidx]);
-    }
+      const uint4* r0 = reinterpret_cast<const uint4*>(sb + (x * 16 + g) * ROW_CHUNK + t * (ROW_CHUNK / 4));
+      const uint4* r8 = reinterpret_cast<const uint4*>(sb + (x * 16 + g + 8) * ROW_CHUNK + t * (ROW_CHUNK / 4));
 #pragma unroll
-    for (int j = 0; j < QD_CHUNK / 16; ++j) {
-      uint32_t af[NT][4];
+      for (int i = 0; i < BITS / 4; ++i) {
+        code[x][0][i] = r0[i];
+        code[x][1][i] = r8[i];
+      }
+    }
+    __syncwarp();
+    if (c + qd_stages<BITS>() - 1 < c_end) issue(c + qd_stages<BITS>() - 1, (c - c_begin + qd_stages<BITS>() - 1) % qd_stages<BITS>());
+    cp_async_commit();
+
+    __half2 s0[NT], s8[NT];
+    if (kScale == kScaleElem) {
+      const int sidx = (c * QD_CHUNK + 32 * t) / a.block_size;
 #pragma unroll
       for (int x = 0; x < NT; ++x) {
-        frag<BITS>(cur[x][0], j, s0[x], af[x][0], af[x][2]);
-        frag<BITS>(cur[x][1], j, s8[x], af[x][1], af[x][3]);
+        s0[x] = __half2half2(sc0[x][sidx]);
+        s8[x] = __half2half2(sc8[x][sidx]);
       }
+    }
+    constexpr int PX = kScale == kScaleChunk ? NT : 1;
+    constexpr int PG = kScale == kScaleChunk ? NG : 1;
+    float part[PX][PG][4];
+    if (kScale == kScaleChunk) {
+#pragma unroll
+      for (int x = 0; x < PX; ++x)
+#pragma unroll
+        for (int y = 0; y < PG; ++y)
+#pragma unroll
+          for (int z = 0; z < 4; ++z) part[x][y][z] = 0.f;
+    }
+
+    // Steps are taken in pairs (j = 2m, 2m+1) that share one 16-byte activation load
+    // per token group: activations 32t+8m .. 32t+8m+7.
+#pragma unroll
+    for (int m = 0; m < QD_CHUNK / 32; ++m) {
+      uint4 xv[NG];
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi)
+        xv[gi] = tok_ok[gi] ? __ldg(reinterpret_cast<const uint4*>(xrow[gi] + c * QD_CHUNK + 8 * m))
+                            : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * m + h;
+        uint32_t af[NT][4];
+#pragma unroll
+        for (int x = 0; x < NT; ++x) {
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {  // r=0: row g -> a0/a2, r=1: row g+8 -> a1/a3
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(code[x][r]);
+            uint32_t lo, hi;
+            if (BITS == 4 && kScale != kScaleElem) {
+              const uint32_t word = w[m] >> (h * 8);  // pairs (0,4),(1,5) or (2,6),(3,7)
+              lo = deq4_pair(word);
+              hi = deq4_pair(word >> 4);
+            } else if (BITS == 4) {
+              const uint32_t word = w[m] >> (h * 16);
+              const __half2 s2 = r ? s8[x] : s0[x];
+              lo = deq4_scaled(word & 0xFFu, s2);
+              hi = deq4_scaled((word >> 8) & 0xFFu, s2);
+            } else if (kScale == kScaleElem) {
+              const __half2 s2 = r ? s8[x] : s0[x];
+              lo = deq8_scaled(w[j], 0x4140u, s2);
+              hi = deq8_scaled(w[j], 0x4342u, s2);
+            } else {
+              lo = deq8(w[j], 0x4140u);
+              hi = deq8(w[j], 0x4342u);
+            }
+            af[x][r] = lo;
+            af[x][r + 2] = hi;
+          }
+        }
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          uint32_t b0, b1;
+          if (BITS == 4 && kScale != kScaleElem) {
+            // Regroup activations as (x_i, x_{i+4}) pairs to match the codes.
+            const uint32_t p0 = h ? xv[gi].y : xv[gi].x;
+            const uint32_t p1 = h ? xv[gi].w : xv[gi].z;
+            b0 = __byte_perm(p0, p1, 0x5410u);
+            b1 = __byte_perm(p0, p1, 0x7632u);
+          } else {
+            b0 = h ? xv[gi].z : xv[gi].x;  // activations 4j, 4j+1
+            b1 = h ? xv[gi].w : xv[gi].y;  // activations 4j+2, 4j+3
+          }
+#pragma unroll
+          for (int x = 0; x < NT; ++x) {
+            if (kScale == kScaleChunk) mma_f16_16816(part[x < PX ? x : 0][gi < PG ? gi : 0], af[x], b0, b1);
+            else mma_f16_16816(acc[x][gi], af[x], b0, b1);
+          }
+        }
+      }
+    }
+    if (kScale == kScaleChunk) {
+      const int sidx = (c * QD_CHUNK) / a.block_size;
+#pragma unroll
+      for (int x = 0; x < NT; ++x) {
+        const float f0 = __half2float(sc0[x][sidx]), f8 = __half2float(sc8[x][sidx]);
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          const float* pp = part[x < PX ? x : 0][gi < PG ? gi : 0];
+          acc[x][gi][0] = fmaf(f0, pp[0], acc[x][gi][0]);
+          acc[x][gi][1] = fmaf(f0, pp[1], acc[x][gi][1]);
+          acc[x][gi][2] = fmaf(f8, pp[2], acc[x][gi][2]);
+          acc[x][gi][3] = fmaf(f8, pp[3], acc[x][gi][3]);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+  if (kScale == kScaleRow) {
+#pragma unroll
+    for (int x = 0; x < NT; ++x) {
+      const float f0 = __half2float(sc0[x][0]), f8 = __half2float(sc8[x][0]);
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) {
-        uint2 bv = make_uint2(0u, 0u);
-        if (tok_ok[gi]) bv = __ldg(reinterpret_cast<const uint2*>(xrow[gi] + c * QD_CHUNK + 4 * j));
-#pragma unroll
-        for (int x = 0; x < NT; ++x) mma_f16_16816(acc[x][gi], af[x], bv.x, bv.y);
-      }
-    }
-    if (c + 1 < c_end) {
-#pragma unroll
-      for (int x = 0; x < NT; ++x) {
-        cur[x][0] = nxt[x][0];
-        cur[x][1] = nxt[x][1];
+        acc[x][gi][0] *= f0;
+        acc[x][gi][1] *= f0;
+        acc[x][gi][2] *= f8;
+        acc[x][gi][3] *= f8;
       }
     }
   }
 
   // Epilogue: acc[x][gi] = {D(n0+g, 2t), D(n0+g, 2t+1), D(n0+g+8, 2t), D(n0+g+8, 2t+1)}
+  const __half* b1p = static_cast<const __half*>(a.bias1);
+  const __half* b3p = static_cast<const __half*>(a.bias3);
 #pragma unroll
   for (int gi = 0; gi < NG; ++gi) {
 #pragma unroll
@@ -189,20 +309,17 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
       if (n >= a.N || tok >= cnt) continue;
       const int64_t row = row_begin + tok;
       float v = acc[0][gi][q];
+      const int64_t bi = e * a.bias_e_stride + static_cast<int64_t>(n) * a.bias_stride;
       if (a.out_partial != nullptr) {
-        if (split == 0 && a.bias1 != nullptr)
-          v += __half2float(static_cast<const __half*>(a.bias1)[e * a.bias_e_stride +
-                                                                static_cast<int64_t>(n) * a.bias_stride]);
-        a.out_partial[(static_cast<int64_t>(split) * a.rows + row) * a.ldo + n] = v;
+        // Split-K partial sums; biases and the activation are applied by the reader.
+        float* prow = a.out_partial + (static_cast<int64_t>(split) * a.rows + row) * a.ldo;
+        prow[n] = v;
+        if (GATED) prow[a.N + n] = acc[NT - 1][gi][q];
       } else {
-        if (a.bias1 != nullptr)
-          v += __half2float(static_cast<const __half*>(a.bias1)[e * a.bias_e_stride +
-                                                                static_cast<int64_t>(n) * a.bias_stride]);
+        if (b1p != nullptr) v += __half2float(b1p[bi]);
         if (GATED) {
           float u = acc[NT - 1][gi][q];
-          if (a.bias3 != nullptr)
-            u += __half2float(static_cast<const __half*>(a.bias3)[e * a.bias_e_stride +
-                                                                  static_cast<int64_t>(n) * a.bias_stride]);
+          if (b3p != nullptr) u += __half2float(b3p[bi]);
           v = act_gated(a.ap, v, u);
         } else {
           v = act_single(a.ap.act, v);
@@ -214,7 +331,12 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
 }
 
 template <int BITS, bool GATED>
+constexpr int ring_bytes() { return qd_stages<BITS>() * (GATED ? 2 : 1) * 16 * QD_CHUNK * BITS / 8; }
+
+template <int BITS, bool GATED, int kScale>
 __global__ void __launch_bounds__(QD_WARPS * 32) qmoe_decode_kernel(const QDecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t s_ring[];  // one ring per warp
+  uint8_t* ring = s_ring + (threadIdx.x >> 5) * ring_bytes<BITS, GATED>();
   const int e = blockIdx.y;
   const int row_begin = a.offsets[e];
   const int cnt = a.offsets[e + 1] - row_begin;
@@ -228,42 +350,112 @@ __global__ void __launch_bounds__(QD_WARPS * 32) qmoe_decode_kernel(const QDecod
   const int c_begin = split * per;
   const int c_end = min(nchunks, c_begin + per);
   if (c_begin >= c_end) {
-    // An empty split still owns its partial-sum slice: write zeros (bias lives in split 0).
+    // An empty split still owns its partial-sum slice: write zeros.
     if (a.out_partial != nullptr) {
       const int lane = threadIdx.x & 31;
       for (int i = lane; i < 16 * cnt; i += 32) {
         const int n = n0 + (i & 15), tok = i >> 4;
-        if (n < a.N)
-          a.out_partial[(static_cast<int64_t>(split) * a.rows + row_begin + tok) * a.ldo + n] = 0.f;
+        if (n >= a.N) continue;
+        float* prow = a.out_partial + (static_cast<int64_t>(split) * a.rows + row_begin + tok) * a.ldo;
+        prow[n] = 0.f;
+        if (GATED) prow[a.N + n] = 0.f;
       }
     }
     return;
   }
-  // Up to 32 routed rows per pass over the weights (4 groups of 8 MMA columns).
-  for (int tok0 = 0; tok0 < cnt; tok0 += 32) {
-    const int groups = min(4, (cnt - tok0 + 7) / 8);
-    if (groups <= 1) run_pass<BITS, 1, GATED>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split);
-    else if (groups <= 2) run_pass<BITS, 2, GATED>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split);
-    else run_pass<BITS, 4, GATED>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split);
+  // Up to kMaxGroups groups of 8 routed rows per pass over the weights.
+  constexpr int kMaxGroups = (GATED && (BITS == 8 || kScale == kScaleChunk)) ? 4 : 8;
+  for (int tok0 = 0; tok0 < cnt; tok0 += 8 * kMaxGroups) {
+    const int groups = min(kMaxGroups, (cnt - tok0 + 7) / 8);
+    if (groups <= 1)
+      run_pass<BITS, 1, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+    else if (groups <= 2)
+      run_pass<BITS, 2, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+    else if (groups <= 4 || kMaxGroups == 4)
+      run_pass<BITS, 4, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+    else
+      run_pass<BITS, 8, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
   }
 }
 
-// out[t] = sum_j w[t,j] * sum_s partial[s][pos[t,j]] (fixed order), fp32 -> fp16.
+// Expert of permuted row r (binary search over the offsets).
+__device__ __forceinline__ int expert_of(const int32_t* offsets, int E, int64_t r) {
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (offsets[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// fc1 finalisation of split-K partial sums: act[r, n] = act(sum_s P[s][r][n] + b1,
+// sum_s P[s][r][N + n] + b3) in fixed split order, fp32 -> fp16.
+__global__ void __launch_bounds__(256)
+finalize_fc1_kernel(const QDecodeArgs a, __half* __restrict__ act) {
+  const int64_t r = blockIdx.y;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= a.N) return;
+  const int e = expert_of(a.offsets, a.E, r);
+  const int64_t bi = e * a.bias_e_stride + static_cast<int64_t>(n) * a.bias_stride;
+  float g = 0.f, u = 0.f;
+  for (int s = 0; s < a.splits; ++s) {
+    const float* prow = a.out_partial + (static_cast<int64_t>(s) * a.rows + r) * a.ldo;
+    g += prow[n];
+    if (a.gated) u += prow[a.N + n];
+  }
+  const __half* b1p = static_cast<const __half*>(a.bias1);
+  const __half* b3p = static_cast<const __half*>(a.bias3);
+  if (b1p != nullptr) g += __half2float(b1p[bi]);
+  float v;
+  if (a.gated) {
+    if (b3p != nullptr) u += __half2float(b3p[bi]);
+    v = act_gated(a.ap, g, u);
+  } else {
+    v = act_single(a.ap.act, g);
+  }
+  act[r * a.N + n] = __float2half_rn(v);
+}
+
+// out[t] = sum_j w[t,j] * (sum_s partial[s][pos[t,j]] + bias) (fixed order), fp32 -> fp16.
 __global__ void __launch_bounds__(256)
 combine_partials_kernel(const float* __restrict__ part, int splits, int64_t rows,
                         const int32_t* __restrict__ pos, const float* __restrict__ w, int k,
-                        int H, __half* __restrict__ out) {
-  const int t = blockIdx.x;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const int64_t r = pos[static_cast<int64_t>(t) * k + j];
-      float y = 0.f;
-      for (int s = 0; s < splits; ++s) y += part[(static_cast<int64_t>(s) * rows + r) * H + c];
-      acc += w[static_cast<int64_t>(t) * k + j] * y;
-    }
-    out[static_cast<int64_t>(t) * H + c] = __float2half_rn(acc);
+                        int H, const int32_t* __restrict__ offsets, int E,
+                        const __half* __restrict__ bias, __half* __restrict__ out) {
+  const int t = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  float acc = 0.f;
+  for (int j = 0; j < k; ++j) {
+    const int64_t r = pos[static_cast<int64_t>(t) * k + j];
+    float y = 0.f;
+    for (int s = 0; s < splits; ++s) y += part[(static_cast<int64_t>(s) * rows + r) * H + c];
+    if (bias != nullptr) y += __half2float(bias[static_cast<int64_t>(expert_of(offsets, E, r)) * H + c]);
+    acc += w[static_cast<int64_t>(t) * k + j] * y;
   }
+  out[static_cast<int64_t>(t) * H + c] = __float2half_rn(acc);
+}
+
+template <int BITS, bool GATED, int kScale>
+cudaError_t launch_decode_t(const QDecodeArgs& a, cudaStream_t s) {
+  constexpr int kSmem = QD_WARPS * ring_bytes<BITS, GATED>();
+  static bool attr_set = false;  // idempotent; a race between first callers is benign
+  if (!attr_set) {
+    cudaError_t st = cudaFuncSetAttribute(qmoe_decode_kernel<BITS, GATED, kScale>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (st != cudaSuccess) return st;
+    attr_set = true;
+  }
+  const dim3 grid((a.N + QD_WARPS * 16 - 1) / (QD_WARPS * 16), a.E, a.splits);
+  qmoe_decode_kernel<BITS, GATED, kScale><<<grid, QD_WARPS * 32, kSmem, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <int BITS, bool GATED>
+cudaError_t launch_decode_b(const QDecodeArgs& a, cudaStream_t s) {
+  if (a.block_size == 0) return launch_decode_t<BITS, GATED, kScaleRow>(a, s);
+  if (a.block_size % QD_CHUNK == 0) return launch_decode_t<BITS, GATED, kScaleChunk>(a, s);
+  return launch_decode_t<BITS, GATED, kScaleElem>(a, s);
 }
 
 }  // namespace
@@ -276,24 +468,26 @@ bool qmoe_decode_supported(int dtype, int bits, int block_size, int64_t H, int64
 }
 
 cudaError_t launch_qmoe_decode(const QDecodeArgs& a, int max_experts_touched, cudaStream_t s) {
-  const dim3 block(QD_WARPS * 32);
-  const dim3 grid((a.N + QD_WARPS * 16 - 1) / (QD_WARPS * 16), a.E, a.splits);
   (void)max_experts_touched;
-  if (a.bits == 4) {
-    if (a.gated) qmoe_decode_kernel<4, true><<<grid, block, 0, s>>>(a);
-    else qmoe_decode_kernel<4, false><<<grid, block, 0, s>>>(a);
-  } else {
-    if (a.gated) qmoe_decode_kernel<8, true><<<grid, block, 0, s>>>(a);
-    else qmoe_decode_kernel<8, false><<<grid, block, 0, s>>>(a);
-  }
+  if (a.bits == 4) return a.gated ? launch_decode_b<4, true>(a, s) : launch_decode_b<4, false>(a, s);
+  return a.gated ? launch_decode_b<8, true>(a, s) : launch_decode_b<8, false>(a, s);
+}
+
+cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s) {
+  if (a.rows == 0) return cudaSuccess;
+  const dim3 grid((a.N + 255) / 256, static_cast<unsigned>(a.rows));
+  finalize_fc1_kernel<<<grid, 256, 0, s>>>(a, act);
   return cudaGetLastError();
 }
 
 cudaError_t launch_combine_partials(const float* part, int splits, int64_t rows, const int32_t* pos,
-                                    const float* w, int T, int k, int H, void* out, cudaStream_t s) {
+                                    const float* w, int T, int k, int H, const int32_t* offsets,
+                                    int E, const void* bias, void* out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  combine_partials_kernel<<<T, 256, 0, s>>>(part, splits, rows, pos, w, k, H,
-                                            static_cast<__half*>(out));
+  const dim3 grid((H + 255) / 256, T);
+  combine_partials_kernel<<<grid, 256, 0, s>>>(part, splits, rows, pos, w, k, H, offsets, E,
+                                               static_cast<const __half*>(bias),
+                                               static_cast<__half*>(out));
   return cudaGetLastError();
 }
 

@@ -14,7 +14,9 @@ struct QOperand {
 };
 
 struct QDecodeArgs {
-  const __half* x;            // [rows, K] routed rows in expert order
+  const __half* x;            // activations: [rows, K] in expert order, or the layer input
+  const int32_t* src_rows;    // if set, routed row p reads x row src_rows[p] / k
+  int k;
   int64_t rows;
   int K;
   int N;
@@ -29,8 +31,9 @@ struct QDecodeArgs {
   const void* bias3;
   int bias_stride;
   int64_t bias_e_stride;
-  __half* out;                // [rows, ldo] activation output (fc1), or
-  float* out_partial;         // [splits][rows][ldo] fp32 partial sums (fc2)
+  __half* out;                // [rows, ldo] activation output (fc1 without split), or
+  float* out_partial;         // [splits][rows][ldo] fp32 partial sums without bias
+                              // (gated: gate sums at [0, N), linear sums at [N, 2N))
   int64_t ldo;
   int splits;
 };
@@ -41,7 +44,11 @@ constexpr int kQmoeMaxSplits = 8;
 
 bool qmoe_decode_supported(int dtype, int bits, int block_size, int64_t H, int64_t I);
 cudaError_t launch_qmoe_decode(const QDecodeArgs& a, int max_experts_touched, cudaStream_t s);
+// act = activation(sum of fc1 partials + bias), fp16 [rows, N].
+cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s);
+// out[t] = sum_j w[t,j] * (sum of fc2 partials of row pos[t,j] + fc2 bias of its expert).
 cudaError_t launch_combine_partials(const float* part, int splits, int64_t rows, const int32_t* pos,
-                                    const float* w, int T, int k, int H, void* out, cudaStream_t s);
+                                    const float* w, int T, int k, int H, const int32_t* offsets,
+                                    int E, const void* bias, void* out, cudaStream_t s);
 
 }  // namespace moe

@@ -14,8 +14,66 @@ namespace moe {
 __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 // ------------------------------------------------------------------------ router
-// One warp per row; lane l holds logits l, l+32, ...  Selection compares fp32
-// values, ties to the lower index.  NaN logits are read as -inf.
+// Routes one row with one warp; lane l holds logits l, l+32, ...  Selection compares
+// fp32 values, ties to the lower index; NaN logits are read as -inf.  Lanes r < k
+// receive the r-th selected expert and its weight.
+template <typename T, int kPerLane>
+__device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int k, int normalize,
+                                          int lane, int& my_idx, float& my_w) {
+  float v[kPerLane];
+#pragma unroll
+  for (int j = 0; j < kPerLane; ++j) {
+    const int e = lane + 32 * j;
+    float x = -INFINITY;
+    if (e < E) {
+      x = to_f(row[e]);
+      if (x != x) x = -INFINITY;
+    }
+    v[j] = x;
+  }
+  // Row max and softmax denominator (fixed butterfly order: deterministic).
+  float m = v[0];
+#pragma unroll
+  for (int j = 1; j < kPerLane; ++j) m = fmaxf(m, v[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPerLane; ++j)
+    if (lane + 32 * j < E) s += expf(v[j] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+
+  uint32_t taken = 0;  // bit j: v[j] already selected
+  float top_val = 0.f, sel_sum = 0.f, my_val = 0.f;
+  my_idx = 0;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !(taken & (1u << j)) && (v[j] > bv || (v[j] == bv && e < bi))) {
+        bv = v[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (r == 0) top_val = bv;
+    const float ex = normalize ? expf(bv - top_val) : expf(bv - m);
+    sel_sum += ex;
+    if (lane == r) { my_val = ex; my_idx = bi; }
+  }
+  my_w = normalize ? my_val / sel_sum : my_val / s;
+}
+
+// One warp per row, kRouteChunk rows per CTA; also the CTA's expert histogram.
 template <typename T, int kPerLane>
 __global__ void __launch_bounds__(kRouteThreads)
 route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int normalize,
@@ -30,58 +88,10 @@ route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int norma
   const int row0 = blockIdx.x * kRouteChunk;
   const int row_end = min(row0 + kRouteChunk, num_rows);
   for (int t = row0 + warp; t < row_end; t += kRouteThreads / 32) {
-    float v[kPerLane];
-#pragma unroll
-    for (int j = 0; j < kPerLane; ++j) {
-      const int e = lane + 32 * j;
-      float x = -INFINITY;
-      if (e < E) {
-        x = to_f(logits[static_cast<int64_t>(t) * E + e]);
-        if (x != x) x = -INFINITY;
-      }
-      v[j] = x;
-    }
-    // Row max and softmax denominator (fixed butterfly order: deterministic).
-    float m = v[0];
-#pragma unroll
-    for (int j = 1; j < kPerLane; ++j) m = fmaxf(m, v[j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < kPerLane; ++j)
-      if (lane + 32 * j < E) s += expf(v[j] - m);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-
-    uint32_t taken = 0;  // bit j: v[j] already selected
-    float top_val = 0.f, sel_sum = 0.f, my_val = 0.f;
-    int my_idx = 0;
-    for (int r = 0; r < k; ++r) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int j = 0; j < kPerLane; ++j) {
-        const int e = lane + 32 * j;
-        if (e < E && !(taken & (1u << j)) && (v[j] > bv || (v[j] == bv && e < bi))) {
-          bv = v[j];
-          bi = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      if (r == 0) top_val = bv;
-      const float ex = normalize ? expf(bv - top_val) : expf(bv - m);
-      sel_sum += ex;
-      if (lane == r) { my_val = ex; my_idx = bi; }
-    }
+    int my_idx;
+    float w;
+    route_row<T, kPerLane>(logits + static_cast<int64_t>(t) * E, E, k, normalize, lane, my_idx, w);
     if (lane < k) {
-      const float w = normalize ? my_val / sel_sum : my_val / s;
       expert_idx[static_cast<int64_t>(t) * k + lane] = my_idx;
       route_w[static_cast<int64_t>(t) * k + lane] = w;
       atomicAdd(&s_counts[my_idx], 1);
@@ -90,6 +100,56 @@ route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int norma
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x)
     chunk_counts[static_cast<int64_t>(blockIdx.x) * E + e] = s_counts[e];
+}
+
+// ------------------------------------------------------------- small dispatch
+// Routing and the whole dispatch plan of a small call (T*k <= kSmallDispatchRows) in
+// one CTA: warp-per-row routing, expert counts, exclusive scan, and the stable rank of
+// each routed row within its expert by counting earlier rows of the same expert.
+template <typename T, int kPerLane>
+__global__ void __launch_bounds__(1024)
+small_dispatch_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int normalize,
+                      int32_t* __restrict__ expert_idx, float* __restrict__ route_w,
+                      int32_t* __restrict__ expert_offsets, int32_t* __restrict__ permuted_pos,
+                      int32_t* __restrict__ permuted_src) {
+  __shared__ int32_t s_idx[kSmallDispatchRows];
+  __shared__ int32_t s_cnt[kMaxExperts + 1];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  for (int t = warp; t < num_rows; t += 32) {
+    int my_idx;
+    float w;
+    route_row<T, kPerLane>(logits + static_cast<int64_t>(t) * E, E, k, normalize, lane, my_idx, w);
+    if (lane < k) {
+      expert_idx[t * k + lane] = my_idx;
+      route_w[t * k + lane] = w;
+      s_idx[t * k + lane] = my_idx;
+      atomicAdd(&s_cnt[my_idx], 1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t o = 0;
+    for (int e = 0; e < E; ++e) {
+      const int32_t c = s_cnt[e];
+      s_cnt[e] = o;
+      o += c;
+    }
+    s_cnt[E] = o;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) expert_offsets[e] = s_cnt[e];
+  const int R = num_rows * k;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) {
+    const int e = s_idx[i];
+    int rank = 0;
+    for (int j = 0; j < i; ++j) rank += s_idx[j] == e;
+    const int p = s_cnt[e] + rank;
+    permuted_pos[i] = p;
+    permuted_src[p] = i;
+  }
 }
 
 // ---------------------------------------------------------- histogram (external)
@@ -295,6 +355,35 @@ cudaError_t launch_route(int dtype, const void* logits, int T_, int E, int k, in
     case kDtF32: return launch_route_t<float>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
     case kDtF16: return launch_route_t<__half>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
     case kDtBF16: return launch_route_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T>
+static cudaError_t launch_small_dispatch_t(const void* logits, int T_, int E, int k, int normalize,
+                                           int32_t* idx, float* w, int32_t* offsets, int32_t* pos,
+                                           int32_t* src, cudaStream_t s) {
+  const T* l = static_cast<const T*>(logits);
+  const int per_lane = (E + 31) / 32;
+  if (per_lane <= 1)
+    small_dispatch_kernel<T, 1><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+  else if (per_lane <= 2)
+    small_dispatch_kernel<T, 2><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+  else if (per_lane <= 4)
+    small_dispatch_kernel<T, 4><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+  else
+    small_dispatch_kernel<T, 8><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_small_dispatch(int dtype, const void* logits, int T_, int E, int k,
+                                  int normalize, int32_t* idx, float* w, int32_t* offsets,
+                                  int32_t* pos, int32_t* src, cudaStream_t s) {
+  if (T_ == 0) return cudaSuccess;
+  switch (dtype) {
+    case kDtF32: return launch_small_dispatch_t<float>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s);
+    case kDtF16: return launch_small_dispatch_t<__half>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s);
+    case kDtBF16: return launch_small_dispatch_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s);
   }
   return cudaErrorInvalidValue;
 }
