@@ -38,8 +38,9 @@ namespace {
 
 constexpr int QD_WARPS = 4;
 constexpr int QD_CHUNK = 128;
-// Stages of the per-warp ring: 8 for int4 and 4 for int8, the same bytes in flight.
-template <int BITS> constexpr int qd_stages() { return BITS == 4 ? 8 : 4; }
+// Stages of the per-warp ring: 6 for int4 and 3 for int8 (the same bytes in flight), sized
+// so four CTAs fit on one SM.
+template <int BITS> constexpr int qd_stages() { return BITS == 4 ? 6 : 3; }
 
 enum ScaleMode { kScaleRow = 0, kScaleChunk = 1, kScaleElem = 2 };
 
@@ -69,6 +70,12 @@ __device__ __forceinline__ uint32_t deq4_scaled(uint32_t byte, __half2 s2) {
 __device__ __forceinline__ uint32_t deq4_pair(uint32_t shifted) {
   const uint32_t u = (shifted & 0x000F000Fu) | 0x64006400u;
   return h2_bits(__hsub2(bits_h2(u), h2c(0x6408)));
+}
+// Nibbles i+1 and i+5 of the same shifted word, masked in place: 1024 + 16q, and
+// (1024 + 16q) / 16 - 72 = q - 8, exact in one fused multiply-add.
+__device__ __forceinline__ uint32_t deq4_pair_hi(uint32_t shifted) {
+  const uint32_t u = (shifted & 0x00F000F0u) | 0x64006400u;
+  return h2_bits(__hfma2(bits_h2(u), h2c(0x2C00), h2c(0xD480)));
 }
 // Bytes of a word selected by `sel` -> (b - 128) exact, optionally scaled.
 __device__ __forceinline__ uint32_t deq8(uint32_t word, uint32_t sel) {
@@ -226,7 +233,7 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
             if (BITS == 4 && kScale != kScaleElem) {
               const uint32_t word = w[m] >> (h * 8);  // pairs (0,4),(1,5) or (2,6),(3,7)
               lo = deq4_pair(word);
-              hi = deq4_pair(word >> 4);
+              hi = deq4_pair_hi(word);
             } else if (BITS == 4) {
               const uint32_t word = w[m] >> (h * 16);
               const __half2 s2 = r ? s8[x] : s0[x];
@@ -334,7 +341,7 @@ template <int BITS, bool GATED>
 constexpr int ring_bytes() { return qd_stages<BITS>() * (GATED ? 2 : 1) * 16 * QD_CHUNK * BITS / 8; }
 
 template <int BITS, bool GATED, int kScale>
-__global__ void __launch_bounds__(QD_WARPS * 32) qmoe_decode_kernel(const QDecodeArgs a) {
+__global__ void __launch_bounds__(QD_WARPS * 32, 4) qmoe_decode_kernel(const QDecodeArgs a) {
   extern __shared__ __align__(128) uint8_t s_ring[];  // one ring per warp
   uint8_t* ring = s_ring + (threadIdx.x >> 5) * ring_bytes<BITS, GATED>();
   const int e = blockIdx.y;
@@ -364,7 +371,7 @@ __global__ void __launch_bounds__(QD_WARPS * 32) qmoe_decode_kernel(const QDecod
     return;
   }
   // Up to kMaxGroups groups of 8 routed rows per pass over the weights.
-  constexpr int kMaxGroups = (GATED && (BITS == 8 || kScale == kScaleChunk)) ? 4 : 8;
+  constexpr int kMaxGroups = 4;
   for (int tok0 = 0; tok0 < cnt; tok0 += 8 * kMaxGroups) {
     const int groups = min(kMaxGroups, (cnt - tok0 + 7) / 8);
     if (groups <= 1)
