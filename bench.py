@@ -25,7 +25,9 @@ for config 4 a Zipf(1.1) per-expert logit bias rescaled to [0, 3].
 * ``--impl reference``: the same CPU restatement timed as the reference arm (the
   reference has no MoE kernel and ONNX Runtime is not installable here).
 
-At N > 1 every rank runs the full layer on its own GPU (replicas; weak scaling).
+At N > 1 the layer runs expert-parallel: rank r owns experts [r*E/N, (r+1)*E/N), routes
+its own T tokens and exchanges routed rows with NCCL all-to-alls (weak scaling: T
+tokens per GPU; ``value`` counts the tokens of all ranks).
 """
 
 from __future__ import annotations
@@ -402,6 +404,85 @@ def bench_ours(args, cfg, rank, world, dev):
     return result
 
 
+def bench_ep(args, cfg, rank, world, dev):
+    """Expert-parallel layer over ``world`` ranks (NCCL all-to-all dispatch/combine)."""
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    from onnxruntime_musa_b200 import ep
+    L = make_layer(cfg, dev, 20261202)          # the same weights on every rank
+    g = torch.Generator(device=dev).manual_seed(7000 + rank)
+    T, H, E = cfg["T"], cfg["H"], cfg["E"]
+    L["x"] = torch.randn(T, H, device=dev, generator=g).to(L["x"].dtype)
+    L["router_probs"] = torch.randn(T, E, device=dev, generator=g).to(L["router_probs"].dtype)
+    out = torch.empty_like(L["x"])
+    prob, tens, inputs, op_attrs, op_type = problem_and_tensors(pkg, cfg, L, out)
+    names = ["fc1_weights", "fc1_scales", "fc1_bias", "fc2_weights", "fc2_scales", "fc2_bias",
+             "fc3_weights", "fc3_scales", "fc3_bias"]
+    local = ep.shard_experts({n: tens.get(n) for n in names}, rank, world)
+    layer = ep.ExpertParallelMoE(pkg, num_experts=E, hidden_size=H, inter_size=cfg["I"],
+                                 dtype=prob.dtype, has_fc3=bool(prob.has_fc3),
+                                 local_weights=local, **op_attrs)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(step):
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    x, lg = L["x"], L["router_probs"]
+    with ClockSampler(dev.index) as clk:
+        ms = timed(lambda: layer.forward(x, lg))
+    hx, hl = x.cpu().pin_memory(), lg.cpu().pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    dx, dl = torch.empty_like(x), torch.empty_like(lg)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        hout.copy_(layer.forward(dx, dl), non_blocking=True)
+
+    e2e_ms = timed(e2e_step)
+    pk = peaks()
+    alg = algorithmic(cfg, L, pkg)
+    es = hx.element_size()
+    achieved = alg["flops"] / (ms / 1e3) / 1e12
+    return {
+        "metric": METRIC, "value": round(world * T / (ms / 1e3), 1), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if cfg.get("dtype") == "float32" else "f16",
+        "data": "synthetic (seeded, on-device; config distributions; random init)",
+        "config": {"workload": cfg["desc"].format(T=T), "global_batch": T * world,
+                   "tokens_per_gpu": T, "parallelism": f"ep{world}",
+                   "l2": "inputs larger than L2 (weights streamed every step)"},
+        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": hx.numel() * es + hl.numel() * es,
+                "d2h_bytes_per_step": hout.numel() * es},
+        "roofline": {"bound": "tensor", "kernel": "expert-parallel layer (all stages, per rank)",
+                     "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
+                     "frac": round(achieved / pk["tflops"], 4), "traffic": None,
+                     "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)"},
+        # dispatch (route, scan, permute, gather) + expert FFN (fill, histogram, scan,
+        # permute, gather, fc1, fc2, un-permute) + combine
+        "gpu_launches": 13 * args.steps,
+        "clocks": clk.summary(),
+    }
+
+
 def bench_reference(args, cfg, rank, world):
     """Reference arm: the CPU restatement of the path on this host's cores."""
     import torch
@@ -458,7 +539,8 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=dev)
     for T in sweep:
-        res = bench_ours(args, dict(base, T=T), rank, world, dev)
+        run = bench_ours if world == 1 else bench_ep
+        res = run(args, dict(base, T=T), rank, world, dev)
         if rank == 0:
             print(json.dumps(res), flush=True)
     if world > 1:

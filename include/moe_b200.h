@@ -160,6 +160,30 @@ int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tenso
                            void* workspace, size_t workspace_bytes, void* stream,
                            float* stage_ms, int32_t num_stages);
 
+/* ---------------------------------------------------- expert parallelism */
+/* Expert parallelism splits one layer over W ranks, rank r owning the experts
+ * [r*E/W, (r+1)*E/W).  No counterpart in the reference (one EP drives one device,
+ * musa/ep/src/ep_factory.cc:466-470); these three calls are the device side of the
+ * exchange, the transport (an NCCL all-to-all) sits between them:
+ *   1. moe_b200_ep_dispatch on every rank: route its T rows over all E experts and
+ *      gather the T*k routed rows into send_rows in expert order, so the rows for rank
+ *      r are the contiguous block [expert_offsets[r*E/W], expert_offsets[(r+1)*E/W]);
+ *   2. exchange counts and rows; each rank runs moe_b200_expert_ffn on what it received
+ *      (problem: its E/W experts, k = 1, num_rows = received rows; row_expert = local
+ *      expert id of each row; router_probs unused; output row i = FFN of row i);
+ *   3. send the FFN rows back in the same layout; moe_b200_ep_combine forms
+ *      out[t] = sum_j w[t,j] * rows[permuted_pos[t,j]]. */
+int moe_b200_ep_dispatch(const moe_b200_problem* problem, const void* router_probs,
+                         const void* input, void* send_rows, int32_t* expert_offsets,
+                         int32_t* permuted_pos, float* route_weight, void* workspace,
+                         size_t workspace_bytes, void* stream);
+int moe_b200_expert_ffn(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                        const int32_t* row_expert, void* workspace, size_t workspace_bytes,
+                        void* stream);
+int moe_b200_ep_combine(int32_t dtype, int64_t num_rows, int64_t hidden_size, int32_t k,
+                        const void* expert_rows, const int32_t* permuted_pos,
+                        const float* route_weight, void* output, void* stream);
+
 /* ------------------------------------------------------ hot-path stages */
 
 /* Router: softmax + top-k (+ renormalisation) of every row of router_probs

@@ -112,6 +112,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                         _SZ, _VP]),
     "moe_b200_forward_timed": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                               _VP, _SZ, _VP, _PF, _I32]),
+    "moe_b200_ep_dispatch": (ctypes.c_int, [ctypes.POINTER(Problem), _VP, _VP, _VP, _VP, _VP,
+                                            _VP, _VP, _SZ, _VP]),
+    "moe_b200_expert_ffn": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors), _VP,
+                                           _VP, _SZ, _VP]),
+    "moe_b200_ep_combine": (ctypes.c_int, [_I32, _I64, _I64, _I32, _VP, _VP, _VP, _VP, _VP]),
     "moe_b200_route": (ctypes.c_int, [_VP, _I32, _I64, _I64, _I32, _I32, _VP, _VP, _VP]),
     "moe_b200_route_noalloc": (ctypes.c_int, [_VP, _I32, _I64, _I64, _I32, _I32, _VP, _VP, _VP]),
     "moe_b200_permute_workspace_size": (_SZ, [_I64, _I32, _I64]),
@@ -362,6 +367,58 @@ def forward(problem: Problem, tensors: Mapping[str, Any], workspace, stream=None
     check(lib().moe_b200_forward(ctypes.byref(problem), ctypes.byref(t),
                                  workspace.data_ptr(), workspace.numel(),
                                  _stream_handle(stream)))
+
+
+def _tensors_struct(tensors: Mapping[str, Any]) -> Tensors:
+    t = Tensors()
+    for name, _ in Tensors._fields_:
+        v = tensors.get(name)
+        setattr(t, name, None if v is None else (v if isinstance(v, int) else v.data_ptr()))
+    return t
+
+
+def ep_dispatch(problem: Problem, router_probs, x, stream=None):
+    """Expert-parallel step 1: route all rows over all experts and gather the routed rows
+    in expert order.  Returns (send_rows [T*k, H], expert_offsets [E+1], permuted_pos
+    [T, k], route_weight [T, k])."""
+    torch = _torch()
+    T, H = x.shape
+    k, E = problem.attrs.k, problem.num_experts
+    dev = x.device
+    send = torch.empty((T * k, H), dtype=x.dtype, device=dev)
+    offs = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    pos = torch.empty((T, k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, k), dtype=torch.float32, device=dev)
+    ws = torch.empty(workspace_size(problem), dtype=torch.uint8, device=dev)
+    check(lib().moe_b200_ep_dispatch(ctypes.byref(problem), router_probs.data_ptr(), x.data_ptr(),
+                                     send.data_ptr(), offs.data_ptr(), pos.data_ptr(),
+                                     w.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     _stream_handle(stream)))
+    return send, offs, pos, w
+
+
+def expert_ffn(problem: Problem, tensors: Mapping[str, Any], row_expert, stream=None) -> None:
+    """Expert-parallel step 2: the expert FFN of rows whose (local) expert is given
+    (``problem`` with k=1 and the local experts; ``tensors['output']`` receives one
+    row per input row)."""
+    torch = _torch()
+    dev = tensors["input"].device
+    ws = torch.empty(workspace_size(problem), dtype=torch.uint8, device=dev)
+    t = _tensors_struct(tensors)
+    check(lib().moe_b200_expert_ffn(ctypes.byref(problem), ctypes.byref(t),
+                                    row_expert.data_ptr() if row_expert.numel() else None,
+                                    ws.data_ptr(), ws.numel(), _stream_handle(stream)))
+
+
+def ep_combine(expert_rows, permuted_pos, route_weight, out, stream=None):
+    """Expert-parallel step 3: out[t] = sum_j w[t,j] * expert_rows[permuted_pos[t,j]]."""
+    T, k = permuted_pos.shape
+    check(lib().moe_b200_ep_combine(elem_type_of(out), T, out.shape[-1], k,
+                                    expert_rows.data_ptr() if expert_rows.numel() else None,
+                                    permuted_pos.data_ptr() if T else None,
+                                    route_weight.data_ptr() if T else None,
+                                    out.data_ptr() if T else None, _stream_handle(stream)))
+    return out
 
 
 STAGES = ("route", "plan", "gather", "dequant", "fc1", "fc2", "combine")

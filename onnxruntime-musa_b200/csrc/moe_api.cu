@@ -251,8 +251,13 @@ cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
 // Stage boundaries recorded when `ev` is non-NULL (kNumStages + 1 events).
 enum Stage { kStRoute = 0, kStPlan, kStGather, kStDequant, kStFc1, kStFc2, kStCombine, kNumStages };
 
+// One layer call.  With `given_idx` (k == 1) the routing is supplied by the caller: rows
+// of `input` are already assigned to experts (expert parallelism: the rows a rank
+// received), every routing weight is 1, and the output row i is expert(row i)'s FFN
+// output; router_probs is not read.
 int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
-                 size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev = nullptr) {
+                 size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev = nullptr,
+                 const int32_t* given_idx = nullptr) {
   auto mark = [&](int i) { if (ev) cudaEventRecord(ev[i], s); };
   const WsLayout L = plan_workspace(p);
   if (ws_bytes < L.total)
@@ -262,8 +267,11 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
     return fail(MOE_B200_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
   if (t.fc1_weights == nullptr || t.fc2_weights == nullptr)
     return fail(MOE_B200_INVALID_ARGUMENT, "fc1/fc2 weights must be non-NULL");
-  if (p.num_rows > 0 && (t.input == nullptr || t.router_probs == nullptr || t.output == nullptr))
+  if (p.num_rows > 0 && (t.input == nullptr || t.output == nullptr ||
+                         (t.router_probs == nullptr && given_idx == nullptr)))
     return fail(MOE_B200_INVALID_ARGUMENT, "input, router_probs and output must be non-NULL");
+  if (given_idx != nullptr && p.attrs.k != 1)
+    return fail(MOE_B200_INVALID_ARGUMENT, "rows with given experts need k == 1");
   if (p.has_fc3 && t.fc3_weights == nullptr)
     return fail(MOE_B200_INVALID_ARGUMENT, "has_fc3 is set but fc3_weights is NULL");
   const int T = static_cast<int>(p.num_rows);
@@ -290,7 +298,30 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
 
   MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, sizeof(int), s), "clear error word");
   const size_t es = dtype_bytes(p.dtype);
-  if (qmoe_use_decode(p)) {
+  if (given_idx != nullptr) {
+    // Supplied routing: unit weights, histogram and plan of the given expert ids.
+    mark(kStRoute);
+    MOE_CUDA_CHECK(launch_fill_f32(w, 1.0f, R, s), "unit weights");
+    MOE_CUDA_CHECK(launch_histogram(given_idx, T, 1, E, cc, err, s), "histogram");
+    mark(kStPlan);
+    MOE_CUDA_CHECK(launch_plan(given_idx, T, 1, E, cc, cb, offs, t128, t64, t256, pos, src, s),
+                   "plan");
+    if (qmoe_use_decode(p)) {
+      mark(kStGather);
+      mark(kStDequant);
+      mark(kStFc1);
+      int st = qmoe_decode_fc1(p, t, src, act, offs, ws + L.qmoe, s);
+      if (st != MOE_B200_OK) return st;
+      mark(kStFc2);
+      st = qmoe_decode_fc2(p, t, act, offs, ws + L.qmoe, s);
+      if (st != MOE_B200_OK) return st;
+      mark(kStCombine);
+      st = qmoe_decode_combine(p, t, ws + L.qmoe, offs, pos, w, s);
+      if (st != MOE_B200_OK) return st;
+      mark(kNumStages);
+      return MOE_B200_OK;
+    }
+  } else if (qmoe_use_decode(p)) {
     // Decode-sized QMoE: one CTA routes and plans, then the packed weights of the
     // touched experts are streamed once (token rows are read in place: no gather).
     mark(kStRoute);
@@ -313,12 +344,14 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
     mark(kNumStages);
     return MOE_B200_OK;
   }
-  mark(kStRoute);
-  MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
-                              p.attrs.normalize_routing_weights, idx, w, cc, s),
-                 "route");
-  mark(kStPlan);
-  MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s), "plan");
+  if (given_idx == nullptr) {
+    mark(kStRoute);
+    MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
+                                p.attrs.normalize_routing_weights, idx, w, cc, s),
+                   "route");
+    mark(kStPlan);
+    MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s), "plan");
+  }
   mark(kStGather);
   MOE_CUDA_CHECK(launch_gather(t.input, static_cast<int64_t>(H) * es, k, src, R, xp, s),
                  "gather");
@@ -424,6 +457,73 @@ int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tenso
   }
   for (int i = 0; i <= kNumStages; ++i) cudaEventDestroy(ev[i]);
   return st;
+}
+
+int moe_b200_ep_dispatch(const moe_b200_problem* problem, const void* router_probs,
+                         const void* input, void* send_rows, int32_t* expert_offsets,
+                         int32_t* permuted_pos, float* route_weight, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  const moe_b200_problem& p = *problem;
+  const WsLayout L = plan_workspace(p);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+    return fail(MOE_B200_INVALID_ARGUMENT, "workspace must be 256-byte aligned and >= %zu bytes",
+                L.total);
+  if (expert_offsets == nullptr || (p.num_rows > 0 && (router_probs == nullptr || input == nullptr ||
+                                                       send_rows == nullptr ||
+                                                       permuted_pos == nullptr ||
+                                                       route_weight == nullptr)))
+    return fail(MOE_B200_INVALID_ARGUMENT, "ep_dispatch: NULL buffer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int T = static_cast<int>(p.num_rows), E = static_cast<int>(p.num_experts), k = p.attrs.k;
+  if (T == 0) {
+    MOE_CUDA_CHECK(cudaMemsetAsync(expert_offsets, 0, (E + 1) * sizeof(int32_t), s), "offsets");
+    return MOE_B200_OK;
+  }
+  auto* idx = reinterpret_cast<int32_t*>(ws + L.idx);
+  auto* cc = reinterpret_cast<int32_t*>(ws + L.chunk_counts);
+  auto* cb = reinterpret_cast<int32_t*>(ws + L.chunk_base);
+  auto* t128 = reinterpret_cast<int32_t*>(ws + L.tiles128);
+  auto* t64 = reinterpret_cast<int32_t*>(ws + L.tiles64);
+  auto* t256 = reinterpret_cast<int32_t*>(ws + L.tiles256);
+  auto* src = reinterpret_cast<int32_t*>(ws + L.src);
+  MOE_CUDA_CHECK(launch_route(p.dtype, router_probs, T, E, k, p.attrs.normalize_routing_weights,
+                              idx, route_weight, cc, s),
+                 "route");
+  MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, expert_offsets, t128, t64, t256, permuted_pos,
+                             src, s),
+                 "plan");
+  MOE_CUDA_CHECK(launch_gather(input, static_cast<int64_t>(p.hidden_size) * dtype_bytes(p.dtype),
+                               k, src, static_cast<int64_t>(T) * k, send_rows, s),
+                 "gather");
+  return MOE_B200_OK;
+}
+
+int moe_b200_expert_ffn(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                        const int32_t* row_expert, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  if (t == nullptr || (problem->num_rows > 0 && row_expert == nullptr))
+    return fail(MOE_B200_INVALID_ARGUMENT, "expert_ffn: NULL tensors or row_expert");
+  return forward_impl(*problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes,
+                      static_cast<cudaStream_t>(stream), nullptr, row_expert);
+}
+
+int moe_b200_ep_combine(int32_t dtype, int64_t num_rows, int64_t hidden_size, int32_t k,
+                        const void* expert_rows, const int32_t* permuted_pos,
+                        const float* route_weight, void* output, void* stream) {
+  if (!is_float_type(dtype)) return fail(MOE_B200_NOT_IMPLEMENTED, "unsupported dtype %d", dtype);
+  if (num_rows < 0 || hidden_size <= 0 || k < 1)
+    return fail(MOE_B200_INVALID_ARGUMENT, "ep_combine: invalid shape");
+  if (num_rows == 0) return MOE_B200_OK;
+  MOE_CUDA_CHECK(launch_combine(dtype, expert_rows, permuted_pos, route_weight,
+                                static_cast<int>(num_rows), k, static_cast<int>(hidden_size),
+                                output, static_cast<cudaStream_t>(stream)),
+                 "combine");
+  return MOE_B200_OK;
 }
 
 int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,

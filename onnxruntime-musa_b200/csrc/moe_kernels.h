@@ -44,6 +44,7 @@ cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* 
                         cudaStream_t s);
 cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
                           int64_t rows, void* xp, cudaStream_t s);
+cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s);
 cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
                            int T, int k, int H, void* out, cudaStream_t s);
 

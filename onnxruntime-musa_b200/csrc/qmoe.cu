@@ -109,7 +109,11 @@ int64_t fc1_rows(const moe_b200_problem& p) {
 bool qmoe_use_decode(const moe_b200_problem& p) {
   if (p.attrs.expert_weight_bits == 0) return false;
   if (std::getenv("MOE_B200_QMOE_NO_DECODE") != nullptr) return false;
-  return p.num_rows * p.attrs.k <= kQmoeDecodeMaxRows &&
+  // MOE_B200_QMOE_DECODE_MAX_ROWS moves the switch-over point (for measurement).
+  int64_t max_rows = kQmoeDecodeMaxRows;
+  if (const char* v = std::getenv("MOE_B200_QMOE_DECODE_MAX_ROWS")) max_rows = std::atoll(v);
+  max_rows = std::min<int64_t>(max_rows, kSmallDispatchRows);
+  return p.num_rows * p.attrs.k <= max_rows &&
          qmoe_decode_supported(p.dtype, p.attrs.expert_weight_bits, p.attrs.block_size,
                                p.hidden_size, p.inter_size);
 }

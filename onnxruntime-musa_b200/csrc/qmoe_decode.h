@@ -39,7 +39,7 @@ struct QDecodeArgs {
 };
 
 // Rows of T*k up to which the decode kernels replace dequantise + tensor-core GEMM.
-constexpr int64_t kQmoeDecodeMaxRows = 128;
+constexpr int64_t kQmoeDecodeMaxRows = 512;
 constexpr int kQmoeMaxSplits = 8;
 
 bool qmoe_decode_supported(int dtype, int bits, int block_size, int64_t H, int64_t I);

@@ -7,6 +7,8 @@
 //   top-k    musa/ep/src/kernels/math/topk_impl.mu:46-65 (ties -> lower index)
 //   scan     musa/ep/src/kernels/math/cumsum_impl.mu:17 (replaced by a two-level scan)
 //   gather   musa/ep/src/kernels/tensor/gather_impl.mu:18
+#include <algorithm>
+
 #include "moe_kernels.h"
 
 namespace moe {
@@ -328,7 +330,20 @@ combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ permuted_pos
   }
 }
 
+__global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = v;
+}
+
 // ------------------------------------------------------------------ launchers
+cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 1184));
+  fill_f32_kernel<<<blocks, 256, 0, s>>>(dst, value, n);
+  return cudaGetLastError();
+}
+
 template <typename T>
 static cudaError_t launch_route_t(const void* logits, int T_, int E, int k, int normalize,
                                   int32_t* idx, float* w, int32_t* chunk_counts,

@@ -1,0 +1,120 @@
+"""Expert parallelism for the MoE / QMoE layer: one process per GPU, experts sharded.
+
+Rank r of W owns experts [r*E/W, (r+1)*E/W) and routes its own T tokens (data-parallel
+routing).  One layer call:
+
+  1. dispatch  (device)  route over all E experts, gather routed rows in expert order:
+                         the rows for rank d form one contiguous block of ``send``;
+  2. counts    (NCCL)    all-to-all of the per-expert row counts, [W, E/W] ints;
+  3. rows      (NCCL)    all-to-all of the routed rows (variable split sizes);
+  4. experts   (device)  expert FFN of the received rows, each with its local expert id
+                         (rows arrive grouped by source, then by expert);
+  5. rows back (NCCL)    all-to-all of the FFN rows along the reverse splits;
+  6. combine   (device)  out[t] = sum_j w[t,j] * rows[pos[t,j]].
+
+The reference plugin has no parallelism at all (one EP instance drives one device,
+``musa/ep/src/ep_factory.cc:466-470``); the design follows the plan for the MoE path:
+the split sizes of the variable all-to-all need the counts on the host, which costs one
+small device-to-host copy per layer call.
+
+The device steps go through a backend object so the exchange logic can be tested on CPU
+ranks (gloo) with a NumPy backend; :class:`CudaBackend` is the product path.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+
+class CudaBackend:
+    """Device steps through the C ABI of libmoe_b200."""
+
+    def __init__(self, pkg):
+        self.pkg = pkg
+
+    def dispatch(self, problem, x, router_probs):
+        return self.pkg.ep_dispatch(problem, router_probs, x)
+
+    def expert_ffn(self, problem, rows, row_expert, weights):
+        out = torch.empty_like(rows)
+        tensors = dict(weights, input=rows, output=out)
+        self.pkg.expert_ffn(problem, tensors, row_expert)
+        return out
+
+    def combine(self, rows, pos, w, out):
+        return self.pkg.ep_combine(rows, pos, w, out)
+
+
+class ExpertParallelMoE:
+    """One MoE (or QMoE) layer sharded by expert over the ranks of ``group``.
+
+    ``local_weights`` holds this rank's experts only (leading dimension E/W) under the
+    names of :class:`Tensors` fields (fc1_weights, fc1_scales, fc1_bias, ...).
+    ``attrs`` are the node attributes (activation_type, k, normalize_routing_weights,
+    expert_weight_bits, block_size, ...).
+    """
+
+    def __init__(self, pkg, *, num_experts: int, hidden_size: int, inter_size: int,
+                 dtype: int, has_fc3: bool, local_weights: dict[str, Any], group=None,
+                 backend=None, **attrs):
+        self.pkg = pkg
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if num_experts % self.world:
+            raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
+        self.E, self.H, self.I = num_experts, hidden_size, inter_size
+        self.E_local = num_experts // self.world
+        self.dtype, self.has_fc3 = dtype, has_fc3
+        self.attrs = dict(attrs)
+        self.k = int(attrs.get("k", 1))
+        self.weights = local_weights
+        self.backend = backend if backend is not None else CudaBackend(pkg)
+
+    def _problem(self, rows: int, experts: int, k: int):
+        a = dict(self.attrs, k=k)
+        return self.pkg.make_problem(rows, self.H, self.I, experts, self.dtype,
+                                     has_fc3=self.has_fc3, **a)
+
+    def _a2a(self, out, inp, out_splits=None, in_splits=None):
+        if self.world == 1:
+            out.copy_(inp)
+            return out
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        return out
+
+    def forward(self, x, router_probs):
+        """x [T, H], router_probs [T, E] -> output [T, H] for this rank's tokens."""
+        T = x.shape[0]
+        W, El = self.world, self.E_local
+        send, offsets, pos, w = self.backend.dispatch(self._problem(T, self.E, self.k), x,
+                                                     router_probs)
+        counts = (offsets[1:] - offsets[:-1]).to(torch.int64).view(W, El)
+        recv_counts = self._a2a(torch.empty_like(counts).view(-1), counts.reshape(-1)).view(W, El)
+        send_splits = counts.sum(1).tolist()          # the one host round trip per call
+        recv_splits = recv_counts.sum(1).tolist()
+        recv = send.new_empty((sum(recv_splits), self.H))
+        self._a2a(recv, send, recv_splits, send_splits)
+        local_ids = torch.arange(El, device=recv.device, dtype=torch.int32).repeat(W)
+        row_expert = torch.repeat_interleave(local_ids, recv_counts.reshape(-1).to(recv.device))
+        y_recv = self.backend.expert_ffn(self._problem(recv.shape[0], El, 1), recv,
+                                         row_expert.to(torch.int32).contiguous(), self.weights)
+        y_send = torch.empty_like(send)
+        self._a2a(y_send, y_recv, send_splits, recv_splits)
+        out = torch.empty_like(x)
+        return self.backend.combine(y_send, pos, w, out)
+
+
+def shard_experts(tensors: dict[str, Any], rank: int, world: int) -> dict[str, Any]:
+    """The slice of each per-expert tensor (leading dimension E) owned by ``rank``."""
+    out = {}
+    for name, t in tensors.items():
+        if t is None:
+            out[name] = None
+            continue
+        el = t.shape[0] // world
+        out[name] = t[rank * el:(rank + 1) * el].contiguous()
+    return out

@@ -160,6 +160,44 @@ def _act(name, x, alpha=1.0, beta=0.0, limit=math.inf, lin=None):
     raise ValueError(f"unknown activation_type {name!r}")
 
 
+def expert_ffn(xe, W1, b1, W2, b2, W3=None, b3=None, *, activation_type="relu",
+               swiglu_fusion=0, activation_alpha=1.0, activation_beta=0.0,
+               swiglu_limit=math.inf):
+    """float64 FFN of one expert on rows ``xe`` [M, H]; W* are that expert's [N, K]
+    matrices and b* its bias vectors (or None)."""
+    xe = np.asarray(xe).astype(np.float64)
+    f64 = lambda a: None if a is None else np.asarray(a).astype(np.float64)
+    W1, W2, W3, b1, b2, b3 = map(f64, (W1, W2, W3, b1, b2, b3))
+    h = xe @ W1.T
+    if b1 is not None:
+        h = h + b1
+    if activation_type == "swiglu":
+        if W3 is not None and swiglu_fusion == 0:
+            u = xe @ W3.T
+            if b3 is not None:
+                u = u + b3
+            g = h
+        elif swiglu_fusion == 1:
+            g, u = h[:, 0::2], h[:, 1::2]
+        elif swiglu_fusion == 2:
+            half = h.shape[1] // 2
+            g, u = h[:, :half], h[:, half:]
+        else:
+            raise ValueError("swiglu needs fc3 weights or swiglu_fusion 1/2")
+        a = _act("swiglu", g, activation_alpha, activation_beta, swiglu_limit, u)
+    else:
+        a = _act(activation_type, h)
+        if W3 is not None:
+            u = xe @ W3.T
+            if b3 is not None:
+                u = u + b3
+            a = a * u
+    y = a @ W2.T
+    if b2 is not None:
+        y = y + b2
+    return y
+
+
 def moe(x, router_probs, fc1_w, fc1_b, fc2_w, fc2_b, fc3_w=None, fc3_b=None, *,
         activation_type="relu", k=1, normalize_routing_weights=0, swiglu_fusion=0,
         activation_alpha=1.0, activation_beta=0.0, swiglu_limit=math.inf,
@@ -173,41 +211,15 @@ def moe(x, router_probs, fc1_w, fc1_b, fc2_w, fc2_b, fc3_w=None, fc3_b=None, *,
     E = fc1_w.shape[0]
     idx, w = route(np.asarray(router_probs).reshape(T, E), k, normalize_routing_weights)
     out = np.zeros((T, H), dtype=np.float64)
-    W1 = np.asarray(fc1_w).astype(np.float64)
-    W2 = np.asarray(fc2_w).astype(np.float64)
-    W3 = None if fc3_w is None else np.asarray(fc3_w).astype(np.float64)
+    sel = lambda a, e: None if a is None else np.asarray(a)[e]
     for e in range(E):
         tok, slot = np.nonzero(idx == e)
         if tok.size == 0:
             continue
-        xe = X[tok]
-        h = xe @ W1[e].T
-        if fc1_b is not None:
-            h = h + np.asarray(fc1_b)[e].astype(np.float64)
-        if activation_type == "swiglu":
-            if W3 is not None and swiglu_fusion == 0:
-                u = xe @ W3[e].T
-                if fc3_b is not None:
-                    u = u + np.asarray(fc3_b)[e].astype(np.float64)
-                g = h
-            elif swiglu_fusion == 1:
-                g, u = h[:, 0::2], h[:, 1::2]
-            elif swiglu_fusion == 2:
-                half = h.shape[1] // 2
-                g, u = h[:, :half], h[:, half:]
-            else:
-                raise ValueError("swiglu needs fc3 weights or swiglu_fusion 1/2")
-            a = _act("swiglu", g, activation_alpha, activation_beta, swiglu_limit, u)
-        else:
-            a = _act(activation_type, h)
-            if W3 is not None:
-                u = xe @ W3[e].T
-                if fc3_b is not None:
-                    u = u + np.asarray(fc3_b)[e].astype(np.float64)
-                a = a * u
-        y = a @ W2[e].T
-        if fc2_b is not None:
-            y = y + np.asarray(fc2_b)[e].astype(np.float64)
+        y = expert_ffn(X[tok], sel(fc1_w, e), sel(fc1_b, e), sel(fc2_w, e), sel(fc2_b, e),
+                       sel(fc3_w, e), sel(fc3_b, e), activation_type=activation_type,
+                       swiglu_fusion=swiglu_fusion, activation_alpha=activation_alpha,
+                       activation_beta=activation_beta, swiglu_limit=swiglu_limit)
         out[tok] += w[tok, slot].astype(np.float64)[:, None] * y
     out = out.reshape(shape)
     if return_routing:

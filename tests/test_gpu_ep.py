@@ -1,0 +1,115 @@
+"""GPU tests of the expert-parallel path through the C ABI (dispatch, expert FFN on
+received rows, combine), single process and, where two GPUs exist, two NCCL ranks."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from gpu_util import TOL, as_np, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _moe_case(orc, dev, T, H, I, E, k, seed, dtype):
+    import torch
+    inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act="silu", gated=True, dtype="float32",
+                              bias=True, normalize=1, seed=seed)
+    dt = getattr(torch, dtype)
+    d = {n: to_dev(inp[n], dev, dt) for n in ("x", "router_probs", "fc1_w", "fc1_b", "fc2_w",
+                                                "fc2_b", "fc3_w", "fc3_b")}
+    weights = dict(fc1_weights=d["fc1_w"], fc1_bias=d["fc1_b"], fc2_weights=d["fc2_w"],
+                   fc2_bias=d["fc2_b"], fc3_weights=d["fc3_w"], fc3_bias=d["fc3_b"])
+    return d, weights, inp["attrs"]
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+def test_ep_single_rank_matches_layer(pkg, orc, dev, dtype):
+    from onnxruntime_musa_b200 import ep
+    d, weights, attrs = _moe_case(orc, dev, 300, 256, 384, 8, 2, 21, dtype)
+    et = {"float16": pkg.FLOAT16, "bfloat16": pkg.BFLOAT16, "float32": pkg.FLOAT}[dtype]
+    layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=256, inter_size=384, dtype=et,
+                                 has_fc3=True, local_weights=weights, **attrs)
+    out = layer.forward(d["x"], d["router_probs"])
+    op = pkg.MoE(**attrs)
+    ref = op([d["x"], d["router_probs"], d["fc1_w"], d["fc1_b"], d["fc2_w"], d["fc2_b"],
+              d["fc3_w"], d["fc3_b"]])
+    op.release()
+    np.testing.assert_allclose(as_np(out), as_np(ref), **TOL[dtype])
+
+
+@pytest.mark.parametrize("T", [4, 400])  # decode kernels and dequantise + GEMM
+def test_ep_single_rank_qmoe(pkg, orc, dev, T):
+    from onnxruntime_musa_b200 import ep
+    q = orc.make_qmoe_inputs(T=T, H=256, I=256, E=8, k=2, bits=4, block_size=128,
+                             scale_mu=-5.0, scale_sigma=0.3, seed=T)
+    g = lambda n: to_dev(q[n], dev)
+    attrs = q["attrs"]
+    weights = dict(fc1_weights=g("fc1_q"), fc1_scales=g("fc1_scales"), fc2_weights=g("fc2_q"),
+                   fc2_scales=g("fc2_scales"), fc3_weights=g("fc3_q"), fc3_scales=g("fc3_scales"))
+    layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=256, inter_size=256,
+                                 dtype=pkg.FLOAT16, has_fc3=True, local_weights=weights, **attrs)
+    out = layer.forward(g("x"), g("router_probs"))
+    ref = orc.qmoe(q["x"], q["router_probs"], q["fc1_q"], q["fc1_scales"], None, q["fc2_q"],
+                   q["fc2_scales"], None, q["fc3_q"], q["fc3_scales"], None, **attrs)
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _nccl_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=__import__("datetime").timedelta(seconds=120))
+    try:
+        pkg, orc = ge.load_package(), ge.load_oracle()
+        from onnxruntime_musa_b200 import ep
+        d, weights, attrs = _moe_case(orc, dev, 512, 512, 256, 8, 2, 33, "float16")
+        T_r = 256
+        xs, ls = d["x"][rank * T_r:(rank + 1) * T_r], d["router_probs"][rank * T_r:(rank + 1) * T_r]
+        layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=512, inter_size=256,
+                                     dtype=pkg.FLOAT16, has_fc3=True,
+                                     local_weights=ep.shard_experts(weights, rank, world), **attrs)
+        out = layer.forward(xs.contiguous(), ls.contiguous())
+        op = pkg.MoE(**attrs)
+        ref = op([xs.contiguous(), ls.contiguous(), d["fc1_w"], d["fc1_b"], d["fc2_w"],
+                  d["fc2_b"], d["fc3_w"], d["fc3_b"]])
+        torch.cuda.synchronize()
+        err = np.abs(as_np(out) - as_np(ref)) - (TOL["float16"]["atol"] +
+                                                 TOL["float16"]["rtol"] * np.abs(as_np(ref)))
+        q.put((rank, float(err.max())))
+    except Exception as exc:
+        q.put((rank, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_two_ranks_nccl():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+        assert res[r] <= 0, f"rank {r} exceeds the fp16 tolerance by {res[r]}"
