@@ -248,6 +248,16 @@ cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
   return launch_gemm_simt(g, s);
 }
 
+// Marks a GEMM pass's B operands as packed QMoE codes with their scales.  For a fused
+// swiglu fc1 both operands share fc1's scales (same stored-row addressing as the codes).
+void set_quantized(const moe_b200_problem& p, GemmArgs& g, const void* scales_a,
+                   const void* scales_b) {
+  g.qbits = p.attrs.expert_weight_bits;
+  g.qblock = p.attrs.block_size;
+  g.b1.scales = scales_a;
+  if (g.gated) g.b3.scales = scales_b != nullptr ? scales_b : scales_a;
+}
+
 // Stage boundaries recorded when `ev` is non-NULL (kNumStages + 1 events).
 enum Stage { kStRoute = 0, kStPlan, kStGather, kStDequant, kStFc1, kStFc2, kStCombine, kNumStages };
 
@@ -360,7 +370,8 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   const void* w2 = t.fc2_weights;
   const void* w3 = t.fc3_weights;
   mark(kStDequant);
-  if (p.attrs.expert_weight_bits != 0) {
+  const bool fused_q = qmoe_use_fused(p);
+  if (p.attrs.expert_weight_bits != 0 && !fused_q) {
     // QMoE prefill: dequantise the weights of every expert into the workspace, then run
     // the same grouped GEMMs.
     QmoeDequantOut dq;
@@ -381,8 +392,15 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g1.out = act;
   g1.ldo = I;
   g1.err = err;
+  if (fused_q) set_quantized(p, g1, t.fc1_scales, t.fc3_scales);
   mark(kStFc1);
-  MOE_CUDA_CHECK(run_gemm(g1, s), "fc1 grouped GEMM");
+  if (fused_q) {
+    if (!tc_q_supported(g1))
+      return fail(MOE_B200_NOT_IMPLEMENTED, "QMoE fc1: operands not 16-byte aligned");
+    MOE_CUDA_CHECK(launch_gemm_tc_q(g1, device_sm_count(), s), "fc1 grouped GEMM (packed)");
+  } else {
+    MOE_CUDA_CHECK(run_gemm(g1, s), "fc1 grouped GEMM");
+  }
 
   GemmArgs g2 = fc2_args(p, w2, t.fc2_bias);
   g2.a = act;
@@ -394,8 +412,15 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g2.out = xp;  // Y aliases the gathered input, dead after fc1
   g2.ldo = H;
   g2.err = err;
+  if (fused_q) set_quantized(p, g2, t.fc2_scales, nullptr);
   mark(kStFc2);
-  MOE_CUDA_CHECK(run_gemm(g2, s), "fc2 grouped GEMM");
+  if (fused_q) {
+    if (!tc_q_supported(g2))
+      return fail(MOE_B200_NOT_IMPLEMENTED, "QMoE fc2: operands not 16-byte aligned");
+    MOE_CUDA_CHECK(launch_gemm_tc_q(g2, device_sm_count(), s), "fc2 grouped GEMM (packed)");
+  } else {
+    MOE_CUDA_CHECK(run_gemm(g2, s), "fc2 grouped GEMM");
+  }
 
   mark(kStCombine);
   MOE_CUDA_CHECK(launch_combine(p.dtype, xp, pos, w, T, k, H, t.output, s), "combine");

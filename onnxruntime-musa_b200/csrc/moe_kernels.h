@@ -60,6 +60,7 @@ struct GemmOperandB {
   int G;               // interleave factor (1 or 2)
   int n_off;           // row offset (split fc1: I for the linear half)
   int n_rows;          // rows of one expert's matrix (as stored: N*G + ...)
+  const void* scales = nullptr;  // packed (QMoE) operand: fp16 scales per stored row/block
 };
 
 struct GemmArgs {
@@ -83,6 +84,8 @@ struct GemmArgs {
   void* out;                   // [R, N]
   int64_t ldo;
   int* err;
+  int qbits = 0;               // 4 / 8: B operands are packed codes (b*.scales set)
+  int qblock = 0;              // scale block along K (0 = one scale per row)
 };
 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);
@@ -90,5 +93,8 @@ cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);
 bool tc_supported(const GemmArgs& g);
 // mode: 0 = choose, 1 = single-CTA kernel, 2 = CTA-pair (cta_group::2) kernel.
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, int mode, cudaStream_t s);
+// CTA-pair kernel with int4/int8 B operands dequantised in shared memory (fp16 only).
+bool tc_q_supported(const GemmArgs& g);
+cudaError_t launch_gemm_tc_q(const GemmArgs& g, int num_sms, cudaStream_t s);
 
 }  // namespace moe

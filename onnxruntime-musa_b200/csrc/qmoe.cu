@@ -249,8 +249,20 @@ int qmoe_decode_combine(const moe_b200_problem& p, const moe_b200_tensors& t, co
   return MOE_B200_OK;
 }
 
+bool qmoe_use_fused(const moe_b200_problem& p) {
+  const int bits = p.attrs.expert_weight_bits;
+  if (bits == 0 || qmoe_use_decode(p) || p.dtype != kDtF16) return false;
+  if (std::getenv("MOE_B200_QMOE_DEQUANT") != nullptr) return false;
+  // Beyond ~16K routed rows the fp16 GEMM on dequantised copies is faster: the one-off
+  // dequantisation is amortised, and the fp16 kernel reaches a higher tensor rate.
+  if (p.num_rows * p.attrs.k > kQmoeFusedMaxRows) return false;
+  const int bs = p.attrs.block_size;
+  auto k_ok = [&](int64_t K) { return K % 64 == 0 && (K * bits / 8) % 16 == 0; };
+  return k_ok(p.hidden_size) && k_ok(p.inter_size) && (bs == 0 || bs % 8 == 0);
+}
+
 size_t qmoe_workspace_bytes(const moe_b200_problem& p) {
-  if (p.attrs.expert_weight_bits == 0) return 0;
+  if (p.attrs.expert_weight_bits == 0 || qmoe_use_fused(p)) return 0;
   if (qmoe_use_decode(p))
     return fc1_partial_bytes(p) +
            align256(static_cast<size_t>(fc2_splits(p)) * p.num_rows * p.attrs.k * p.hidden_size *

@@ -20,6 +20,10 @@ int64_t fc1_rows(const moe_b200_problem& p);
 // True when this QMoE call takes the weight-streaming decode kernels.
 bool qmoe_use_decode(const moe_b200_problem& p);
 
+// True when a QMoE call beyond the decode sizes runs the tensor-core kernel that
+// dequantises the packed weights in shared memory (no unpacked copy in HBM).
+bool qmoe_use_fused(const moe_b200_problem& p);
+
 // Workspace bytes of the QMoE path: fp32 partial sums (decode) or the dequantised
 // weight copies (larger calls); 0 for MoE problems.
 size_t qmoe_workspace_bytes(const moe_b200_problem& p);

@@ -41,6 +41,8 @@ struct QDecodeArgs {
 // Rows of T*k up to which the decode kernels replace dequantise + tensor-core GEMM.
 constexpr int64_t kQmoeDecodeMaxRows = 512;
 constexpr int kQmoeMaxSplits = 8;
+// Routed rows up to which QMoE prefill dequantises in shared memory inside the GEMM.
+constexpr int64_t kQmoeFusedMaxRows = 16384;
 
 bool qmoe_decode_supported(int dtype, int bits, int block_size, int64_t H, int64_t I);
 cudaError_t launch_qmoe_decode(const QDecodeArgs& a, int max_experts_touched, cudaStream_t s);

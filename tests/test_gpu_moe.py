@@ -302,3 +302,34 @@ def test_qmoe_decode_variants(pkg, orc, dev, variant):
     ref = orc.moe(q["x"], q["router_probs"], W1, q.get("fc1_b"), W2, q.get("fc2_b"), W3, None,
                   **{kk: v for kk, v in attrs.items() if kk not in ("expert_weight_bits", "block_size")})
     np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+
+
+QMOE_PREFILL_CASES = [
+    # (T, H, I, E, k, bits, block_size)
+    (300, 512, 384, 8, 2, 4, 128),
+    (400, 256, 640, 8, 2, 8, 0),
+    (700, 384, 256, 16, 2, 4, 32),
+    (260, 256, 256, 4, 4, 8, 64),
+]
+
+
+@pytest.mark.parametrize("case", QMOE_PREFILL_CASES, ids=lambda c: f"T{c[0]}H{c[1]}I{c[2]}E{c[3]}k{c[4]}b{c[5]}bs{c[6]}")
+def test_qmoe_prefill_fused_dequant(pkg, orc, dev, case):
+    """T*k beyond the decode sizes: packed weights dequantised in shared memory by the
+    tensor-core kernel, against the oracle and the dequantise-to-HBM path."""
+    T, H, I, E, k, bits, bs = case
+    mu = -5.0 if bits == 4 else -8.5
+    q = orc.make_qmoe_inputs(T=T, H=H, I=I, E=E, k=k, bits=bits, block_size=bs,
+                             scale_mu=mu, scale_sigma=0.3, seed=T + bits)
+    attrs = dict(q["attrs"], k=k)
+    ref = orc.qmoe(q["x"], q["router_probs"], q["fc1_q"], q["fc1_scales"], None, q["fc2_q"],
+                   q["fc2_scales"], None, q["fc3_q"], q["fc3_scales"], None, **attrs)
+    out = _qmoe_run(pkg, dev, q, attrs)
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+    os.environ["MOE_B200_QMOE_DEQUANT"] = "1"
+    try:
+        out2 = _qmoe_run(pkg, dev, q, attrs)
+    finally:
+        del os.environ["MOE_B200_QMOE_DEQUANT"]
+    np.testing.assert_allclose(as_np(out2), ref, **TOL["float16"])
+    np.testing.assert_allclose(as_np(out), as_np(out2), rtol=1e-2, atol=1e-3)
