@@ -98,7 +98,7 @@ WsLayout plan_workspace(const moe_b200_problem& p) {
   WsLayout L{};
   const int64_t T = p.num_rows, E = p.num_experts, k = p.attrs.k;
   const int64_t R = T * k;
-  const int64_t chunks = num_route_chunks(T);
+  const int64_t chunks = num_route_chunks(T, layer_route_chunk(T));
   const size_t es = static_cast<size_t>(dtype_bytes(p.dtype));
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
@@ -308,13 +308,15 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
 
   MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, sizeof(int), s), "clear error word");
   const size_t es = dtype_bytes(p.dtype);
+  const int chunk = layer_route_chunk(T);
   if (given_idx != nullptr) {
     // Supplied routing: unit weights, histogram and plan of the given expert ids.
     mark(kStRoute);
     MOE_CUDA_CHECK(launch_fill_f32(w, 1.0f, R, s), "unit weights");
-    MOE_CUDA_CHECK(launch_histogram(given_idx, T, 1, E, cc, err, s), "histogram");
+    MOE_CUDA_CHECK(launch_histogram(given_idx, T, 1, E, cc, err, s, chunk), "histogram");
     mark(kStPlan);
-    MOE_CUDA_CHECK(launch_plan(given_idx, T, 1, E, cc, cb, offs, t128, t64, t256, pos, src, s),
+    MOE_CUDA_CHECK(launch_plan(given_idx, T, 1, E, cc, cb, offs, t128, t64, t256, pos, src, s,
+                               chunk),
                    "plan");
     if (qmoe_use_decode(p)) {
       mark(kStGather);
@@ -357,10 +359,11 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   if (given_idx == nullptr) {
     mark(kStRoute);
     MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
-                                p.attrs.normalize_routing_weights, idx, w, cc, s),
+                                p.attrs.normalize_routing_weights, idx, w, cc, s, chunk),
                    "route");
     mark(kStPlan);
-    MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s), "plan");
+    MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s, chunk),
+                   "plan");
   }
   mark(kStGather);
   MOE_CUDA_CHECK(launch_gather(t.input, static_cast<int64_t>(H) * es, k, src, R, xp, s),
@@ -514,11 +517,12 @@ int moe_b200_ep_dispatch(const moe_b200_problem* problem, const void* router_pro
   auto* t64 = reinterpret_cast<int32_t*>(ws + L.tiles64);
   auto* t256 = reinterpret_cast<int32_t*>(ws + L.tiles256);
   auto* src = reinterpret_cast<int32_t*>(ws + L.src);
+  const int chunk = layer_route_chunk(T);
   MOE_CUDA_CHECK(launch_route(p.dtype, router_probs, T, E, k, p.attrs.normalize_routing_weights,
-                              idx, route_weight, cc, s),
+                              idx, route_weight, cc, s, chunk),
                  "route");
   MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, expert_offsets, t128, t64, t256, permuted_pos,
-                             src, s),
+                             src, s, chunk),
                  "plan");
   MOE_CUDA_CHECK(launch_gather(input, static_cast<int64_t>(p.hidden_size) * dtype_bytes(p.dtype),
                                k, src, static_cast<int64_t>(T) * k, send_rows, s),

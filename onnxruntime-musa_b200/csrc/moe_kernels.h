@@ -18,11 +18,18 @@ int set_error(int code, const char* fmt, ...);
 
 inline int dtype_bytes(int dt) { return dt == kDtF32 ? 4 : (dt == kDtU8 ? 1 : 2); }
 
-// Routing chunk: rows handled by one CTA of the router / permutation kernels.
+// Routing chunk: rows handled by one CTA of the router / permutation kernels (the
+// standalone stage entry points use kRouteChunk; a layer call sizes chunks to the GPU).
 constexpr int kRouteThreads = 256;
 constexpr int kRouteChunk = 256;
-inline int num_route_chunks(int64_t rows) {
-  return static_cast<int>((rows + kRouteChunk - 1) / kRouteChunk);
+inline int num_route_chunks(int64_t rows, int chunk = kRouteChunk) {
+  return static_cast<int>((rows + chunk - 1) / chunk);
+}
+// Rows per routing chunk of a layer call: about one chunk per SM, 32..256 rows.
+inline int layer_route_chunk(int64_t rows) {
+  int64_t c = (rows + 147) / 148;
+  c = (c + 31) / 32 * 32;
+  return static_cast<int>(c < 32 ? 32 : (c > kRouteChunk ? kRouteChunk : c));
 }
 constexpr int kMaxExperts = 256;
 constexpr int kMaxK = 32;
@@ -30,18 +37,19 @@ constexpr int kMaxK = 32;
 constexpr int kSmallDispatchRows = 1024;
 
 cudaError_t launch_route(int dtype, const void* logits, int T, int E, int k, int normalize,
-                         int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s);
+                         int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s,
+                         int chunk = kRouteChunk);
 // Routing + offsets + permutation of a call with T*k <= kSmallDispatchRows, one CTA
 // (no GEMM tile prefixes: for the decode kernels only).
 cudaError_t launch_small_dispatch(int dtype, const void* logits, int T, int E, int k,
                                   int normalize, int32_t* idx, float* w, int32_t* offsets,
                                   int32_t* pos, int32_t* src, cudaStream_t s);
 cudaError_t launch_histogram(const int32_t* idx, int T, int k, int E, int32_t* chunk_counts,
-                             int* err, cudaStream_t s);
+                             int* err, cudaStream_t s, int chunk = kRouteChunk);
 cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* chunk_counts,
                         int32_t* chunk_base, int32_t* offsets, int32_t* tiles128,
                         int32_t* tiles64, int32_t* tiles256, int32_t* pos, int32_t* src,
-                        cudaStream_t s);
+                        cudaStream_t s, int chunk = kRouteChunk);
 cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
                           int64_t rows, void* xp, cudaStream_t s);
 cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s);

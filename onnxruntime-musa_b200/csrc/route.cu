@@ -75,20 +75,20 @@ __device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int 
   my_w = normalize ? my_val / sel_sum : my_val / s;
 }
 
-// One warp per row, kRouteChunk rows per CTA; also the CTA's expert histogram.
+// One warp per row, `chunk` rows per CTA; also the CTA's expert histogram.
 template <typename T, int kPerLane>
 __global__ void __launch_bounds__(kRouteThreads)
 route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int normalize,
              int32_t* __restrict__ expert_idx, float* __restrict__ route_w,
-             int32_t* __restrict__ chunk_counts) {
+             int32_t* __restrict__ chunk_counts, int chunk) {
   extern __shared__ int32_t s_counts[];  // [E]
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_counts[e] = 0;
   __syncthreads();
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int row0 = blockIdx.x * kRouteChunk;
-  const int row_end = min(row0 + kRouteChunk, num_rows);
+  const int row0 = blockIdx.x * chunk;
+  const int row_end = min(row0 + chunk, num_rows);
   for (int t = row0 + warp; t < row_end; t += kRouteThreads / 32) {
     int my_idx;
     float w;
@@ -158,12 +158,12 @@ small_dispatch_kernel(const T* __restrict__ logits, int num_rows, int E, int k, 
 // Per-chunk histogram of an existing expert_idx (used when routing is supplied).
 __global__ void __launch_bounds__(kRouteThreads)
 histogram_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, int E,
-                 int32_t* __restrict__ chunk_counts, int* __restrict__ err) {
+                 int32_t* __restrict__ chunk_counts, int* __restrict__ err, int chunk) {
   extern __shared__ int32_t s_counts[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_counts[e] = 0;
   __syncthreads();
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk * k;
-  const int64_t end = imin64(base + static_cast<int64_t>(kRouteChunk) * k,
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * chunk * k;
+  const int64_t end = imin64(base + static_cast<int64_t>(chunk) * k,
                                    static_cast<int64_t>(num_rows) * k);
   for (int64_t i = base + threadIdx.x; i < end; i += blockDim.x) {
     const int e = expert_idx[i];
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kRouteThreads)
 permute_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, int E,
                const int32_t* __restrict__ expert_offsets,
                const int32_t* __restrict__ chunk_base, int32_t* __restrict__ permuted_pos,
-               int32_t* __restrict__ permuted_src) {
+               int32_t* __restrict__ permuted_src, int chunk) {
   extern __shared__ int32_t smem[];
   constexpr int kWarps = kRouteThreads / 32;
   int32_t* s_warp = smem;               // [kWarps][E]
@@ -239,8 +239,8 @@ permute_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, int 
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRouteChunk * k;
-  const int64_t end = imin64(base + static_cast<int64_t>(kRouteChunk) * k,
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * chunk * k;
+  const int64_t end = imin64(base + static_cast<int64_t>(chunk) * k,
                                    static_cast<int64_t>(num_rows) * k);
   const uint32_t lt_mask = (1u << lane) - 1u;
   for (int64_t g = base; g < end; g += kRouteThreads) {
@@ -347,29 +347,30 @@ cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s) 
 template <typename T>
 static cudaError_t launch_route_t(const void* logits, int T_, int E, int k, int normalize,
                                   int32_t* idx, float* w, int32_t* chunk_counts,
-                                  cudaStream_t s) {
-  const int chunks = num_route_chunks(T_);
+                                  cudaStream_t s, int chunk) {
+  const int chunks = num_route_chunks(T_, chunk);
   const size_t sm = static_cast<size_t>(E) * sizeof(int32_t);
   const T* l = static_cast<const T*>(logits);
   const int per_lane = (E + 31) / 32;
   if (per_lane <= 1)
-    route_kernel<T, 1><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+    route_kernel<T, 1><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
   else if (per_lane <= 2)
-    route_kernel<T, 2><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+    route_kernel<T, 2><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
   else if (per_lane <= 4)
-    route_kernel<T, 4><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+    route_kernel<T, 4><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
   else
-    route_kernel<T, 8><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts);
+    route_kernel<T, 8><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
   return cudaGetLastError();
 }
 
 cudaError_t launch_route(int dtype, const void* logits, int T_, int E, int k, int normalize,
-                         int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s) {
+                         int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s,
+                         int chunk) {
   if (T_ == 0) return cudaSuccess;
   switch (dtype) {
-    case kDtF32: return launch_route_t<float>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
-    case kDtF16: return launch_route_t<__half>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
-    case kDtBF16: return launch_route_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, chunk_counts, s);
+    case kDtF32: return launch_route_t<float>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk);
+    case kDtF16: return launch_route_t<__half>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk);
+    case kDtBF16: return launch_route_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk);
   }
   return cudaErrorInvalidValue;
 }
@@ -404,24 +405,25 @@ cudaError_t launch_small_dispatch(int dtype, const void* logits, int T_, int E, 
 }
 
 cudaError_t launch_histogram(const int32_t* idx, int T_, int k, int E, int32_t* chunk_counts,
-                             int* err, cudaStream_t s) {
+                             int* err, cudaStream_t s, int chunk) {
   if (T_ == 0) return cudaSuccess;
-  histogram_kernel<<<num_route_chunks(T_), kRouteThreads, E * sizeof(int32_t), s>>>(
-      idx, T_, k, E, chunk_counts, err);
+  histogram_kernel<<<num_route_chunks(T_, chunk), kRouteThreads, E * sizeof(int32_t), s>>>(
+      idx, T_, k, E, chunk_counts, err, chunk);
   return cudaGetLastError();
 }
 
 cudaError_t launch_plan(const int32_t* idx, int T_, int k, int E, const int32_t* chunk_counts,
                         int32_t* chunk_base, int32_t* offsets, int32_t* tiles128,
                         int32_t* tiles64, int32_t* tiles256, int32_t* pos, int32_t* src,
-                        cudaStream_t s) {
-  const int chunks = num_route_chunks(T_);
+                        cudaStream_t s, int chunk) {
+  const int chunks = num_route_chunks(T_, chunk);
   scan_kernel<<<1, 1024, E * sizeof(int32_t), s>>>(chunk_counts, chunks, E, chunk_base,
                                                    offsets, tiles128, tiles64, tiles256);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess || T_ == 0) return st;
   const size_t sm = (static_cast<size_t>(kRouteThreads / 32) + 2) * E * sizeof(int32_t);
-  permute_kernel<<<chunks, kRouteThreads, sm, s>>>(idx, T_, k, E, offsets, chunk_base, pos, src);
+  permute_kernel<<<chunks, kRouteThreads, sm, s>>>(idx, T_, k, E, offsets, chunk_base, pos, src,
+                                                   chunk);
   return cudaGetLastError();
 }
 
