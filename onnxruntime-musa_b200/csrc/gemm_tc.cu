@@ -66,6 +66,9 @@ struct TcParams {
   int qblock;
   int b1_G, b3_G;
   int b1_rows, b3_rows;  // stored rows of one expert
+  // Test hook: the producers issue no loads, so the consumers' bounded waits expire and
+  // the kernel unwinds with an error code (exercises failure handling without a fault).
+  int test_stall;
 };
 
 __device__ __forceinline__ void decode_tile(int L, const int32_t* s_tiles, int E, int n_tiles,
@@ -256,7 +259,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int L = blockIdx.x; L < total && !*abort_flag; L += gridDim.x) {
+      for (int L = blockIdx.x; L < total && !*abort_flag && !p.test_stall; L += gridDim.x) {
         int e, m, n;
         decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
         const int row0 = s_offs[e] + m * BM;
@@ -452,7 +455,7 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int L = pair; L < total && !*abort_flag; L += npairs) {
+      for (int L = pair; L < total && !*abort_flag && !p.test_stall; L += npairs) {
         int e, m, n;
         decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
         const int row0 = s_offs[e] + m * P_BM + static_cast<int>(rank) * BM;
@@ -707,7 +710,7 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int L = pair; L < total && !*abort_flag; L += npairs) {
+      for (int L = pair; L < total && !*abort_flag && !p.test_stall; L += npairs) {
         int e, m, n;
         decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
         const int row0 = s_offs[e] + m * P_BM + static_cast<int>(rank) * BM;
@@ -729,7 +732,7 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int L = pair; L < total && !*abort_flag; L += npairs) {
+      for (int L = pair; L < total && !*abort_flag && !p.test_stall; L += npairs) {
         int e, m, n;
         decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
         const CUtensorMap* qmap = use3 ? &map_q3 : &map_q1;
@@ -989,6 +992,7 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   p.out = g.out;
   p.ldo = g.ldo;
   p.err = g.err;
+  p.test_stall = g.test_stall;
   // The attribute call is idempotent; a race between first callers is benign.
   static bool attr_set[2] = {false, false};
   if (!attr_set[pair]) {
@@ -1065,6 +1069,7 @@ cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.out = g.out;
   p.ldo = g.ldo;
   p.err = g.err;
+  p.test_stall = g.test_stall;
   p.scales1 = static_cast<const __half*>(g.b1.scales);
   p.scales3 = static_cast<const __half*>(g.gated ? g.b3.scales : g.b1.scales);
   p.qblock = g.qblock;

@@ -395,6 +395,9 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g1.out = act;
   g1.ldo = I;
   g1.err = err;
+  // MOE_B200_TEST_STALL=1 (tests only): the GEMM producers issue no loads, the kernel's
+  // bounded waits expire and the call reports the device error instead of hanging.
+  g1.test_stall = env_flag("MOE_B200_TEST_STALL") ? 1 : 0;
   if (fused_q) set_quantized(p, g1, t.fc1_scales, t.fc3_scales);
   mark(kStFc1);
   if (fused_q) {
@@ -415,6 +418,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g2.out = xp;  // Y aliases the gathered input, dead after fc1
   g2.ldo = H;
   g2.err = err;
+  g2.test_stall = g1.test_stall;
   if (fused_q) set_quantized(p, g2, t.fc2_scales, nullptr);
   mark(kStFc2);
   if (fused_q) {

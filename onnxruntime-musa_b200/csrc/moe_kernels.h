@@ -94,6 +94,7 @@ struct GemmArgs {
   int* err;
   int qbits = 0;               // 4 / 8: B operands are packed codes (b*.scales set)
   int qblock = 0;              // scale block along K (0 = one scale per row)
+  int test_stall = 0;          // test hook: tensor-core producers issue nothing
 };
 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);

@@ -8,6 +8,7 @@ single-device layer on its own tokens with all experts.
 
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -101,3 +102,49 @@ def test_expert_parallel_exchange_matches_single_device(world):
     for r in range(world):
         assert not isinstance(results[r], str), results[r]
         assert results[r] < 1e-10, f"rank {r}: max |ep - ref| = {results[r]}"
+
+
+def _dead_peer_worker(rank, world, port, result_q):
+    import datetime
+    import __graft_entry__ as ge
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    if rank == 1:  # this rank leaves between layer calls, before its next collective
+        result_q.put((rank, "left"))
+        return
+    pkg, orc = ge.load_package(), ge.load_oracle()
+    from onnxruntime_musa_b200 import ep
+    attrs = dict(activation_type="silu", k=2, normalize_routing_weights=1)
+    full = orc.make_moe_inputs(T=16, H=16, I=8, E=4, k=2, act="silu", gated=True,
+                               dtype="float64", seed=1)
+    w = dict(fc1_weights=full["fc1_w"], fc2_weights=full["fc2_w"], fc3_weights=full["fc3_w"])
+    local = ep.shard_experts({n: torch.from_numpy(v) for n, v in w.items()}, rank, world)
+    layer = ep.ExpertParallelMoE(pkg, num_experts=4, hidden_size=16, inter_size=8,
+                                 dtype=pkg.FLOAT, has_fc3=True, local_weights=local,
+                                 backend=OracleBackend(orc, attrs), **attrs)
+    t0 = time.time()
+    try:
+        layer.forward(torch.from_numpy(full["x"]), torch.from_numpy(full["router_probs"]))
+        result_q.put((rank, "no error"))
+    except Exception as exc:
+        result_q.put((rank, ("raised", type(exc).__name__, time.time() - t0)))
+
+
+def test_expert_parallel_dead_peer_raises():
+    """A rank that stops taking part makes the survivor's next collective fail with an
+    error (connection loss or the process-group timeout), never a hang."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left"
+    assert isinstance(res[0], tuple) and res[0][0] == "raised", res[0]
+    assert res[0][2] < 60
