@@ -444,8 +444,9 @@ def bench_ep(args, cfg, rank, world, dev):
         return float(t.item())
 
     x, lg = L["x"], L["router_probs"]
+    chunks = args.ep_chunks or 1
     with ClockSampler(dev.index) as clk:
-        ms = timed(lambda: layer.forward(x, lg))
+        ms = timed(lambda: layer.forward(x, lg, chunks=chunks))
     hx, hl = x.cpu().pin_memory(), lg.cpu().pin_memory()
     hout = torch.empty_like(hx).pin_memory()
     dx, dl = torch.empty_like(x), torch.empty_like(lg)
@@ -453,7 +454,7 @@ def bench_ep(args, cfg, rank, world, dev):
     def e2e_step():
         dx.copy_(hx, non_blocking=True)
         dl.copy_(hl, non_blocking=True)
-        hout.copy_(layer.forward(dx, dl), non_blocking=True)
+        hout.copy_(layer.forward(dx, dl, chunks=chunks), non_blocking=True)
 
     e2e_ms = timed(e2e_step)
     pk = peaks()
@@ -467,7 +468,7 @@ def bench_ep(args, cfg, rank, world, dev):
         "vs_baseline": None, "dtype": "f32" if cfg.get("dtype") == "float32" else "f16",
         "data": "synthetic (seeded, on-device; config distributions; random init)",
         "config": {"workload": cfg["desc"].format(T=T), "global_batch": T * world,
-                   "tokens_per_gpu": T, "parallelism": f"ep{world}",
+                   "tokens_per_gpu": T, "parallelism": f"ep{world}", "ep_chunks": chunks,
                    "l2": "inputs larger than L2 (weights streamed every step)"},
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": hx.numel() * es + hl.numel() * es,
@@ -478,7 +479,7 @@ def bench_ep(args, cfg, rank, world, dev):
                      "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)"},
         # dispatch (route, scan, permute, gather) + expert FFN (fill, histogram, scan,
         # permute, gather, fc1, fc2, un-permute) + combine
-        "gpu_launches": 13 * args.steps,
+        "gpu_launches": 13 * chunks * args.steps,
         "clocks": clk.summary(),
     }
 
@@ -519,6 +520,9 @@ def main():
     ap.add_argument("--tokens", default=None,
                     help="tokens per GPU (comma list for a sweep); default: the config's")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--ep-chunks", type=int, default=None,
+                    help="token chunks pipelined through the expert-parallel exchange "
+                         "(default 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -12,6 +12,9 @@ routing).  One layer call:
   5. rows back (NCCL)    all-to-all of the FFN rows along the reverse splits;
   6. combine   (device)  out[t] = sum_j w[t,j] * rows[pos[t,j]].
 
+Optionally the tokens go through in chunks whose row all-to-alls run on NCCL's stream while
+another chunk's experts compute (off by default; see :meth:`ExpertParallelMoE.forward`).
+
 The reference plugin has no parallelism at all (one EP instance drives one device,
 ``musa/ep/src/ep_factory.cc:466-470``); the design follows the plan for the MoE path:
 the split sizes of the variable all-to-all need the counts on the host, which costs one
@@ -86,26 +89,64 @@ class ExpertParallelMoE:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
         return out
 
-    def forward(self, x, router_probs):
-        """x [T, H], router_probs [T, E] -> output [T, H] for this rank's tokens."""
+    def forward(self, x, router_probs, chunks: int | None = None):
+        """x [T, H], router_probs [T, E] -> output [T, H] for this rank's tokens.
+
+        With ``chunks`` > 1 the tokens are processed in chunks whose row exchanges run
+        asynchronously on NCCL's stream while the previous chunk's experts compute; the
+        count exchange of all chunks costs one host round trip.  The default is one chunk:
+        the persistent expert GEMM holds every SM, so the exchange kernels cannot run beside
+        it, and smaller chunks only lower the rows per expert (measured on two B200s at
+        4096 tokens per rank: 2.92 ms with 1 chunk, 3.37 ms with 2, 4.38 ms with 4)."""
         T = x.shape[0]
         W, El = self.world, self.E_local
-        send, offsets, pos, w = self.backend.dispatch(self._problem(T, self.E, self.k), x,
-                                                     router_probs)
-        counts = (offsets[1:] - offsets[:-1]).to(torch.int64).view(W, El)
-        recv_counts = self._a2a(torch.empty_like(counts).view(-1), counts.reshape(-1)).view(W, El)
-        send_splits = counts.sum(1).tolist()          # the one host round trip per call
-        recv_splits = recv_counts.sum(1).tolist()
-        recv = send.new_empty((sum(recv_splits), self.H))
-        self._a2a(recv, send, recv_splits, send_splits)
-        local_ids = torch.arange(El, device=recv.device, dtype=torch.int32).repeat(W)
-        row_expert = torch.repeat_interleave(local_ids, recv_counts.reshape(-1).to(recv.device))
-        y_recv = self.backend.expert_ffn(self._problem(recv.shape[0], El, 1), recv,
-                                         row_expert.to(torch.int32).contiguous(), self.weights)
-        y_send = torch.empty_like(send)
-        self._a2a(y_send, y_recv, send_splits, recv_splits)
+        if chunks is None:
+            chunks = 1
+        bounds = [T * c // chunks for c in range(chunks + 1)]
+        parts = []
+        for c in range(chunks):
+            xs, ls = x[bounds[c]:bounds[c + 1]], router_probs[bounds[c]:bounds[c + 1]]
+            send, offsets, pos, w = self.backend.dispatch(
+                self._problem(xs.shape[0], self.E, self.k), xs, ls)
+            parts.append(dict(send=send, offsets=offsets, pos=pos, w=w))
+        counts = torch.stack([(p["offsets"][1:] - p["offsets"][:-1]).to(torch.int64).view(W, El)
+                              for p in parts])                      # [chunks, W, El]
+        # Per destination rank: the counts of every chunk, as one even all-to-all.
+        send_c = counts.permute(1, 0, 2).reshape(-1).contiguous()  # [W, chunks, El]
+        recv_c = self._a2a(torch.empty_like(send_c), send_c).view(W, chunks, El)
+        send_splits = counts.sum(2).tolist()                       # the one host round trip
+        recv_splits = recv_c.sum(2).t().tolist()                   # [chunks][W]
+        for c, p in enumerate(parts):
+            p["send_splits"], p["recv_splits"] = send_splits[c], recv_splits[c]
+            p["recv_counts"] = recv_c[:, c, :]
+            p["recv"] = p["send"].new_empty((sum(recv_splits[c]), self.H))
+            p["h"] = self._a2a_async(p["recv"], p["send"], p["recv_splits"], p["send_splits"])
+        for c, p in enumerate(parts):
+            self._wait(p["h"])
+            local_ids = torch.arange(El, device=p["recv"].device, dtype=torch.int32).repeat(W)
+            row_expert = torch.repeat_interleave(local_ids, p["recv_counts"].reshape(-1).to(
+                p["recv"].device))
+            y_recv = self.backend.expert_ffn(self._problem(p["recv"].shape[0], El, 1), p["recv"],
+                                             row_expert.to(torch.int32).contiguous(), self.weights)
+            p["y_send"] = torch.empty_like(p["send"])
+            p["hb"] = self._a2a_async(p["y_send"], y_recv, p["send_splits"], p["recv_splits"])
         out = torch.empty_like(x)
-        return self.backend.combine(y_send, pos, w, out)
+        for c, p in enumerate(parts):
+            self._wait(p["hb"])
+            self.backend.combine(p["y_send"], p["pos"], p["w"], out[bounds[c]:bounds[c + 1]])
+        return out
+
+    def _a2a_async(self, out, inp, out_splits, in_splits):
+        if self.world == 1:
+            out.copy_(inp)
+            return None
+        return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group,
+                                      async_op=True)
+
+    @staticmethod
+    def _wait(handle):
+        if handle is not None:
+            handle.wait()
 
 
 def shard_experts(tensors: dict[str, Any], rank: int, world: int) -> dict[str, Any]:

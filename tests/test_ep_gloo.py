@@ -58,7 +58,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, result_q):
+def _worker(rank, world, port, result_q, chunks=None):
     import __graft_entry__ as ge
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -78,7 +78,7 @@ def _worker(rank, world, port, result_q):
         layer = ep.ExpertParallelMoE(pkg, num_experts=E, hidden_size=H, inter_size=I,
                                      dtype=pkg.FLOAT, has_fc3=True, local_weights=local,
                                      backend=OracleBackend(orc, attrs), **attrs)
-        out = layer.forward(torch.from_numpy(x), torch.from_numpy(lg)).numpy()
+        out = layer.forward(torch.from_numpy(x), torch.from_numpy(lg), chunks=chunks).numpy()
         ref = orc.moe(x, lg, full["fc1_w"], full["fc1_b"], full["fc2_w"], full["fc2_b"],
                       full["fc3_w"], full["fc3_b"], **attrs)
         result_q.put((rank, float(np.abs(out - ref).max())))
@@ -88,12 +88,13 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [1, 2, 4])
-def test_expert_parallel_exchange_matches_single_device(world):
+@pytest.mark.parametrize("world,chunks", [(1, None), (2, None), (4, None), (2, 3), (4, 2)])
+def test_expert_parallel_exchange_matches_single_device(world, chunks):
+    """chunks > 1 pipelines the token chunks through asynchronous row exchanges."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, chunks)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=120) for _ in range(world))
