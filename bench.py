@@ -307,7 +307,7 @@ def bench_ours(args, cfg, rank, world, dev):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(step, steps):
+    def timed(step, steps, timed_step=None):
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize(dev)
@@ -316,22 +316,27 @@ def bench_ours(args, cfg, rank, world, dev):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(steps):
-            step()
+            (timed_step or step)()
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
         return max_over_ranks(e0.elapsed_time(e1)) / steps
 
-    # ---- device-resident throughput
+    # ---- device-resident throughput; the stage boundaries of every timed call are
+    # recorded with CUDA events on the same stream (no synchronisation inside the loop),
+    # so the per-stage times come from the timed region itself.
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(pkg.STAGES) + 1)]
+           for _ in range(args.steps)]
+    for row in evs:
+        for ev in row:
+            ev.record(stream)  # creates the event handle
+    it = iter(evs)
     with ClockSampler(dev.index) as clk:
-        ms = timed(lambda: pkg.forward(prob, tens, ws, stream), args.steps)
+        ms = timed(lambda: pkg.forward(prob, tens, ws, stream), args.steps,
+                   timed_step=lambda: pkg.forward_staged(prob, tens, ws, next(it), stream))
     value = world * T / (ms / 1e3)
-
-    # ---- per-stage CUDA-event times
-    stage = {s: [] for s in pkg.STAGES}
-    for _ in range(max(3, min(args.steps, 10))):
-        for s, v in pkg.forward_timed(prob, tens, ws, stream).items():
-            stage[s].append(v)
+    stage = {s: [row[i].elapsed_time(row[i + 1]) for row in evs]
+             for i, s in enumerate(pkg.STAGES)}
     stage_ms = {s: statistics.median(v) for s, v in stage.items()}
 
     # ---- end to end through the kernel object with host buffers

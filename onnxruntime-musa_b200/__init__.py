@@ -112,6 +112,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                         _SZ, _VP]),
     "moe_b200_forward_timed": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                               _VP, _SZ, _VP, _PF, _I32]),
+    "moe_b200_forward_staged": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
+                                               _VP, _SZ, _VP, ctypes.POINTER(_VP), _I32]),
     "moe_b200_ep_dispatch": (ctypes.c_int, [ctypes.POINTER(Problem), _VP, _VP, _VP, _VP, _VP,
                                             _VP, _VP, _SZ, _VP]),
     "moe_b200_expert_ffn": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors), _VP,
@@ -436,6 +438,21 @@ def forward_timed(problem: Problem, tensors: Mapping[str, Any], workspace, strea
                                        workspace.data_ptr(), workspace.numel(),
                                        _stream_handle(stream), ms, len(STAGES)))
     return dict(zip(STAGES, list(ms)))
+
+
+def forward_staged(problem: Problem, tensors: Mapping[str, Any], workspace, events,
+                   stream=None) -> None:
+    """``forward`` that records ``events`` (len(STAGES) + 1 ``torch.cuda.Event`` objects
+    with timing, each recorded at least once before) at the stage boundaries, without
+    synchronising; ``events[i].elapsed_time(events[i + 1])`` is stage i."""
+    t = Tensors()
+    for name, _ in Tensors._fields_:
+        v = tensors.get(name)
+        setattr(t, name, None if v is None else (v if isinstance(v, int) else v.data_ptr()))
+    handles = (_VP * len(events))(*[ev.cuda_event for ev in events])
+    check(lib().moe_b200_forward_staged(ctypes.byref(problem), ctypes.byref(t),
+                                        workspace.data_ptr(), workspace.numel(),
+                                        _stream_handle(stream), handles, len(events)))
 
 
 # ------------------------------------------------------------------ stages

@@ -69,6 +69,11 @@ struct TcParams {
   // Test hook: the producers issue no loads, so the consumers' bounded waits expire and
   // the kernel unwinds with an error code (exercises failure handling without a fault).
   int test_stall;
+  // CTA-pair kernel: last tiles of an expert with <= swap_max rows run swapped (0 = never).
+  int swap_max;
+  // CTA-pair kernel: zeroed counter from which pairs claim tiles in order (dynamic
+  // schedule); nullptr = static round-robin.
+  int* tile_counter;
 };
 
 __device__ __forceinline__ void decode_tile(int L, const int32_t* s_tiles, int E, int n_tiles,
@@ -383,20 +388,147 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
 constexpr int P_BM = 256;         // rows per pair tile
 constexpr int P_STAGES = 6;
 constexpr int P_STAGE_BYTES = A_BYTES + B_HALF;  // per CTA: 128x64 of A + 128x64 of B
-constexpr int P_SMEM_BYTES =
-    1024 + P_STAGES * P_STAGE_BYTES + 64 * 8 + 2 * (kMaxExperts + 1) * 4;
+constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + 16 * 32 * 4 * 4 /*exchange*/ +
+                             64 * 8 + 2 * (kMaxExperts + 1) * 4;
+
+constexpr int SW_TOK_ROWS = 64;   // token rows per TMA box of a swapped tile (1-2 per CTA)
+constexpr int kPairSwapLimit = 240;  // largest swapped tail (rows); 256 is a full tile
+constexpr int SW_HALF = 64;       // gated swapped tile: gate rows, then linear rows, per CTA
+constexpr int XCH_SLOTS = 4;      // gate/linear exchange slots (lane quarter pair x column half)
+constexpr int XCH_BYTES = XCH_SLOTS * 16 * 32 * 4;
+
+// One tile of the pair kernel.  A tile whose rows (the expert's last, ragged m-tile) are at
+// most swap_max is computed swapped: D[w, t] = sum_k W[w, k] X[t, k] with the 256 weight rows
+// of the tile as M (128 per CTA, in TMEM lanes) and its rows as N = nt (rows rounded up to
+// 16; nt / 2 per CTA), so its MMA work scales with the rows instead of a full 256.
+struct PairTile {
+  int e, m, n;
+  int r0;     // first permuted row
+  int rows;   // valid rows (<= 256)
+  int nt;     // swapped: MMA N; 0 for a normal tile
+};
+
+__device__ __forceinline__ PairTile pair_tile(int L, const int32_t* s_tiles,
+                                              const int32_t* s_offs, const TcParams& p) {
+  PairTile t;
+  decode_tile(L, s_tiles, p.E, p.n_tiles, t.e, t.m, t.n);
+  t.r0 = s_offs[t.e] + t.m * P_BM;
+  t.rows = min(P_BM, s_offs[t.e + 1] - t.r0);
+  t.nt = t.rows <= p.swap_max ? (t.rows + 15) & ~15 : 0;
+  return t;
+}
+
+// Gate/linear hand-over of the gated swapped epilogue: one slot of 16 columns x 32 lanes
+// of fp32, filled by a linear-quarter warp and drained by its gate-quarter partner.
+struct Exchange {
+  float* buf;        // [XCH_SLOTS][16][32]
+  uint64_t* full;    // [XCH_SLOTS], 32 arrivals (the linear warp's lanes)
+  uint64_t* empty;   // [XCH_SLOTS], 32 arrivals (the gate warp's lanes)
+};
+
+// Epilogue of a swapped tile for the calling warp (TMEM lane quarter q, column chunks of
+// 16 starting at c_first, stride 32).  Returns false when a bounded wait expired.
+//  plain: lane l of CTA `rank` holds output column f = n*256 + rank*128 + q*32 + l for the
+//         tile's rows (TMEM columns);
+//  gated: lanes 0..63 of CTA `rank` hold the gate rows and lanes 64..127 the linear rows of
+//         output columns f = n*128 + rank*64 + [0, 64); a linear-quarter warp (q = 2, 3)
+//         passes its chunk (+ bias) through shared memory to the gate-quarter warp q - 2,
+//         which applies the activation and stores.
+template <typename T>
+__device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTile& t,
+                                                 uint32_t taddr, int rank, int q, int lane,
+                                                 int half, const Exchange& x, uint32_t& xuse) {
+  T* out = static_cast<T*>(p.out);
+  const int c_first = 16 * half;
+  if (p.gated) {
+    const bool lin = q >= 2;
+    const int f = t.n * (BN / 2) + rank * SW_HALF + (q & 1) * 32 + lane;
+    const bool fok = f < p.N;
+    const int fc = min(f, p.N - 1);
+    const int slot = (q & 1) * 2 + half;
+    float* buf = x.buf + slot * 16 * 32;
+    const float own_bias = lin ? bias_val<T>(p.bias3, t.e, fc, p) : bias_val<T>(p.bias1, t.e, fc, p);
+#pragma unroll 1
+    for (int c = c_first; c < t.nt; c += 32, ++xuse) {
+      const uint32_t par = xuse & 1;
+      float v[16];
+      tmem_ld16(taddr + c, v);
+      tmem_ld_wait();
+      if (lin) {
+        if (!mbar_wait(&x.empty[slot], par ^ 1)) return false;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) buf[j * 32 + lane] = v[j] + own_bias;
+        mbar_arrive(&x.full[slot]);
+      } else {
+        if (!mbar_wait(&x.full[slot], par)) return false;
+        float u[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) u[j] = buf[j * 32 + lane];
+        mbar_arrive(&x.empty[slot]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int tok = c + j;
+          if (fok && tok < t.rows)
+            out[static_cast<int64_t>(t.r0 + tok) * p.ldo + f] =
+                from_f<T>(fast_act_gated(p.ap, v[j] + own_bias, u[j]));
+        }
+      }
+    }
+  } else {
+    const int f = t.n * BN + rank * (BN / 2) + q * 32 + lane;
+    const bool fok = f < p.N;
+    const float b = bias_val<T>(p.bias1, t.e, min(f, p.N - 1), p);
+#pragma unroll 1
+    for (int c = c_first; c < t.nt; c += 32) {
+      float v[16];
+      tmem_ld16(taddr + c, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int tok = c + j;
+        if (fok && tok < t.rows)
+          out[static_cast<int64_t>(t.r0 + tok) * p.ldo + f] =
+              from_f<T>(fast_act_single(p.ap.act, v[j] + b));
+      }
+    }
+  }
+  return true;
+}
+
+// Tile queue of the pair kernel.  The leader's producer claims tile numbers in order
+// (atomic counter) and publishes each in a TQ-deep queue in both CTAs' shared memory; the
+// consumers (leader MMA and epilogue warps, peer producer and epilogue warps) read it and
+// release the slot on the leader's tq_empty.  -1 ends the schedule.  Claiming in order
+// keeps the m-tiles that share a weight tile running at the same time (L2 reuse) while
+// pairs that drew cheap (swapped) tiles take more of them.
+constexpr int TQ = 4;
+constexpr int TQ_CONSUMERS = 2 + 2 * EPI_WARPS;
+
+__device__ __forceinline__ bool tq_take(int it, const volatile int* s_tq, uint64_t* tq_full,
+                                        uint64_t* tq_empty, bool leader, int& L) {
+  const int slot = it % TQ;
+  if (!mbar_wait_cluster(&tq_full[slot], (it / TQ) & 1)) return false;
+  L = s_tq[slot];
+  if (leader) mbar_arrive(&tq_empty[slot]);
+  else mbar_arrive_cluster(mapa_shared(smem_u32(&tq_empty[slot]), 0));
+  return true;
+}
 
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                             const __grid_constant__ CUtensorMap map_b1,
-                            const __grid_constant__ CUtensorMap map_b3, const TcParams p) {
+                            const __grid_constant__ CUtensorMap map_b3,
+                            const __grid_constant__ CUtensorMap map_a_sw,
+                            const __grid_constant__ CUtensorMap map_b1_sw,
+                            const __grid_constant__ CUtensorMap map_b3_sw, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + P_STAGES * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + P_STAGES * B_HALF);
+  float* xbuf = reinterpret_cast<float*>(sB + P_STAGES * B_HALF);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + P_STAGES * B_HALF + XCH_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + P_STAGES;
   uint64_t* tfull = bars + 2 * P_STAGES;
@@ -404,8 +536,14 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
   uint64_t* done = bars + 2 * P_STAGES + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Exchange xch{xbuf, bars + 32, bars + 32 + XCH_SLOTS};
+  uint64_t* tq_full = bars + 40;
+  uint64_t* tq_empty = bars + 44;
+  volatile int* s_tq = reinterpret_cast<volatile int*>(bars + 48);
   int32_t* s_tiles = reinterpret_cast<int32_t*>(bars + 64);
   int32_t* s_offs = s_tiles + (kMaxExperts + 1);
+  static_assert(2 * P_STAGES + 6 <= 32, "pair kernel barrier slots overlap the exchange");
+  static_assert(32 + 2 * XCH_SLOTS <= 40 && TQ == 4, "pair kernel barrier slots overlap");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -427,6 +565,14 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
       mbar_init(&tempty[a], 2 * EPI_WARPS);
     }
     mbar_init(done, 1);
+    for (int i = 0; i < XCH_SLOTS; ++i) {
+      mbar_init(&xch.full[i], 32);
+      mbar_init(&xch.empty[i], 32);
+    }
+    for (int i = 0; i < TQ; ++i) {
+      mbar_init(&tq_full[i], 1);
+      mbar_init(&tq_empty[i], TQ_CONSUMERS);
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -455,10 +601,33 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int L = pair; L < total && !*abort_flag && !p.test_stall; L += npairs) {
-        int e, m, n;
-        decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
-        const int row0 = s_offs[e] + m * P_BM + static_cast<int>(rank) * BM;
+      for (int it = 0;; ++it) {
+        int L;
+        if (leader) {
+          const int slot = it % TQ;
+          if (!mbar_wait_cluster(&tq_empty[slot], ((it / TQ) & 1) ^ 1)) {
+            atomicExch(p.err, kErrTimeoutProducer);
+            *abort_flag = 1;
+          }
+          L = *abort_flag ? -1
+                          : (p.tile_counter != nullptr ? atomicAdd(p.tile_counter, 1)
+                                                       : pair + it * npairs);
+          if (L >= total) L = -1;
+          s_tq[slot] = L;
+          st_cluster_s32(mapa_shared(smem_u32(const_cast<int*>(&s_tq[slot])), 1), L);
+          mbar_arrive(&tq_full[slot]);
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tq_full[slot]), 1));
+        } else if (*abort_flag || !tq_take(it, s_tq, tq_full, tq_empty, false, L)) {
+          atomicExch(p.err, kErrTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        if (L < 0) break;
+        if (p.test_stall) continue;
+        const PairTile t = pair_tile(L, s_tiles, s_offs, p);
+        const int e = t.e, n = t.n;
+        const int row0 = t.nt ? t.r0 + static_cast<int>(rank) * (t.nt / 2)
+                              : t.r0 + static_cast<int>(rank) * BM;
         const CUtensorMap* bmap = (p.gated && rank == 1) ? &map_b3 : &map_b1;
         int bg, brow;
         if (p.gated) {
@@ -468,6 +637,12 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
           bg = p.b1_g;
           brow = n * BN + static_cast<int>(rank) * (BN / 2) + p.b1_noff;
         }
+        // Swapped gated tile: this CTA's weight rows are the 64 gate rows, then the 64
+        // linear rows, of output columns n*128 + rank*64 + [0,64).
+        const int sw_col = n * (BN / 2) + static_cast<int>(rank) * SW_HALF;
+        const int tok_boxes = (t.nt / 2 + SW_TOK_ROWS - 1) / SW_TOK_ROWS;  // 1 or 2
+        const uint32_t tx =
+            t.nt ? 2 * (B_HALF + tok_boxes * SW_TOK_ROWS * BK * 2) : 2 * P_STAGE_BYTES;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             atomicExch(p.err, kErrTimeoutProducer);
@@ -475,10 +650,25 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
             break;
           }
           const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          if (leader) mbar_arrive_expect_tx(&full[stage], tx);
           const int kc = kb * BK;
-          tma_load_2d_pair(sA + stage * A_BYTES, &map_a, full_leader, kc, row0);
-          tma_load_4d_pair(sB + stage * B_HALF, bmap, full_leader, kc, bg, brow, e);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_HALF;
+          if (!t.nt) {
+            tma_load_2d_pair(a_dst, &map_a, full_leader, kc, row0);
+            tma_load_4d_pair(b_dst, bmap, full_leader, kc, bg, brow, e);
+          } else {
+            for (int j = 0; j < tok_boxes; ++j)
+              tma_load_2d_pair(a_dst + j * SW_TOK_ROWS * BK * 2, &map_a_sw, full_leader, kc,
+                               row0 + j * SW_TOK_ROWS);
+            if (p.gated) {
+              tma_load_4d_pair(b_dst, &map_b1_sw, full_leader, kc, p.b1_g, sw_col + p.b1_noff, e);
+              tma_load_4d_pair(b_dst + SW_HALF * BK * 2, &map_b3_sw, full_leader, kc, p.b3_g,
+                               sw_col + p.b3_noff, e);
+            } else {
+              tma_load_4d_pair(b_dst, bmap, full_leader, kc, bg, brow, e);
+            }
+          }
           if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -490,10 +680,18 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
       const uint32_t idesc = idesc_f16(kFmt, P_BM, BN);
       int stage = 0;
       uint32_t phase = 0;
-      int i = 0;
-      for (int L = pair; L < total && !*abort_flag; L += npairs, ++i) {
+      for (int i = 0;; ++i) {
+        int L;
+        if (*abort_flag || !tq_take(i, s_tq, tq_full, tq_empty, true, L)) {
+          atomicExch(p.err, kErrTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        if (L < 0) break;
         const int acc = i & 1;
         const uint32_t acc_phase = (i >> 1) & 1;
+        const PairTile t = pair_tile(L, s_tiles, s_offs, p);
+        const uint32_t id = t.nt ? idesc_f16(kFmt, P_BM, t.nt) : idesc;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
           atomicExch(p.err, kErrTimeoutMma);
           *abort_flag = 1;
@@ -510,12 +708,14 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_HALF);
+          const uint32_t x_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t w_addr = smem_u32(sB + stage * B_HALF);
+          const uint32_t a_addr = t.nt ? w_addr : x_addr;
+          const uint32_t b_addr = t.nt ? x_addr : w_addr;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             tc_mma_f16_pair(d_tmem, smem_desc_k_sw128(a_addr + kk * 32),
-                            smem_desc_k_sw128(b_addr + kk * 32), idesc,
+                            smem_desc_k_sw128(b_addr + kk * 32), id,
                             (kb | kk) != 0 ? 1u : 0u);
           }
           tc_commit_pair(&empty[stage], 0x3);
@@ -533,8 +733,19 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
     const int r_in_tile = static_cast<int>(rank) * BM + q * 32 + lane;
     int ec0, ec1;
     epi_cols(p, warp, ec0, ec1);
-    int i = 0;
-    for (int L = pair; L < total && !*abort_flag; L += npairs, ++i) {
+    uint32_t xuse = 0;
+    for (int i = 0;; ++i) {
+      int L = -1, ok = 1;
+      if (lane == 0) {
+        ok = !*abort_flag && tq_take(i, s_tq, tq_full, tq_empty, leader, L);
+        if (!ok) {
+          atomicExch(p.err, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      L = __shfl_sync(0xffffffffu, L, 0);
+      if (!ok || L < 0) break;
       const int acc = i & 1;
       const uint32_t acc_phase = (i >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase)) {
@@ -543,12 +754,21 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
         break;
       }
       tc_fence_after();
-      int e, m, n;
-      decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
-      const int row = s_offs[e] + m * P_BM + r_in_tile;
-      const bool valid = row < s_offs[e + 1];
+      const PairTile t = pair_tile(L, s_tiles, s_offs, p);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      epilogue_rows<T>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1);
+      if (t.nt) {
+        if (!epilogue_swapped<T>(p, t, taddr, static_cast<int>(rank), q, lane, warp < 6 ? 0 : 1,
+                                 xch, xuse)) {
+          atomicExch(p.err, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+          break;
+        }
+      } else {
+        const int row = t.r0 + r_in_tile;
+        const bool valid = row < t.r0 + t.rows;
+        epilogue_rows<T>(p, taddr, row, valid, t.e, p.gated ? t.n * (BN / 2) : t.n * BN, ec0,
+                         ec1);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
@@ -930,13 +1150,14 @@ CUtensorMapDataType tma_dtype(int dt) {
   return dt == kDtBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-// A: [rows, K] row-major, box 128 rows x 64 columns.
-bool make_map_a(CUtensorMap* m, int dt, const void* ptr, int64_t rows, int K) {
+// A: [rows, K] row-major, box box_rows x 64 columns.
+bool make_map_a(CUtensorMap* m, int dt, const void* ptr, int64_t rows, int K,
+                int box_rows = BM) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-  cuuint32_t box[2] = {BK, BM};
+  cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
   return enc(m, tma_dtype(dt), 2, const_cast<void*>(ptr), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -944,8 +1165,9 @@ bool make_map_a(CUtensorMap* m, int dt, const void* ptr, int64_t rows, int K) {
          CUDA_SUCCESS;
 }
 
-// B: weights of all experts viewed as [E][Nrows/G][G][K], box 1 x 128 x 1 x 64.
-bool make_map_b(CUtensorMap* m, int dt, const GemmOperandB& b, int K, int E) {
+// B: weights of all experts viewed as [E][Nrows/G][G][K], box 1 x box_rows x 1 x 64.
+bool make_map_b(CUtensorMap* m, int dt, const GemmOperandB& b, int K, int E,
+                int box_rows = BN / 2) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const cuuint64_t rows_g = static_cast<cuuint64_t>(b.n_rows / b.G);
@@ -954,7 +1176,7 @@ bool make_map_b(CUtensorMap* m, int dt, const GemmOperandB& b, int K, int E) {
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(K) * 2,
                            static_cast<cuuint64_t>(K) * 2 * b.G,
                            static_cast<cuuint64_t>(K) * 2 * b.n_rows};
-  cuuint32_t box[4] = {BK, 1, BN / 2, 1};
+  cuuint32_t box[4] = {BK, 1, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   return enc(m, tma_dtype(dt), 4, const_cast<void*>(b.ptr), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -993,6 +1215,17 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   p.ldo = g.ldo;
   p.err = g.err;
   p.test_stall = g.test_stall;
+  p.swap_max = pair ? std::max(0, std::min(g.swap_max, kPairSwapLimit)) / 16 * 16 : 0;
+  p.tile_counter = pair ? g.tile_counter : nullptr;
+  CUtensorMap ma_sw = ma, mb1_sw = mb1, mb3_sw = mb3;
+  if (p.swap_max > 0) {
+    if (!make_map_a(&ma_sw, g.dtype, g.a, g.rows, g.K, SW_TOK_ROWS)) return cudaErrorInvalidValue;
+    if (g.gated) {
+      if (!make_map_b(&mb1_sw, g.dtype, g.b1, g.K, g.E, SW_HALF) ||
+          !make_map_b(&mb3_sw, g.dtype, g.b3, g.K, g.E, SW_HALF))
+        return cudaErrorInvalidValue;
+    }
+  }
   // The attribute call is idempotent; a race between first callers is benign.
   static bool attr_set[2] = {false, false};
   if (!attr_set[pair]) {
@@ -1011,7 +1244,7 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   if (pair) {
     const int64_t pairs = std::min<int64_t>(ub, num_sms / 2);
     tc_pair_grouped_gemm_kernel<T><<<static_cast<int>(2 * pairs), THREADS, P_SMEM_BYTES, s>>>(
-        ma, mb1, mb3, p);
+        ma, mb1, mb3, ma_sw, mb1_sw, mb3_sw, p);
   } else {
     const int grid = static_cast<int>(std::min<int64_t>(ub, num_sms));
     tc_grouped_gemm_kernel<T><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb1, mb3, p);

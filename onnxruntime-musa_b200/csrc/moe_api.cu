@@ -238,11 +238,14 @@ GemmArgs fc2_args(const moe_b200_problem& p, const void* w2, const void* b2) {
 }
 
 // MOE_B200_FORCE_SIMT=1 selects the FFMA GEMMs; MOE_B200_TC_MODE=1|2 forces the
-// single-CTA or CTA-pair tensor-core kernel (used by tests to cover both).
+// single-CTA or CTA-pair tensor-core kernel (used by tests to cover both);
+// MOE_B200_PAIR_SWAP_MAX overrides the swapped-tail-tile limit.
 cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
   if (!env_flag("MOE_B200_FORCE_SIMT") && tc_supported(g)) {
     const char* m = std::getenv("MOE_B200_TC_MODE");
     const int mode = m ? std::atoi(m) : 0;
+    // MOE_B200_PAIR_SWAP_MAX: row limit of the pair kernel's swapped tail tiles (0 = off).
+    if (const char* sw = std::getenv("MOE_B200_PAIR_SWAP_MAX")) g.swap_max = std::atoi(sw);
     return launch_gemm_tc(g, device_sm_count(), mode, s);
   }
   return launch_gemm_simt(g, s);
@@ -306,7 +309,8 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   void* xp = ws + L.xp;
   void* act = ws + L.act;
 
-  MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, sizeof(int), s), "clear error word");
+  // err[0]: device error word; err[1], err[2]: tile counters of the fc1 / fc2 GEMMs.
+  MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, 4 * sizeof(int), s), "clear error word");
   const size_t es = dtype_bytes(p.dtype);
   const int chunk = layer_route_chunk(T);
   if (given_idx != nullptr) {
@@ -395,6 +399,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g1.out = act;
   g1.ldo = I;
   g1.err = err;
+  g1.tile_counter = err + 1;
   // MOE_B200_TEST_STALL=1 (tests only): the GEMM producers issue no loads, the kernel's
   // bounded waits expire and the call reports the device error instead of hanging.
   g1.test_stall = env_flag("MOE_B200_TEST_STALL") ? 1 : 0;
@@ -418,6 +423,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g2.out = xp;  // Y aliases the gathered input, dead after fc1
   g2.ldo = H;
   g2.err = err;
+  g2.tile_counter = err + 2;
   g2.test_stall = g1.test_stall;
   if (fused_q) set_quantized(p, g2, t.fc2_scales, nullptr);
   mark(kStFc2);
@@ -488,6 +494,26 @@ int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tenso
     for (int i = 0; i < kNumStages; ++i) stage_ms[i] = 0.f;
   }
   for (int i = 0; i <= kNumStages; ++i) cudaEventDestroy(ev[i]);
+  return st;
+}
+
+int moe_b200_forward_staged(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                            void* workspace, size_t workspace_bytes, void* stream,
+                            void* const* events, int32_t num_events) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  if (t == nullptr || events == nullptr || num_events < kNumStages + 1)
+    return fail(MOE_B200_INVALID_ARGUMENT, "tensors/events NULL or num_events < %d",
+                kNumStages + 1);
+  cudaEvent_t ev[kNumStages + 1];
+  for (int i = 0; i <= kNumStages; ++i) {
+    if (events[i] == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "events[%d] is NULL", i);
+    ev[i] = static_cast<cudaEvent_t>(events[i]);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = forward_impl(*problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes, s, ev);
+  if (st == MOE_B200_OK && problem->num_rows == 0)
+    for (int i = 0; i <= kNumStages; ++i) MOE_CUDA_CHECK(cudaEventRecord(ev[i], s), "event");
   return st;
 }
 

@@ -35,6 +35,8 @@ constexpr int kMaxExperts = 256;
 constexpr int kMaxK = 32;
 // Routed rows (T*k) up to which routing and the dispatch plan run in one CTA.
 constexpr int kSmallDispatchRows = 1024;
+// Default row limit of the CTA-pair kernel's swapped tail tiles (multiple of 16, <= 240).
+constexpr int kPairSwapMax = 128;
 
 cudaError_t launch_route(int dtype, const void* logits, int T, int E, int k, int normalize,
                          int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s,
@@ -95,6 +97,12 @@ struct GemmArgs {
   int qbits = 0;               // 4 / 8: B operands are packed codes (b*.scales set)
   int qblock = 0;              // scale block along K (0 = one scale per row)
   int test_stall = 0;          // test hook: tensor-core producers issue nothing
+  // CTA-pair kernel: the last tile of an expert with at most this many rows runs with the
+  // operands swapped (weights as M = 256, its rows as N = rows rounded up to 16); 0 = never.
+  int swap_max = kPairSwapMax;
+  // CTA-pair kernel: a zeroed int from which CTA pairs claim tiles in order (dynamic
+  // schedule); nullptr = static round-robin.
+  int* tile_counter = nullptr;
 };
 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);

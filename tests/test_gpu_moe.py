@@ -333,3 +333,81 @@ def test_qmoe_prefill_fused_dequant(pkg, orc, dev, case):
         del os.environ["MOE_B200_QMOE_DEQUANT"]
     np.testing.assert_allclose(as_np(out2), ref, **TOL["float16"])
     np.testing.assert_allclose(as_np(out), as_np(out2), rtol=1e-2, atol=1e-3)
+
+
+# Per-expert row counts around the 16-row granularity and the 128 / 256 tile sizes of the
+# CTA-pair kernel: tails of 1..16 rows, exactly 128, one past 128 / 256, and an empty expert.
+SWAP_COUNTS = [1, 15, 16, 17, 0, 127, 128, 129, 255, 256, 257, 391, 496]
+
+
+@pytest.mark.parametrize("swap_max", ["0", "16", "128", "240"], ids=["off", "16", "128", "240"])
+@pytest.mark.parametrize("variant", ["silu_bias_f16", "gelu_plain_bias_bf16",
+                                     "swiglu_interleaved_f16", "swiglu_halves_bf16"])
+def test_pair_kernel_swapped_tail_tiles(pkg, orc, dev, swap_max, variant):
+    """CTA-pair kernel with the ragged last tile of each expert computed swapped (weights as
+    M, rows as N) up to `swap_max` rows, against the oracle on exact per-expert counts."""
+    counts = SWAP_COUNTS
+    E, T, H, I, k = len(counts), sum(counts), 320, 200, 1
+    act = {"silu_bias_f16": "silu", "gelu_plain_bias_bf16": "gelu"}.get(variant, "swiglu")
+    gated = variant != "gelu_plain_bias_bf16"
+    dtype_name = "bfloat16" if variant.endswith("bf16") else "float16"
+    inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act=act, gated=gated, dtype="float32",
+                              bias=True, normalize=1, seed=int(swap_max) + len(variant))
+    owner = np.repeat(np.arange(E), counts)
+    np.random.default_rng(3).shuffle(owner)
+    lg = inp["router_probs"] * 0.1
+    lg[np.arange(T), owner] += 4.0
+    inp["router_probs"] = lg
+    attrs = dict(inp["attrs"])
+    if act == "swiglu":
+        fusion = 1 if "interleaved" in variant else 2
+        w1, w3, b1, b3 = inp["fc1_w"], inp["fc3_w"], inp["fc1_b"], inp["fc3_b"]
+        if fusion == 1:
+            W = np.empty((E, 2 * I, H), np.float32); W[:, 0::2] = w1; W[:, 1::2] = w3
+            B = np.empty((E, 2 * I), np.float32); B[:, 0::2] = b1; B[:, 1::2] = b3
+            inp.update(fc1_w=W, fc1_b=B)
+        else:
+            inp.update(fc1_w=np.concatenate([w1, w3], 1), fc1_b=np.concatenate([b1, b3], 1))
+        inp.update(fc3_w=None, fc3_b=None)
+        attrs.update(swiglu_fusion=fusion, activation_alpha=1.702, activation_beta=1.0,
+                     swiglu_limit=7.0)
+    d, h = moe_inputs_on(dev, inp, dtype_name)
+    idx, _ = pkg.route(d["router_probs"], k, 1)
+    np.testing.assert_array_equal(np.bincount(idx.cpu().numpy().ravel(), minlength=E), counts)
+    os.environ.update(MOE_B200_TC_MODE="2", MOE_B200_PAIR_SWAP_MAX=swap_max)
+    try:
+        out = run_moe(pkg, d, attrs)
+    finally:
+        del os.environ["MOE_B200_TC_MODE"], os.environ["MOE_B200_PAIR_SWAP_MAX"]
+    np.testing.assert_allclose(as_np(out), oracle_out(orc, h, attrs), **TOL[dtype_name])
+
+
+def test_stage_timing_entries(pkg, orc, dev):
+    """forward_timed and forward_staged compute the same layer as forward and report
+    non-negative stage times whose sum brackets the whole call."""
+    import torch
+    inp = orc.make_moe_inputs(T=512, H=256, I=384, E=8, k=2, act="silu", gated=True,
+                              dtype="float32", seed=91)
+    d, h = moe_inputs_on(dev, inp, "float16")
+    ref = oracle_out(orc, h, inp["attrs"])
+    out = torch.empty_like(d["x"])
+    prob = pkg.make_problem(512, 256, 384, 8, pkg.FLOAT16, has_fc3=True, **inp["attrs"])
+    tens = dict(input=d["x"], router_probs=d["router_probs"], fc1_weights=d["fc1_w"],
+                fc2_weights=d["fc2_w"], fc3_weights=d["fc3_w"], output=out)
+    ws = torch.empty(pkg.workspace_size(prob), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ms = pkg.forward_timed(prob, tens, ws, stream)
+    assert set(ms) == set(pkg.STAGES) and min(ms.values()) >= 0
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+    out.zero_()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(pkg.STAGES) + 1)]
+    for ev in evs:
+        ev.record(stream)
+    pkg.forward_staged(prob, tens, ws, evs, stream)
+    torch.cuda.synchronize(dev)
+    parts = [evs[i].elapsed_time(evs[i + 1]) for i in range(len(pkg.STAGES))]
+    assert min(parts) >= 0
+    assert abs(sum(parts) - evs[0].elapsed_time(evs[-1])) < 1e-3
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+    with pytest.raises(pkg.InvalidArgument):
+        pkg.forward_staged(prob, tens, ws, evs[:3], stream)
