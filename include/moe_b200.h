@@ -264,6 +264,32 @@ int moe_b200_notification_destroy(void* event);
 int moe_b200_copy(void* dst, const void* src, size_t bytes, int32_t kind,
                   void* stream);
 
+/* ------------------------------------------------ host-buffer call pipeline */
+
+/* Calls of one layer on host-resident input, router logits and output (weights stay on
+ * the device).  A session run with CPU inputs does this through the data transfer
+ * (musa/ep/src/ep_data_transfer.cc:108-161) and, with do_copy_in_default_stream = 0,
+ * separate copy streams ordered by notifications (musa/ep/src/ep_stream.cc:30-185):
+ * here a copy-in stream, a compute stream and a copy-out stream with `depth` device
+ * staging slots, so the copies of neighbouring calls overlap the compute of this one. */
+typedef struct moe_b200_pipeline moe_b200_pipeline;
+
+/* problem->num_rows is the largest call; `weights` holds the device weight/scale/bias
+ * pointers (its input, router_probs and output are ignored); depth in [1, 8]. */
+int moe_b200_pipeline_create(const moe_b200_problem* problem,
+                             const moe_b200_tensors* weights, int32_t depth,
+                             moe_b200_pipeline** pipeline);
+/* Enqueues one call: H2D of host_input [num_rows, H] and host_router_probs
+ * [num_rows, E], the layer, D2H into host_output [num_rows, H].  Never blocks the host;
+ * the buffers must stay valid until moe_b200_pipeline_synchronize.  Pinned host memory
+ * (moe_b200_alloc_pinned) lets the copies run asynchronously. */
+int moe_b200_pipeline_submit(moe_b200_pipeline* pipeline, const void* host_input,
+                             const void* host_router_probs, void* host_output,
+                             int64_t num_rows);
+/* Waits for every submitted call (host outputs complete). */
+int moe_b200_pipeline_synchronize(moe_b200_pipeline* pipeline);
+int moe_b200_pipeline_destroy(moe_b200_pipeline* pipeline);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

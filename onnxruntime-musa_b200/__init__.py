@@ -114,6 +114,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                               _VP, _SZ, _VP, _PF, _I32]),
     "moe_b200_forward_staged": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                                _VP, _SZ, _VP, ctypes.POINTER(_VP), _I32]),
+    "moe_b200_pipeline_create": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
+                                                _I32, ctypes.POINTER(_VP)]),
+    "moe_b200_pipeline_submit": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I64]),
+    "moe_b200_pipeline_synchronize": (ctypes.c_int, [_VP]),
+    "moe_b200_pipeline_destroy": (ctypes.c_int, [_VP]),
     "moe_b200_ep_dispatch": (ctypes.c_int, [ctypes.POINTER(Problem), _VP, _VP, _VP, _VP, _VP,
                                             _VP, _VP, _SZ, _VP]),
     "moe_b200_expert_ffn": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors), _VP,
@@ -453,6 +458,52 @@ def forward_staged(problem: Problem, tensors: Mapping[str, Any], workspace, even
     check(lib().moe_b200_forward_staged(ctypes.byref(problem), ctypes.byref(t),
                                         workspace.data_ptr(), workspace.numel(),
                                         _stream_handle(stream), handles, len(events)))
+
+
+class Pipeline:
+    """Calls of one layer on host tensors (``moe_b200_pipeline_*``): inputs and outputs in
+    pinned host memory, weights on the device.  ``submit`` enqueues a call and returns;
+    the H2D copy of the next call and the D2H copy of the previous one overlap the
+    compute of this one.  Host tensors must stay alive until :meth:`synchronize`."""
+
+    def __init__(self, problem: Problem, weights: Mapping[str, Any], depth: int = 2):
+        t = Tensors()
+        for name, _ in Tensors._fields_:
+            v = weights.get(name)
+            setattr(t, name, None if v is None else (v if isinstance(v, int) else v.data_ptr()))
+        self._weights = dict(weights)  # keeps the device tensors alive
+        self._max_rows = problem.num_rows
+        h = _VP()
+        check(lib().moe_b200_pipeline_create(ctypes.byref(problem), ctypes.byref(t), depth,
+                                             ctypes.byref(h)))
+        self._h = h
+
+    def submit(self, host_input, host_router_probs, host_output) -> None:
+        rows = host_input.shape[0] if host_input.dim() == 2 else host_input.numel() // \
+            host_input.shape[-1]
+        check(lib().moe_b200_pipeline_submit(self._h, host_input.data_ptr(),
+                                             host_router_probs.data_ptr(),
+                                             host_output.data_ptr(), rows))
+
+    def synchronize(self) -> None:
+        check(lib().moe_b200_pipeline_synchronize(self._h))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().moe_b200_pipeline_destroy(self._h))
+            self._h = _VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ------------------------------------------------------------------ stages
