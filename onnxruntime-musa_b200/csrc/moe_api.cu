@@ -310,13 +310,15 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   void* act = ws + L.act;
 
   // err[0]: device error word; err[1], err[2]: tile counters of the fc1 / fc2 GEMMs.
-  MOE_CUDA_CHECK(cudaMemsetAsync(err, 0, 4 * sizeof(int), s), "clear error word");
+  // Zeroed by the call's first kernel (route, small dispatch or unit-weight fill): a
+  // memset here would put a copy-engine operation between the previous call's kernels
+  // and this one's.
   const size_t es = dtype_bytes(p.dtype);
   const int chunk = layer_route_chunk(T);
   if (given_idx != nullptr) {
     // Supplied routing: unit weights, histogram and plan of the given expert ids.
     mark(kStRoute);
-    MOE_CUDA_CHECK(launch_fill_f32(w, 1.0f, R, s), "unit weights");
+    MOE_CUDA_CHECK(launch_fill_f32(w, 1.0f, R, s, err), "unit weights");
     MOE_CUDA_CHECK(launch_histogram(given_idx, T, 1, E, cc, err, s, chunk), "histogram");
     mark(kStPlan);
     MOE_CUDA_CHECK(launch_plan(given_idx, T, 1, E, cc, cb, offs, t128, t64, t256, pos, src, s,
@@ -343,7 +345,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
     mark(kStRoute);
     MOE_CUDA_CHECK(launch_small_dispatch(p.dtype, t.router_probs, T, E, k,
                                          p.attrs.normalize_routing_weights, idx, w, offs, pos,
-                                         src, s),
+                                         src, s, err),
                    "route");
     mark(kStPlan);
     mark(kStGather);
@@ -363,7 +365,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   if (given_idx == nullptr) {
     mark(kStRoute);
     MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
-                                p.attrs.normalize_routing_weights, idx, w, cc, s, chunk),
+                                p.attrs.normalize_routing_weights, idx, w, cc, s, chunk, err),
                    "route");
     mark(kStPlan);
     MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s, chunk),

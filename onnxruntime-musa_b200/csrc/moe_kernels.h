@@ -38,14 +38,18 @@ constexpr int kSmallDispatchRows = 1024;
 // Default row limit of the CTA-pair kernel's swapped tail tiles (multiple of 16, <= 240).
 constexpr int kPairSwapMax = 128;
 
+// Words of a layer call's status block (error word + GEMM tile counters) that the first
+// kernel of the call zeroes (`clear`, nullable): no separate memset in the stream.
+constexpr int kClearWords = 4;
 cudaError_t launch_route(int dtype, const void* logits, int T, int E, int k, int normalize,
                          int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s,
-                         int chunk = kRouteChunk);
+                         int chunk = kRouteChunk, int* clear = nullptr);
 // Routing + offsets + permutation of a call with T*k <= kSmallDispatchRows, one CTA
 // (no GEMM tile prefixes: for the decode kernels only).
 cudaError_t launch_small_dispatch(int dtype, const void* logits, int T, int E, int k,
                                   int normalize, int32_t* idx, float* w, int32_t* offsets,
-                                  int32_t* pos, int32_t* src, cudaStream_t s);
+                                  int32_t* pos, int32_t* src, cudaStream_t s,
+                                  int* clear = nullptr);
 cudaError_t launch_histogram(const int32_t* idx, int T, int k, int E, int32_t* chunk_counts,
                              int* err, cudaStream_t s, int chunk = kRouteChunk);
 cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* chunk_counts,
@@ -54,7 +58,8 @@ cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* 
                         cudaStream_t s, int chunk = kRouteChunk);
 cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
                           int64_t rows, void* xp, cudaStream_t s);
-cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s);
+cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s,
+                            int* clear = nullptr);
 cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
                            int T, int k, int H, void* out, cudaStream_t s);
 

@@ -80,8 +80,9 @@ template <typename T, int kPerLane>
 __global__ void __launch_bounds__(kRouteThreads)
 route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int normalize,
              int32_t* __restrict__ expert_idx, float* __restrict__ route_w,
-             int32_t* __restrict__ chunk_counts, int chunk) {
+             int32_t* __restrict__ chunk_counts, int chunk, int* __restrict__ clear) {
   extern __shared__ int32_t s_counts[];  // [E]
+  if (clear != nullptr && blockIdx.x == 0 && threadIdx.x < kClearWords) clear[threadIdx.x] = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_counts[e] = 0;
   __syncthreads();
 
@@ -113,8 +114,9 @@ __global__ void __launch_bounds__(1024)
 small_dispatch_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int normalize,
                       int32_t* __restrict__ expert_idx, float* __restrict__ route_w,
                       int32_t* __restrict__ expert_offsets, int32_t* __restrict__ permuted_pos,
-                      int32_t* __restrict__ permuted_src) {
+                      int32_t* __restrict__ permuted_src, int* __restrict__ clear) {
   __shared__ int32_t s_idx[kSmallDispatchRows];
+  if (clear != nullptr && threadIdx.x < kClearWords) clear[threadIdx.x] = 0;
   __shared__ int32_t s_cnt[kMaxExperts + 1];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -330,47 +332,49 @@ combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ permuted_pos
   }
 }
 
-__global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n) {
+__global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n,
+                                int* __restrict__ clear) {
+  if (clear != nullptr && blockIdx.x == 0 && threadIdx.x < kClearWords) clear[threadIdx.x] = 0;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     dst[i] = v;
 }
 
 // ------------------------------------------------------------------ launchers
-cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s) {
+cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s, int* clear) {
   if (n == 0) return cudaSuccess;
   const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 1184));
-  fill_f32_kernel<<<blocks, 256, 0, s>>>(dst, value, n);
+  fill_f32_kernel<<<blocks, 256, 0, s>>>(dst, value, n, clear);
   return cudaGetLastError();
 }
 
 template <typename T>
 static cudaError_t launch_route_t(const void* logits, int T_, int E, int k, int normalize,
                                   int32_t* idx, float* w, int32_t* chunk_counts,
-                                  cudaStream_t s, int chunk) {
+                                  cudaStream_t s, int chunk, int* clear) {
   const int chunks = num_route_chunks(T_, chunk);
   const size_t sm = static_cast<size_t>(E) * sizeof(int32_t);
   const T* l = static_cast<const T*>(logits);
   const int per_lane = (E + 31) / 32;
   if (per_lane <= 1)
-    route_kernel<T, 1><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
+    route_kernel<T, 1><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   else if (per_lane <= 2)
-    route_kernel<T, 2><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
+    route_kernel<T, 2><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   else if (per_lane <= 4)
-    route_kernel<T, 4><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
+    route_kernel<T, 4><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   else
-    route_kernel<T, 8><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk);
+    route_kernel<T, 8><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   return cudaGetLastError();
 }
 
 cudaError_t launch_route(int dtype, const void* logits, int T_, int E, int k, int normalize,
                          int32_t* idx, float* w, int32_t* chunk_counts, cudaStream_t s,
-                         int chunk) {
+                         int chunk, int* clear) {
   if (T_ == 0) return cudaSuccess;
   switch (dtype) {
-    case kDtF32: return launch_route_t<float>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk);
-    case kDtF16: return launch_route_t<__half>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk);
-    case kDtBF16: return launch_route_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk);
+    case kDtF32: return launch_route_t<float>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk, clear);
+    case kDtF16: return launch_route_t<__half>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk, clear);
+    case kDtBF16: return launch_route_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, chunk_counts, s, chunk, clear);
   }
   return cudaErrorInvalidValue;
 }
@@ -378,28 +382,28 @@ cudaError_t launch_route(int dtype, const void* logits, int T_, int E, int k, in
 template <typename T>
 static cudaError_t launch_small_dispatch_t(const void* logits, int T_, int E, int k, int normalize,
                                            int32_t* idx, float* w, int32_t* offsets, int32_t* pos,
-                                           int32_t* src, cudaStream_t s) {
+                                           int32_t* src, cudaStream_t s, int* clear) {
   const T* l = static_cast<const T*>(logits);
   const int per_lane = (E + 31) / 32;
   if (per_lane <= 1)
-    small_dispatch_kernel<T, 1><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+    small_dispatch_kernel<T, 1><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src, clear);
   else if (per_lane <= 2)
-    small_dispatch_kernel<T, 2><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+    small_dispatch_kernel<T, 2><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src, clear);
   else if (per_lane <= 4)
-    small_dispatch_kernel<T, 4><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+    small_dispatch_kernel<T, 4><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src, clear);
   else
-    small_dispatch_kernel<T, 8><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src);
+    small_dispatch_kernel<T, 8><<<1, 1024, 0, s>>>(l, T_, E, k, normalize, idx, w, offsets, pos, src, clear);
   return cudaGetLastError();
 }
 
 cudaError_t launch_small_dispatch(int dtype, const void* logits, int T_, int E, int k,
                                   int normalize, int32_t* idx, float* w, int32_t* offsets,
-                                  int32_t* pos, int32_t* src, cudaStream_t s) {
+                                  int32_t* pos, int32_t* src, cudaStream_t s, int* clear) {
   if (T_ == 0) return cudaSuccess;
   switch (dtype) {
-    case kDtF32: return launch_small_dispatch_t<float>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s);
-    case kDtF16: return launch_small_dispatch_t<__half>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s);
-    case kDtBF16: return launch_small_dispatch_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s);
+    case kDtF32: return launch_small_dispatch_t<float>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s, clear);
+    case kDtF16: return launch_small_dispatch_t<__half>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s, clear);
+    case kDtBF16: return launch_small_dispatch_t<__nv_bfloat16>(logits, T_, E, k, normalize, idx, w, offsets, pos, src, s, clear);
   }
   return cudaErrorInvalidValue;
 }
