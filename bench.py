@@ -498,6 +498,7 @@ def bench_ep(args, cfg, rank, world, dev):
         "data": "synthetic (seeded, on-device; config distributions; random init)",
         "config": {"workload": cfg["desc"].format(T=T), "global_batch": T * world,
                    "tokens_per_gpu": T, "parallelism": f"ep{world}", "ep_chunks": chunks,
+                   "ep_transport": layer.transport,
                    "l2": "inputs larger than L2 (weights streamed every step)"},
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": hx.numel() * es + hl.numel() * es,
@@ -508,7 +509,9 @@ def bench_ep(args, cfg, rank, world, dev):
                      "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)"},
         # dispatch (route, scan, permute, gather) + expert FFN (fill, histogram, scan,
         # permute, gather, fc1, fc2, un-permute) + combine
-        "gpu_launches": 13 * chunks * args.steps,
+        # p2p: route, scan, permute, counts, send, signal, wait, fc1, fc2, signal, wait,
+        # combine; collective: 13 per chunk
+        "gpu_launches": (12 if layer.transport == "p2p" else 13 * chunks) * args.steps,
         "clocks": clk.summary(),
     }
 

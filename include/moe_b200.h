@@ -264,6 +264,39 @@ int moe_b200_notification_destroy(void* event);
 int moe_b200_copy(void* dst, const void* src, size_t bytes, int32_t kind,
                   void* stream);
 
+/* --------------------------------------- device-side expert parallelism (P2P) */
+
+/* Expert-parallel layer over the GPUs of one node with no host synchronisation and no
+ * collective library on the data path: rank r of W owns experts [r*E/W, (r+1)*E/W) and
+ * one IPC-shared device region (receive buffer, return buffer, count matrix, flags).
+ * Per call the ranks exchange per-expert counts with peer stores, the dispatch gather
+ * writes routed rows into the owners' receive buffers, the fc2 epilogue writes the FFN
+ * rows back into the senders' return buffers, and flags (bounded waits) order the steps.
+ * The reference EP has no multi-device path (musa/ep/src/ep_factory.cc:466-470); these
+ * entries are the dispatch / combine exchange of the MoE path.  fp16/bf16 MoE only. */
+typedef struct moe_b200_ep_comm moe_b200_ep_comm;
+
+/* Allocates this rank's region for calls of up to max_rows tokens with k <= k_max. */
+int moe_b200_ep_comm_create(int32_t rank, int32_t world, int64_t max_rows, int32_t k_max,
+                            int64_t hidden_size, int64_t num_experts, int32_t dtype,
+                            moe_b200_ep_comm** comm);
+/* Bytes of one rank's IPC handle (cudaIpcMemHandle_t). */
+int moe_b200_ep_comm_handle_size(size_t* bytes);
+int moe_b200_ep_comm_get_handle(moe_b200_ep_comm* comm, void* handle);
+/* handles: world handles in rank order (this rank's own entry is ignored). */
+int moe_b200_ep_comm_connect(moe_b200_ep_comm* comm, const void* handles);
+int moe_b200_ep_comm_destroy(moe_b200_ep_comm* comm);
+/* Workspace of one call (problem: this rank's num_rows, local num_experts = E / W). */
+int moe_b200_ep_workspace_size(const moe_b200_ep_comm* comm,
+                               const moe_b200_problem* problem, size_t* bytes);
+/* One layer call on every rank of the communicator (all ranks call it the same number
+ * of times).  t: this rank's input / router_probs [T, E] / output and its local weights
+ * ([E/W, ...]).  A peer that does not take part makes the waits expire after 2 s with
+ * device error code 6 in the workspace's error word. */
+int moe_b200_ep_forward(moe_b200_ep_comm* comm, const moe_b200_problem* problem,
+                        const moe_b200_tensors* t, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 /* ------------------------------------------------ host-buffer call pipeline */
 
 /* Calls of one layer on host-resident input, router logits and output (weights stay on

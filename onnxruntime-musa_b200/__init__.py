@@ -114,6 +114,16 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                               _VP, _SZ, _VP, _PF, _I32]),
     "moe_b200_forward_staged": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                                _VP, _SZ, _VP, ctypes.POINTER(_VP), _I32]),
+    "moe_b200_ep_comm_create": (ctypes.c_int, [_I32, _I32, _I64, _I32, _I64, _I64, _I32,
+                                               ctypes.POINTER(_VP)]),
+    "moe_b200_ep_comm_handle_size": (ctypes.c_int, [ctypes.POINTER(_SZ)]),
+    "moe_b200_ep_comm_get_handle": (ctypes.c_int, [_VP, _VP]),
+    "moe_b200_ep_comm_connect": (ctypes.c_int, [_VP, _VP]),
+    "moe_b200_ep_comm_destroy": (ctypes.c_int, [_VP]),
+    "moe_b200_ep_workspace_size": (ctypes.c_int, [_VP, ctypes.POINTER(Problem),
+                                                  ctypes.POINTER(_SZ)]),
+    "moe_b200_ep_forward": (ctypes.c_int, [_VP, ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
+                                           _VP, _SZ, _VP]),
     "moe_b200_pipeline_create": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                                 _I32, ctypes.POINTER(_VP)]),
     "moe_b200_pipeline_submit": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I64]),
@@ -458,6 +468,56 @@ def forward_staged(problem: Problem, tensors: Mapping[str, Any], workspace, even
     check(lib().moe_b200_forward_staged(ctypes.byref(problem), ctypes.byref(t),
                                         workspace.data_ptr(), workspace.numel(),
                                         _stream_handle(stream), handles, len(events)))
+
+
+class EpComm:
+    """This rank's region of the device-side expert-parallel exchange
+    (``moe_b200_ep_comm_*``).  ``handle()`` is exported to the other ranks, whose handles
+    (rank order) are passed to ``connect``."""
+
+    def __init__(self, rank: int, world: int, max_rows: int, k_max: int, hidden_size: int,
+                 num_experts: int, dtype: int):
+        h = _VP()
+        check(lib().moe_b200_ep_comm_create(rank, world, max_rows, k_max, hidden_size,
+                                            num_experts, dtype, ctypes.byref(h)))
+        self._h = h
+        self.max_rows, self.k_max = max_rows, k_max
+
+    def handle(self) -> bytes:
+        n = _SZ()
+        check(lib().moe_b200_ep_comm_handle_size(ctypes.byref(n)))
+        buf = ctypes.create_string_buffer(n.value)
+        check(lib().moe_b200_ep_comm_get_handle(self._h, buf))
+        return buf.raw
+
+    def connect(self, handles: Sequence[bytes]) -> None:
+        blob = b"".join(handles)
+        check(lib().moe_b200_ep_comm_connect(self._h, ctypes.c_char_p(blob)))
+
+    def workspace_size(self, problem: Problem) -> int:
+        n = _SZ()
+        check(lib().moe_b200_ep_workspace_size(self._h, ctypes.byref(problem), ctypes.byref(n)))
+        return n.value
+
+    def forward(self, problem: Problem, tensors: Mapping[str, Any], workspace, stream=None):
+        t = Tensors()
+        for name, _ in Tensors._fields_:
+            v = tensors.get(name)
+            setattr(t, name, None if v is None else (v if isinstance(v, int) else v.data_ptr()))
+        check(lib().moe_b200_ep_forward(self._h, ctypes.byref(problem), ctypes.byref(t),
+                                        workspace.data_ptr(), workspace.numel(),
+                                        _stream_handle(stream)))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().moe_b200_ep_comm_destroy(self._h))
+            self._h = _VP()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Pipeline:

@@ -24,6 +24,7 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 3,
   kErrBadExpert = 4,
   kErrBadRow = 5,
+  kErrTimeoutPeer = 6,   // a peer rank's flag did not arrive (expert-parallel exchange)
 };
 
 // Wall-time bound of one mbarrier wait.

@@ -74,7 +74,27 @@ struct TcParams {
   // CTA-pair kernel: zeroed counter from which pairs claim tiles in order (dynamic
   // schedule); nullptr = static round-robin.
   int* tile_counter;
+  // Output row remap (expert-parallel return over peer memory): row p of segment q
+  // (seg_start[q] <= p < seg_start[q+1]) goes to row seg_dst[q] + p - seg_start[q] of
+  // out_peers[q % remap_world]; seg_start == nullptr: row p of `out`.
+  const int32_t* seg_start;
+  const int32_t* seg_dst;
+  int nseg;
+  int remap_world;
+  void* out_peers[kMaxEpRanks];
 };
+
+template <typename T>
+__device__ __forceinline__ T* out_row(const TcParams& p, int row) {
+  if (p.seg_start == nullptr) return static_cast<T*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+  int lo = 0, hi = p.nseg - 1;  // the last segment starting at or before `row`
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(&p.seg_start[mid]) <= row) lo = mid; else hi = mid - 1;
+  }
+  const int dst = __ldg(&p.seg_dst[lo]) + row - __ldg(&p.seg_start[lo]);
+  return static_cast<T*>(p.out_peers[lo % p.remap_world]) + static_cast<int64_t>(dst) * p.ldo;
+}
 
 __device__ __forceinline__ void decode_tile(int L, const int32_t* s_tiles, int E, int n_tiles,
                                             int& e, int& m, int& n) {
@@ -148,7 +168,7 @@ __device__ __forceinline__ float fast_act_gated(const ActParams& p, float g, flo
 template <typename T>
 __device__ __forceinline__ void epilogue_rows(const TcParams& p, uint32_t taddr, int row,
                                               bool valid, int e, int n0, int c0, int c1) {
-  T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+  T* orow = valid ? out_row<T>(p, row) : nullptr;
   const bool has_b1 = p.bias1 != nullptr, has_b3 = p.bias3 != nullptr;
   if (p.gated) {
 #pragma unroll 1
@@ -438,7 +458,6 @@ template <typename T>
 __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTile& t,
                                                  uint32_t taddr, int rank, int q, int lane,
                                                  int half, const Exchange& x, uint32_t& xuse) {
-  T* out = static_cast<T*>(p.out);
   const int c_first = 16 * half;
   if (p.gated) {
     const bool lin = q >= 2;
@@ -469,8 +488,7 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
         for (int j = 0; j < 16; ++j) {
           const int tok = c + j;
           if (fok && tok < t.rows)
-            out[static_cast<int64_t>(t.r0 + tok) * p.ldo + f] =
-                from_f<T>(fast_act_gated(p.ap, v[j] + own_bias, u[j]));
+            out_row<T>(p, t.r0 + tok)[f] = from_f<T>(fast_act_gated(p.ap, v[j] + own_bias, u[j]));
         }
       }
     }
@@ -483,12 +501,14 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
       float v[16];
       tmem_ld16(taddr + c, v);
       tmem_ld_wait();
+      // Lane j < 16 resolves the output row of row c + j once for the warp.
+      const int my_tok = c + (lane & 15);
+      const unsigned long long my_row =
+          my_tok < t.rows ? reinterpret_cast<unsigned long long>(out_row<T>(p, t.r0 + my_tok)) : 0ull;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int tok = c + j;
-        if (fok && tok < t.rows)
-          out[static_cast<int64_t>(t.r0 + tok) * p.ldo + f] =
-              from_f<T>(fast_act_single(p.ap.act, v[j] + b));
+        T* row = reinterpret_cast<T*>(__shfl_sync(0xffffffffu, my_row, j));
+        if (fok && c + j < t.rows) row[f] = from_f<T>(fast_act_single(p.ap.act, v[j] + b));
       }
     }
   }
@@ -1217,6 +1237,11 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   p.test_stall = g.test_stall;
   p.swap_max = pair ? std::max(0, std::min(g.swap_max, kPairSwapLimit)) / 16 * 16 : 0;
   p.tile_counter = pair ? g.tile_counter : nullptr;
+  p.seg_start = g.seg_start;
+  p.seg_dst = g.seg_dst;
+  p.nseg = g.nseg;
+  p.remap_world = g.remap_world;
+  for (int i = 0; i < kMaxEpRanks; ++i) p.out_peers[i] = g.out_peers[i];
   CUtensorMap ma_sw = ma, mb1_sw = mb1, mb3_sw = mb3;
   if (p.swap_max > 0) {
     if (!make_map_a(&ma_sw, g.dtype, g.a, g.rows, g.K, SW_TOK_ROWS)) return cudaErrorInvalidValue;

@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "../../include/moe_b200.h"
+#include "ep_p2p.h"
 #include "moe_kernels.h"
 #include "qmoe.h"
 
@@ -246,6 +247,8 @@ cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
     const int mode = m ? std::atoi(m) : 0;
     // MOE_B200_PAIR_SWAP_MAX: row limit of the pair kernel's swapped tail tiles (0 = off).
     if (const char* sw = std::getenv("MOE_B200_PAIR_SWAP_MAX")) g.swap_max = std::atoi(sw);
+    // MOE_B200_PAIR_STATIC=1: static round-robin tile schedule (comparison runs).
+    if (env_flag("MOE_B200_PAIR_STATIC")) g.tile_counter = nullptr;
     return launch_gemm_tc(g, device_sm_count(), mode, s);
   }
   return launch_gemm_simt(g, s);
@@ -450,7 +453,162 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   return MOE_B200_OK;
 }
 
+// ------------------------------------------------ device-side expert parallelism
+struct EpWsLayout {
+  size_t idx, w, cc, cb, myoff, t128, t64, t256, pos, src, err;
+  size_t send_base, eoff, rt128, rt64, rt256, seg_start, seg_dst, act, total;
+};
+
+EpWsLayout plan_ep_workspace(const moe_b200_ep_comm* c, const moe_b200_problem& p) {
+  EpWsLayout L{};
+  const int64_t T = p.num_rows, E = c->num_experts, k = p.attrs.k, W = c->world, El = E / W;
+  const int64_t R = T * k;
+  const int64_t chunks = std::max<int64_t>(num_route_chunks(T, layer_route_chunk(T)), 1);
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
+  L.idx = take(R * 4);
+  L.w = take(R * 4);
+  L.cc = take(chunks * E * 4);
+  L.cb = take(chunks * E * 4);
+  L.myoff = take((E + 1) * 4);
+  L.t128 = take((E + 1) * 4);
+  L.t64 = take((E + 1) * 4);
+  L.t256 = take((E + 1) * 4);
+  L.pos = take(R * 4);
+  L.src = take(R * 4);
+  L.err = take(16);
+  L.send_base = take(E * 4);
+  L.eoff = take((El + 1) * 4);
+  L.rt128 = take((El + 1) * 4);
+  L.rt64 = take((El + 1) * 4);
+  L.rt256 = take((El + 1) * 4);
+  L.seg_start = take((El * W + 1) * 4);
+  L.seg_dst = take(El * W * 4);
+  L.act = take(static_cast<size_t>(c->cap_rows) * p.inter_size * dtype_bytes(p.dtype));
+  L.total = o;
+  return L;
+}
+
 }  // namespace
+
+namespace moe {
+
+size_t ep_workspace_bytes(const moe_b200_ep_comm* c, const moe_b200_problem& p) {
+  return plan_ep_workspace(c, p).total;
+}
+
+// One layer call of the device-side expert-parallel path: route and plan over all E
+// experts, exchange counts (device), send rows into the owners' receive buffers, expert
+// FFN on the received rows with the fc2 epilogue storing into the senders' return
+// buffers, combine.  Local weights: [E / W, ...].  No host synchronisation.
+int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b200_tensors& t,
+                    uint8_t* ws, size_t ws_bytes, cudaStream_t s) {
+  int st = validate_problem(&p);
+  if (st != MOE_B200_OK) return st;
+  const int W = c->world, E = c->num_experts, El = E / W, r = c->rank;
+  if (p.num_experts != El)
+    return fail(MOE_B200_INVALID_ARGUMENT, "problem.num_experts=%lld must be the local %d",
+                (long long)p.num_experts, El);
+  if (p.dtype != c->dtype || p.hidden_size != c->hidden || p.num_rows > c->max_rows ||
+      p.attrs.k > c->k_max)
+    return fail(MOE_B200_INVALID_ARGUMENT,
+                "problem (dtype %d, hidden %lld, rows %lld, k %d) outside the communicator's "
+                "(dtype %d, hidden %lld, rows <= %lld, k <= %d)",
+                p.dtype, (long long)p.hidden_size, (long long)p.num_rows, p.attrs.k, c->dtype,
+                (long long)c->hidden, (long long)c->max_rows, c->k_max);
+  if (p.attrs.expert_weight_bits != 0)
+    return fail(MOE_B200_NOT_IMPLEMENTED, "device-side expert parallelism runs MoE (not QMoE)");
+  if (p.attrs.k > E) return fail(MOE_B200_INVALID_ARGUMENT, "k=%d > %d experts", p.attrs.k, E);
+  if (t.fc1_weights == nullptr || t.fc2_weights == nullptr || (p.has_fc3 && !t.fc3_weights))
+    return fail(MOE_B200_INVALID_ARGUMENT, "local fc1/fc2(/fc3) weights must be non-NULL");
+  const int T = static_cast<int>(p.num_rows), k = p.attrs.k;
+  const int H = static_cast<int>(p.hidden_size), I = static_cast<int>(p.inter_size);
+  if (T > 0 && (t.input == nullptr || t.router_probs == nullptr || t.output == nullptr))
+    return fail(MOE_B200_INVALID_ARGUMENT, "input, router_probs and output must be non-NULL");
+  const EpWsLayout L = plan_ep_workspace(c, p);
+  if (ws_bytes < L.total || (reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+    return fail(MOE_B200_INVALID_ARGUMENT, "workspace must be 256-byte aligned and >= %zu bytes",
+                L.total);
+  auto i32 = [&](size_t off) { return reinterpret_cast<int32_t*>(ws + off); };
+  int* err = reinterpret_cast<int*>(ws + L.err);
+  const uint32_t epoch = ++c->epoch;
+  const int64_t R = static_cast<int64_t>(T) * k;
+  const int chunk = layer_route_chunk(T);
+  const size_t es = dtype_bytes(p.dtype);
+
+  // Route and plan over all E experts (expert-ordered rows of this rank's tokens).
+  MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
+                              p.attrs.normalize_routing_weights, i32(L.idx),
+                              reinterpret_cast<float*>(ws + L.w), i32(L.cc), s, chunk),
+                 "route");
+  if (T > 0)
+    MOE_CUDA_CHECK(launch_plan(i32(L.idx), T, k, E, i32(L.cc), i32(L.cb), i32(L.myoff),
+                               i32(L.t128), i32(L.t64), i32(L.t256), i32(L.pos), i32(L.src), s,
+                               chunk),
+                   "plan");
+  const EpTables tab{i32(L.send_base), i32(L.eoff), i32(L.rt128), i32(L.rt64), i32(L.rt256),
+                     i32(L.seg_start), i32(L.seg_dst)};
+  MOE_CUDA_CHECK(launch_ep_exchange_counts(c->peers, c->lay, r, W, E, epoch,
+                                           T > 0 ? i32(L.myoff) : nullptr, tab, err, s),
+                 "count exchange");
+  MOE_CUDA_CHECK(launch_ep_send_rows(c->peers, c->lay, W, E, t.input, static_cast<int64_t>(H) * es,
+                                     k, i32(L.idx), i32(L.src), R, tab.send_base, err, s),
+                 "send rows");
+  MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpRows, epoch, s), "signal rows");
+  MOE_CUDA_CHECK(launch_ep_wait(c->sym, c->lay, W, kEpRows, epoch, err, s), "wait rows");
+
+  // Expert FFN on the received rows (row count known on the device only: the GEMMs are
+  // sized for the communicator's capacity and schedule from the device offsets).
+  void* act = ws + L.act;
+  moe_b200_problem pl = p;
+  GemmArgs g1 = fc1_args(pl, t.fc1_weights, t.fc1_bias, t.fc3_weights, t.fc3_bias);
+  g1.a = c->sym + c->lay.recv;
+  g1.rows = c->cap_rows;
+  g1.offsets = tab.eoff;
+  g1.tiles128 = tab.t128;
+  g1.tiles64 = tab.t64;
+  g1.tiles256 = tab.t256;
+  g1.out = act;
+  g1.ldo = I;
+  g1.err = err;
+  g1.tile_counter = err + 1;
+  if (!tc_supported(g1))
+    return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc1: tensor-core path unsupported");
+  MOE_CUDA_CHECK(launch_gemm_tc(g1, device_sm_count(), 2, s), "fc1 grouped GEMM");
+  GemmArgs g2 = fc2_args(pl, t.fc2_weights, t.fc2_bias);
+  g2.a = act;
+  g2.rows = c->cap_rows;
+  g2.offsets = tab.eoff;
+  g2.tiles128 = tab.t128;
+  g2.tiles64 = tab.t64;
+  g2.tiles256 = tab.t256;
+  g2.out = c->sym + c->lay.ret;  // alignment check only: rows go to the senders' buffers
+  g2.ldo = H;
+  g2.err = err;
+  g2.tile_counter = err + 2;
+  g2.seg_start = tab.seg_start;
+  g2.seg_dst = tab.seg_dst;
+  g2.nseg = El * W;
+  g2.remap_world = W;
+  for (int d = 0; d < W; ++d) g2.out_peers[d] = c->peers.base[d] + c->lay.ret;
+  if (!tc_supported(g2))
+    return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc2: tensor-core path unsupported");
+  MOE_CUDA_CHECK(launch_gemm_tc(g2, device_sm_count(), 2, s), "fc2 grouped GEMM");
+  MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpReturn, epoch, s), "signal return");
+  MOE_CUDA_CHECK(launch_ep_wait(c->sym, c->lay, W, kEpReturn, epoch, err, s), "wait return");
+  MOE_CUDA_CHECK(launch_combine(p.dtype, c->sym + c->lay.ret, i32(L.pos),
+                                reinterpret_cast<float*>(ws + L.w), T, k, H, t.output, s),
+                 "combine");
+  if (env_flag("MOE_B200_TRACE_SYNC")) {
+    MOE_CUDA_CHECK(cudaStreamSynchronize(s), "stream synchronize");
+    int herr = 0;
+    MOE_CUDA_CHECK(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+    if (herr != 0) return fail(MOE_B200_EP_FAIL, "device error code %d", herr);
+  }
+  return MOE_B200_OK;
+}
+
+}  // namespace moe
 
 // ==================================================================== C ABI
 extern "C" {

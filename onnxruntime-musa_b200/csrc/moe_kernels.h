@@ -32,6 +32,7 @@ inline int layer_route_chunk(int64_t rows) {
   return static_cast<int>(c < 32 ? 32 : (c > kRouteChunk ? kRouteChunk : c));
 }
 constexpr int kMaxExperts = 256;
+constexpr int kMaxEpRanks = 8;   // expert-parallel ranks (GPUs of one node)
 constexpr int kMaxK = 32;
 // Routed rows (T*k) up to which routing and the dispatch plan run in one CTA.
 constexpr int kSmallDispatchRows = 1024;
@@ -108,6 +109,14 @@ struct GemmArgs {
   // CTA-pair kernel: a zeroed int from which CTA pairs claim tiles in order (dynamic
   // schedule); nullptr = static round-robin.
   int* tile_counter = nullptr;
+  // Tensor-core kernels: output row remap for the expert-parallel return (row p of
+  // segment q, seg_start[q] <= p < seg_start[q+1], is stored at row seg_dst[q] + p -
+  // seg_start[q] of out_peers[q % remap_world]); seg_start == nullptr: rows of `out`.
+  const int32_t* seg_start = nullptr;
+  const int32_t* seg_dst = nullptr;
+  int nseg = 0;
+  int remap_world = 1;
+  void* out_peers[kMaxEpRanks] = {};
 };
 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);

@@ -15,6 +15,12 @@ routing).  One layer call:
 Optionally the tokens go through in chunks whose row all-to-alls run on NCCL's stream while
 another chunk's experts compute (off by default; see :meth:`ExpertParallelMoE.forward`).
 
+Transport "p2p" (the default for fp16/bf16 MoE) replaces steps 2-6 by the device-side
+exchange of the library (``moe_b200_ep_forward``): counts, rows and returned rows move by
+peer stores between IPC-shared regions, ordered by flags with bounded waits, so a layer
+call has no host synchronisation; the fc2 epilogue writes straight into the sender's
+return buffer.
+
 The reference plugin has no parallelism at all (one EP instance drives one device,
 ``musa/ep/src/ep_factory.cc:466-470``); the design follows the plan for the MoE path:
 the split sizes of the variable all-to-all need the counts on the host, which costs one
@@ -62,7 +68,8 @@ class ExpertParallelMoE:
 
     def __init__(self, pkg, *, num_experts: int, hidden_size: int, inter_size: int,
                  dtype: int, has_fc3: bool, local_weights: dict[str, Any], group=None,
-                 backend=None, **attrs):
+                 backend=None, transport: str = "auto", max_rows: int | None = None,
+                 **attrs):
         self.pkg = pkg
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -76,6 +83,22 @@ class ExpertParallelMoE:
         self.k = int(attrs.get("k", 1))
         self.weights = local_weights
         self.backend = backend if backend is not None else CudaBackend(pkg)
+        # "p2p": device-side exchange over peer memory (moe_b200_ep_*: no host sync, no
+        # collective on the data path); "collective": NCCL all-to-all around the device
+        # steps.  "auto" takes p2p for fp16/bf16 MoE on CUDA ranks with the CUDA backend.
+        p2p_ok = (backend is None and dtype in (pkg.FLOAT16, pkg.BFLOAT16)
+                  and int(attrs.get("expert_weight_bits", 0)) == 0
+                  and self.world <= 8 and torch.cuda.is_available())
+        if transport == "auto":
+            transport = "p2p" if p2p_ok else "collective"
+        if transport == "p2p" and not p2p_ok:
+            raise ValueError("the p2p transport needs fp16/bf16 MoE weights on CUDA ranks")
+        if transport not in ("p2p", "collective"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self.max_rows = max_rows
+        self._comm = None
+        self._ws = None
 
     def _problem(self, rows: int, experts: int, k: int):
         a = dict(self.attrs, k=k)
@@ -89,7 +112,58 @@ class ExpertParallelMoE:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
         return out
 
+    # ------------------------------------------------------------- p2p transport
+    def _connect(self, T: int, device) -> None:
+        """Creates this rank's exchange region (same size on every rank: the largest call,
+        agreed by an all-reduce) and opens the other ranks' regions (IPC handles)."""
+        max_rows = self.max_rows
+        if max_rows is None:
+            t = torch.tensor([T], dtype=torch.int64, device=device)
+            if self.world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            max_rows = max(1, int(t.item()))
+        self.max_rows = max_rows
+        comm = self.pkg.EpComm(self.rank, self.world, max_rows, self.k, self.H, self.E,
+                               self.dtype)
+        mine = comm.handle()
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, mine, group=self.group)
+        else:
+            handles = [mine]
+        comm.connect(handles)
+        self._comm = comm
+
+    def _forward_p2p(self, x, router_probs):
+        T = x.shape[0]
+        if self._comm is None:
+            self._connect(T, x.device)
+        if T > self.max_rows:
+            raise ValueError(f"{T} rows exceed the exchange's max_rows={self.max_rows}; "
+                             "construct the layer with a larger max_rows")
+        prob = self._problem(T, self.E_local, self.k)
+        out = torch.empty_like(x)
+        nbytes = self._comm.workspace_size(prob)
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        self._comm.forward(prob, dict(self.weights, input=x, router_probs=router_probs,
+                                      output=out), self._ws)
+        return out
+
+    def close(self) -> None:
+        if self._comm is not None:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)  # no rank frees its region while peers use it
+            self._comm.close()
+            self._comm = None
+
     def forward(self, x, router_probs, chunks: int | None = None):
+        if self.transport == "p2p":
+            return self._forward_p2p(x, router_probs)
+        return self._forward_collective(x, router_probs, chunks)
+
+    def _forward_collective(self, x, router_probs, chunks: int | None = None):
         """x [T, H], router_probs [T, E] -> output [T, H] for this rank's tokens.
 
         With ``chunks`` > 1 the tokens are processed in chunks whose row exchanges run
@@ -125,7 +199,7 @@ class ExpertParallelMoE:
             self._wait(p["h"])
             local_ids = torch.arange(El, device=p["recv"].device, dtype=torch.int32).repeat(W)
             row_expert = torch.repeat_interleave(local_ids, p["recv_counts"].reshape(-1).to(
-                p["recv"].device))
+                p["recv"].device), output_size=p["recv"].shape[0])
             y_recv = self.backend.expert_ffn(self._problem(p["recv"].shape[0], El, 1), p["recv"],
                                              row_expert.to(torch.int32).contiguous(), self.weights)
             p["y_send"] = torch.empty_like(p["send"])

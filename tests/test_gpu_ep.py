@@ -24,13 +24,17 @@ def _moe_case(orc, dev, T, H, I, E, k, seed, dtype):
     return d, weights, inp["attrs"]
 
 
-@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
-def test_ep_single_rank_matches_layer(pkg, orc, dev, dtype):
+@pytest.mark.parametrize("dtype,transport", [("float16", "p2p"), ("bfloat16", "p2p"),
+                                             ("float16", "collective"),
+                                             ("float32", "collective")])
+def test_ep_single_rank_matches_layer(pkg, orc, dev, dtype, transport):
     from onnxruntime_musa_b200 import ep
     d, weights, attrs = _moe_case(orc, dev, 300, 256, 384, 8, 2, 21, dtype)
     et = {"float16": pkg.FLOAT16, "bfloat16": pkg.BFLOAT16, "float32": pkg.FLOAT}[dtype]
     layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=256, inter_size=384, dtype=et,
-                                 has_fc3=True, local_weights=weights, **attrs)
+                                 has_fc3=True, local_weights=weights, transport=transport,
+                                 **attrs)
+    assert layer.transport == transport
     out = layer.forward(d["x"], d["router_probs"])
     op = pkg.MoE(**attrs)
     ref = op([d["x"], d["router_probs"], d["fc1_w"], d["fc1_b"], d["fc2_w"], d["fc2_b"],
@@ -64,7 +68,31 @@ def _free_port():
     return p
 
 
-def _nccl_worker(rank, world, port, q):
+def test_ep_p2p_single_rank_ragged_calls(pkg, orc, dev):
+    """Device-side exchange on one rank: successive calls with different row counts
+    (including none) against the single-device layer; the output is bit-identical to the
+    plain layer's (same kernels, same summation order)."""
+    import torch
+    from onnxruntime_musa_b200 import ep
+    d, weights, attrs = _moe_case(orc, dev, 600, 256, 512, 16, 4, 23, "float16")
+    layer = ep.ExpertParallelMoE(pkg, num_experts=16, hidden_size=256, inter_size=512,
+                                 dtype=pkg.FLOAT16, has_fc3=True, local_weights=weights,
+                                 transport="p2p", max_rows=600, **attrs)
+    op = pkg.MoE(**attrs)
+    for T in (600, 1, 0, 257, 600):
+        x, lg = d["x"][:T].contiguous(), d["router_probs"][:T].contiguous()
+        out = layer.forward(x, lg)
+        ref = op([x, lg, d["fc1_w"], d["fc1_b"], d["fc2_w"], d["fc2_b"], d["fc3_w"], d["fc3_b"]])
+        torch.cuda.synchronize()
+        assert out.shape == (T, 256)
+        np.testing.assert_allclose(as_np(out), as_np(ref), **TOL["float16"])
+    op.release()
+    with pytest.raises(ValueError):
+        layer.forward(d["x"][:1].repeat(601, 1), d["router_probs"][:1].repeat(601, 1))
+    layer.close()
+
+
+def _nccl_worker(rank, world, port, q, transport="p2p"):
     import torch
     import torch.distributed as dist
     import __graft_entry__ as ge
@@ -81,22 +109,31 @@ def _nccl_worker(rank, world, port, q):
         xs, ls = d["x"][rank * T_r:(rank + 1) * T_r], d["router_probs"][rank * T_r:(rank + 1) * T_r]
         layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=512, inter_size=256,
                                      dtype=pkg.FLOAT16, has_fc3=True,
-                                     local_weights=ep.shard_experts(weights, rank, world), **attrs)
+                                     local_weights=ep.shard_experts(weights, rank, world),
+                                     transport=transport, **attrs)
+        # Ragged per-rank calls: rank 1 sends fewer rows on the second call.
         out = layer.forward(xs.contiguous(), ls.contiguous())
+        T2 = T_r if rank == 0 else 100
+        out2 = layer.forward(xs[:T2].contiguous(), ls[:T2].contiguous())
         op = pkg.MoE(**attrs)
         ref = op([xs.contiguous(), ls.contiguous(), d["fc1_w"], d["fc1_b"], d["fc2_w"],
                   d["fc2_b"], d["fc3_w"], d["fc3_b"]])
         torch.cuda.synchronize()
         err = np.abs(as_np(out) - as_np(ref)) - (TOL["float16"]["atol"] +
                                                  TOL["float16"]["rtol"] * np.abs(as_np(ref)))
-        q.put((rank, float(err.max())))
+        err2 = np.abs(as_np(out2) - as_np(ref)[:T2]) - (
+            TOL["float16"]["atol"] + TOL["float16"]["rtol"] * np.abs(as_np(ref)[:T2]))
+        if hasattr(layer, "close"):
+            layer.close()
+        q.put((rank, float(max(err.max(), err2.max()))))
     except Exception as exc:
         q.put((rank, repr(exc)))
     finally:
         dist.destroy_process_group()
 
 
-def test_ep_two_ranks_nccl():
+@pytest.mark.parametrize("transport", ["p2p", "collective"])
+def test_ep_two_ranks(transport):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -104,7 +141,7 @@ def test_ep_two_ranks_nccl():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, transport)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))
