@@ -503,9 +503,11 @@ size_t ep_workspace_bytes(const moe_b200_ep_comm* c, const moe_b200_problem& p) 
 // buffers, combine.  Local weights: [E / W, ...].  No host synchronisation.
 int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b200_tensors& t,
                     uint8_t* ws, size_t ws_bytes, cudaStream_t s) {
-  int st = validate_problem(&p);
-  if (st != MOE_B200_OK) return st;
   const int W = c->world, E = c->num_experts, El = E / W, r = c->rank;
+  moe_b200_problem global = p;  // routing is over all E experts (k <= E, not E / W)
+  global.num_experts = E;
+  int st = validate_problem(&global);
+  if (st != MOE_B200_OK) return st;
   if (p.num_experts != El)
     return fail(MOE_B200_INVALID_ARGUMENT, "problem.num_experts=%lld must be the local %d",
                 (long long)p.num_experts, El);
@@ -554,7 +556,11 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
   MOE_CUDA_CHECK(launch_ep_send_rows(c->peers, c->lay, W, E, t.input, static_cast<int64_t>(H) * es,
                                      k, i32(L.idx), i32(L.src), R, tab.send_base, err, s),
                  "send rows");
-  MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpRows, epoch, s), "signal rows");
+  // MOE_B200_TEST_STALL=1 (tests only): the rows and return flags are never raised, so the
+  // bounded waits expire and the call reports device error kErrTimeoutPeer.
+  const bool stall = env_flag("MOE_B200_TEST_STALL");
+  if (!stall)
+    MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpRows, epoch, s), "signal rows");
   MOE_CUDA_CHECK(launch_ep_wait(c->sym, c->lay, W, kEpRows, epoch, err, s), "wait rows");
 
   // Expert FFN on the received rows (row count known on the device only: the GEMMs are
@@ -594,7 +600,9 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
   if (!tc_supported(g2))
     return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc2: tensor-core path unsupported");
   MOE_CUDA_CHECK(launch_gemm_tc(g2, device_sm_count(), 2, s), "fc2 grouped GEMM");
-  MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpReturn, epoch, s), "signal return");
+  if (!stall)
+    MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpReturn, epoch, s),
+                   "signal return");
   MOE_CUDA_CHECK(launch_ep_wait(c->sym, c->lay, W, kEpReturn, epoch, err, s), "wait return");
   MOE_CUDA_CHECK(launch_combine(p.dtype, c->sym + c->lay.ret, i32(L.pos),
                                 reinterpret_cast<float*>(ws + L.w), T, k, H, t.output, s),

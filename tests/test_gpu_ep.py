@@ -92,7 +92,7 @@ def test_ep_p2p_single_rank_ragged_calls(pkg, orc, dev):
     layer.close()
 
 
-def _nccl_worker(rank, world, port, q, transport="p2p"):
+def _nccl_worker(rank, world, port, q, transport="p2p", E=8):
     import torch
     import torch.distributed as dist
     import __graft_entry__ as ge
@@ -104,10 +104,10 @@ def _nccl_worker(rank, world, port, q, transport="p2p"):
     try:
         pkg, orc = ge.load_package(), ge.load_oracle()
         from onnxruntime_musa_b200 import ep
-        d, weights, attrs = _moe_case(orc, dev, 512, 512, 256, 8, 2, 33, "float16")
+        d, weights, attrs = _moe_case(orc, dev, 512, 512, 256, E, 2, 33 + E, "float16")
         T_r = 256
         xs, ls = d["x"][rank * T_r:(rank + 1) * T_r], d["router_probs"][rank * T_r:(rank + 1) * T_r]
-        layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=512, inter_size=256,
+        layer = ep.ExpertParallelMoE(pkg, num_experts=E, hidden_size=512, inter_size=256,
                                      dtype=pkg.FLOAT16, has_fc3=True,
                                      local_weights=ep.shard_experts(weights, rank, world),
                                      transport=transport, **attrs)
@@ -132,8 +132,9 @@ def _nccl_worker(rank, world, port, q, transport="p2p"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["p2p", "collective"])
-def test_ep_two_ranks(transport):
+@pytest.mark.parametrize("transport,E", [("p2p", 8), ("collective", 8), ("p2p", 2)],
+                         ids=["p2p", "collective", "p2p_one_expert_per_rank"])
+def test_ep_two_ranks(transport, E):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -141,7 +142,8 @@ def test_ep_two_ranks(transport):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, transport)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, transport, E))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))

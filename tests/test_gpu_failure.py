@@ -39,3 +39,35 @@ def test_bounded_wait_expires_cleanly(pkg, orc, dev, mode):
     ref = orc.moe(h["x"], h["router_probs"], h["fc1_w"], h["fc1_b"], h["fc2_w"], h["fc2_b"],
                   h["fc3_w"], h["fc3_b"], **inp["attrs"])
     np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+
+
+def test_ep_exchange_wait_expires_cleanly(pkg, orc, dev):
+    """Device-side expert-parallel exchange: with the test hook the rows / return flags are
+    never raised (a peer that does not take part looks the same to the waiter).  The
+    waits give up after 2 s each, the call reports device error 6 (peer timeout), and the
+    next call on the same communicator is correct."""
+    import torch
+    from onnxruntime_musa_b200 import ep
+    inp = orc.make_moe_inputs(T=200, H=256, I=256, E=4, k=2, act="silu", gated=True,
+                              dtype="float32", seed=92)
+    d, h = moe_inputs_on(dev, inp, "float16")
+    weights = dict(fc1_weights=d["fc1_w"], fc2_weights=d["fc2_w"], fc3_weights=d["fc3_w"])
+    layer = ep.ExpertParallelMoE(pkg, num_experts=4, hidden_size=256, inter_size=256,
+                                 dtype=pkg.FLOAT16, has_fc3=True, local_weights=weights,
+                                 transport="p2p", **inp["attrs"])
+    layer.forward(d["x"], d["router_probs"])  # connect
+    os.environ.update(MOE_B200_TEST_STALL="1", MOE_B200_TRACE_SYNC="1")
+    try:
+        t0 = time.time()
+        with pytest.raises(pkg.EPFail, match="device error code 6"):
+            layer.forward(d["x"], d["router_probs"])
+        assert time.time() - t0 < 60
+    finally:
+        for v in ("MOE_B200_TEST_STALL", "MOE_B200_TRACE_SYNC"):
+            os.environ.pop(v, None)
+    out = layer.forward(d["x"], d["router_probs"])
+    torch.cuda.synchronize()
+    layer.close()
+    ref = orc.moe(h["x"], h["router_probs"], h["fc1_w"], None, h["fc2_w"], None, h["fc3_w"],
+                  None, **inp["attrs"])
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
