@@ -223,6 +223,52 @@ class ExpertParallelMoE:
             handle.wait()
 
 
+class HostPipeline:
+    """Calls of an expert-parallel layer on pinned host tensors: the H2D copy of call i+1
+    and the D2H copy of call i-1 run on their own streams while call i computes on the
+    current stream (the multi-GPU counterpart of ``moe_b200_pipeline_*``).  Host tensors
+    must stay alive until :meth:`synchronize`."""
+
+    def __init__(self, layer: ExpertParallelMoE, max_rows: int, dtype, device, depth: int = 2):
+        self.layer = layer
+        self.device = device
+        self.cin = torch.cuda.Stream(device)
+        self.cout = torch.cuda.Stream(device)
+        self.slots = [dict(x=torch.empty(max_rows, layer.H, dtype=dtype, device=device),
+                           lg=torch.empty(max_rows, layer.E, dtype=dtype, device=device),
+                           in_done=torch.cuda.Event(), comp_done=torch.cuda.Event(),
+                           out_done=torch.cuda.Event(), out=None)
+                      for _ in range(depth)]
+        self.calls = 0
+
+    def submit(self, host_x, host_logits, host_out) -> None:
+        s = self.slots[self.calls % len(self.slots)]
+        reuse = self.calls >= len(self.slots)
+        n = host_x.shape[0]
+        comp = torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(self.cin):
+            if reuse:
+                self.cin.wait_event(s["comp_done"])
+            s["x"][:n].copy_(host_x, non_blocking=True)
+            s["lg"][:n].copy_(host_logits, non_blocking=True)
+            s["in_done"].record(self.cin)
+        comp.wait_event(s["in_done"])
+        if reuse:
+            comp.wait_event(s["out_done"])
+        out = self.layer.forward(s["x"][:n], s["lg"][:n])
+        s["comp_done"].record(comp)
+        with torch.cuda.stream(self.cout):
+            self.cout.wait_event(s["comp_done"])
+            host_out.copy_(out, non_blocking=True)
+            s["out_done"].record(self.cout)
+        out.record_stream(self.cout)
+        s["out"] = out
+        self.calls += 1
+
+    def synchronize(self) -> None:
+        torch.cuda.synchronize(self.device)
+
+
 def shard_experts(tensors: dict[str, Any], rank: int, world: int) -> dict[str, Any]:
     """The slice of each per-expert tensor (leading dimension E) owned by ``rank``."""
     out = {}

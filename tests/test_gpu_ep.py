@@ -152,3 +152,27 @@ def test_ep_two_ranks(transport, E):
     for r in range(2):
         assert not isinstance(res[r], str), res[r]
         assert res[r] <= 0, f"rank {r} exceeds the fp16 tolerance by {res[r]}"
+
+
+def test_ep_host_pipeline(pkg, orc, dev):
+    """ep.HostPipeline: calls on pinned host tensors give the layer's own outputs."""
+    import torch
+    from onnxruntime_musa_b200 import ep
+    d, weights, attrs = _moe_case(orc, dev, 256, 256, 384, 8, 2, 24, "float16")
+    layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=256, inter_size=384,
+                                 dtype=pkg.FLOAT16, has_fc3=True, local_weights=weights,
+                                 **attrs)
+    pipe = ep.HostPipeline(layer, 256, torch.float16, dev, depth=2)
+    g = torch.Generator().manual_seed(3)
+    calls = []
+    for T in (256, 100, 256, 7):
+        hx = torch.randn(T, 256, generator=g).half().pin_memory()
+        hl = torch.randn(T, 8, generator=g).half().pin_memory()
+        ho = torch.empty(T, 256, dtype=torch.float16).pin_memory()
+        pipe.submit(hx, hl, ho)
+        calls.append((hx, hl, ho))
+    pipe.synchronize()
+    for hx, hl, ho in calls:
+        ref = layer.forward(hx.to(dev), hl.to(dev)).cpu()
+        assert torch.equal(ho, ref)
+    layer.close()
