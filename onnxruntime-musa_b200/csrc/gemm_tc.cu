@@ -19,7 +19,9 @@
 //  math/gemm_post_kernels.mu:27-53), which this single kernel replaces.
 #include <algorithm>
 #include <mutex>
+#include <cstdio>
 #include <type_traits>
+#include <vector>
 
 #include "moe_kernels.h"
 
@@ -38,8 +40,8 @@ constexpr int THREADS = 320;      // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int EPI_WARPS = 8;      // two warps per TMEM lane quarter, splitting the columns
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES =
-    1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + 64 * 8 /*barriers*/ +
-    2 * (kMaxExperts + 1) * 4;
+    1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * 2048 /*epilogue staging*/ +
+    64 * 8 /*barriers*/ + 2 * (kMaxExperts + 1) * 4;
 
 struct TcParams {
   const int32_t* offsets;
@@ -82,7 +84,27 @@ struct TcParams {
   int nseg;
   int remap_world;
   void* out_peers[kMaxEpRanks];
+  int trace;   // diagnostics: CTA 0 records per-tile phase timestamps (MOE_B200_GEMM_TRACE)
 };
+
+// Per-tile phase trace of CTA 0 (diagnostics only).  Entry i: [2i] = %globaltimer ns,
+// [2i+1] = event << 32 | tile.
+constexpr unsigned kTraceCap = 16384;
+__device__ unsigned long long g_tile_trace[2 * kTraceCap];
+__device__ unsigned int g_trace_n;
+enum TraceEvent : unsigned {
+  kTrClaim = 1, kTrProdDone = 2, kTrMmaStart = 3, kTrMmaFirst = 4, kTrMmaDone = 5,
+  kTrEpiStart = 6, kTrEpiDone = 7,
+};
+__device__ __forceinline__ void trace(const TcParams& p, unsigned ev, int tile) {
+  if (!p.trace || blockIdx.x != 0) return;
+  const unsigned i = atomicAdd(&g_trace_n, 1u);
+  if (i < kTraceCap) {
+    g_tile_trace[2 * i] = globaltimer_ns();
+    g_tile_trace[2 * i + 1] = (static_cast<unsigned long long>(ev) << 32) |
+                              static_cast<unsigned>(tile);
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ T* out_row(const TcParams& p, int row) {
@@ -139,75 +161,124 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int valid_
 }
 
 // Fast-math activations for the 16-bit epilogue (inputs and outputs are fp16/bf16,
-// so the few-ulp error of the approximate exp and reciprocal is far below the
-// output rounding).
-__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+// so the few-ulp error of the approximate exp and reciprocal is far below the output
+// rounding).  The activation is dispatched once per chunk of n values, each variant a
+// straight loop: a per-element switch, unrolled over the chunk with erf, exp and an IEEE
+// reciprocal inlined in every copy, ran the epilogue out of the instruction cache
+// (2.8 us per 32 values, ~10x the whole rest of the epilogue).
+__device__ __forceinline__ float fast_sigmoid(float x) {
+  return __fdividef(1.0f, 1.0f + __expf(-x));
+}
 
-__device__ __forceinline__ float fast_act_single(int act, float x) {
+template <int n>
+__device__ __forceinline__ void act_chunk(int act, float (&v)[n]) {
   switch (act) {
-    case kRelu: return fmaxf(x, 0.0f);
-    case kGelu: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-    case kSilu: return x * fast_sigmoid(x);
-    default: return x;
+    case kRelu:
+#pragma unroll
+      for (int j = 0; j < n; ++j) v[j] = fmaxf(v[j], 0.0f);
+      break;
+    case kGelu:
+#pragma unroll
+      for (int j = 0; j < n; ++j) v[j] = 0.5f * v[j] * (1.0f + erff(v[j] * 0.70710678118654752f));
+      break;
+    case kSilu:
+#pragma unroll
+      for (int j = 0; j < n; ++j) v[j] = v[j] * fast_sigmoid(v[j]);
+      break;
+    default:
+      break;
   }
 }
 
-__device__ __forceinline__ float fast_act_gated(const ActParams& p, float g, float u) {
-  if (p.act == kSwiglu) {
-    g = fminf(g, p.limit);
-    u = fminf(fmaxf(u, -p.limit), p.limit);
-    return g * fast_sigmoid(p.alpha * g) * (u + p.beta);
+// v[j] = act(g[j]) * u[j] (swiglu: the clamped, alpha-scaled form with u + beta).
+template <int n>
+__device__ __forceinline__ void act_gated_chunk(const ActParams& ap, float (&g)[n],
+                                                const float (&u)[n]) {
+  if (ap.act == kSwiglu) {
+    const float lim = ap.limit, al = ap.alpha, be = ap.beta;
+#pragma unroll
+    for (int j = 0; j < n; ++j) {
+      const float gc = fminf(g[j], lim);
+      const float uc = fminf(fmaxf(u[j], -lim), lim);
+      g[j] = gc * fast_sigmoid(al * gc) * (uc + be);
+    }
+    return;
   }
-  return fast_act_single(p.act, g) * u;
+  act_chunk<n>(ap.act, g);
+#pragma unroll
+  for (int j = 0; j < n; ++j) g[j] *= u[j];
+}
+
+// Adds bias[e, col0 + j] (clamped to column N - 1) to v[0..n).
+template <typename T, int n>
+__device__ __forceinline__ void add_bias(float (&v)[n], const void* bias, int e, int col0,
+                                         const TcParams& p) {
+  if (bias == nullptr) return;
+#pragma unroll
+  for (int j = 0; j < n; ++j) v[j] += bias_val<T>(bias, e, min(col0 + j, p.N - 1), p);
 }
 
 // Epilogue of one accumulator tile for the calling warp's 32 TMEM lanes (one output
-// row per thread), accumulator columns [c0, c1).  Gated: columns [0,128) hold the gate
-// and [128,256) the linear half of output columns n0..n0+127 (c ranges over the gate
-// columns); plain: columns [0,256) are outputs n0..n0+255.
+// row per lane), accumulator columns [c0, c1) in chunks of 32 output columns.  Gated:
+// columns [0,128) hold the gate and [128,256) the linear half of output columns
+// n0..n0+127 (c ranges over the gate columns); plain: columns [0,256) are outputs
+// n0..n0+255.  Each chunk goes through the warp's 2 KB staging area (32 rows x 64 B,
+// 16-byte granules XOR-swizzled by row so both the row-wise writes and the column-wise
+// reads are conflict-free) and leaves as 16-byte stores that cover 8 rows x 64 B per
+// instruction, instead of one 16-byte piece of 32 different rows.
+constexpr int EPI_CHUNK = 32;                 // output columns per staged chunk
+constexpr int EPI_STAGE_BYTES = 32 * EPI_CHUNK * 2;  // per epilogue warp
+
 template <typename T>
 __device__ __forceinline__ void epilogue_rows(const TcParams& p, uint32_t taddr, int row,
-                                              bool valid, int e, int n0, int c0, int c1) {
-  T* orow = valid ? out_row<T>(p, row) : nullptr;
-  const bool has_b1 = p.bias1 != nullptr, has_b3 = p.bias3 != nullptr;
-  if (p.gated) {
+                                              bool valid, int e, int n0, int c0, int c1,
+                                              uint8_t* stage, int lane) {
+  const unsigned long long my_row =
+      valid ? reinterpret_cast<unsigned long long>(out_row<T>(p, row)) : 0ull;
+  uint4* st_row = reinterpret_cast<uint4*>(stage + lane * (EPI_CHUNK * 2));
+  const int wsw = (lane >> 1) & 3;
 #pragma unroll 1
-    for (int c = c0; c < c1; c += 16) {
-      float g[16], u[16];
-      tmem_ld16(taddr + c, g);
-      tmem_ld16(taddr + BN / 2 + c, u);
+  for (int c = c0; c < c1; c += EPI_CHUNK) {
+    const int col = n0 + c;
+    float v[EPI_CHUNK];
+    if (p.gated) {
+      float g[EPI_CHUNK], u[EPI_CHUNK];
+      tmem_ld16(taddr + c, *reinterpret_cast<float(*)[16]>(&g[0]));
+      tmem_ld16(taddr + c + 16, *reinterpret_cast<float(*)[16]>(&g[16]));
+      tmem_ld16(taddr + BN / 2 + c, *reinterpret_cast<float(*)[16]>(&u[0]));
+      tmem_ld16(taddr + BN / 2 + c + 16, *reinterpret_cast<float(*)[16]>(&u[16]));
       tmem_ld_wait();
-      const int col = n0 + c;
-      if (valid && col < p.N) {
-        float v[16];
+      add_bias<T, EPI_CHUNK>(g, p.bias1, e, col, p);
+      add_bias<T, EPI_CHUNK>(u, p.bias3, e, col, p);
+      act_gated_chunk<EPI_CHUNK>(p.ap, g, u);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int cj = min(col + j, p.N - 1);
-          const float gb = has_b1 ? g[j] + bias_val<T>(p.bias1, e, cj, p) : g[j];
-          const float ub = has_b3 ? u[j] + bias_val<T>(p.bias3, e, cj, p) : u[j];
-          v[j] = fast_act_gated(p.ap, gb, ub);
-        }
-        store16<T>(orow + col, v, p.N - col);
-      }
-    }
-  } else {
-#pragma unroll 1
-    for (int c = c0; c < c1; c += 16) {
-      float a[16];
-      tmem_ld16(taddr + c, a);
+      for (int j = 0; j < EPI_CHUNK; ++j) v[j] = g[j];
+    } else {
+      tmem_ld16(taddr + c, *reinterpret_cast<float(*)[16]>(&v[0]));
+      tmem_ld16(taddr + c + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
       tmem_ld_wait();
-      const int col = n0 + c;
-      if (valid && col < p.N) {
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int cj = min(col + j, p.N - 1);
-          const float ab = has_b1 ? a[j] + bias_val<T>(p.bias1, e, cj, p) : a[j];
-          v[j] = fast_act_single(p.ap.act, ab);
-        }
-        store16<T>(orow + col, v, p.N - col);
-      }
+      add_bias<T, EPI_CHUNK>(v, p.bias1, e, col, p);
+      act_chunk<EPI_CHUNK>(p.ap.act, v);
+
     }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+      w.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+      w.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+      w.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+      st_row[q ^ wsw] = w;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int r = pass * 8 + (lane >> 2), q = lane & 3;
+      T* rp = reinterpret_cast<T*>(__shfl_sync(0xffffffffu, my_row, r));
+      const uint4 w = reinterpret_cast<const uint4*>(stage + r * (EPI_CHUNK * 2))[q ^ ((r >> 1) & 3)];
+      if (rp != nullptr && col + 8 * q + 8 <= p.N) *reinterpret_cast<uint4*>(rp + col + 8 * q) = w;
+    }
+    __syncwarp();
   }
 }
 
@@ -230,7 +301,8 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* epi_stage = sB + STAGES * B_BYTES;  // [EPI_WARPS][32 rows x 64 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + EPI_WARPS * EPI_STAGE_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -379,7 +451,8 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
       const int row = s_offs[e] + m * BM + r_in_tile;
       const bool valid = row < s_offs[e + 1];
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      epilogue_rows<T>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1);
+      epilogue_rows<T>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1,
+                       epi_stage + (warp - 2) * EPI_STAGE_BYTES, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -409,7 +482,8 @@ constexpr int P_BM = 256;         // rows per pair tile
 constexpr int P_STAGES = 6;
 constexpr int P_STAGE_BYTES = A_BYTES + B_HALF;  // per CTA: 128x64 of A + 128x64 of B
 constexpr int P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + 16 * 32 * 4 * 4 /*exchange*/ +
-                             64 * 8 + 2 * (kMaxExperts + 1) * 4;
+                             EPI_WARPS * 2048 /*epilogue staging*/ + 64 * 8 +
+                             2 * (kMaxExperts + 1) * 4;
 
 constexpr int SW_TOK_ROWS = 64;   // token rows per TMA box of a swapped tile (1-2 per CTA)
 constexpr int kPairSwapLimit = 240;  // largest swapped tail (rows); 256 is a full tile
@@ -485,10 +559,12 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
         for (int j = 0; j < 16; ++j) u[j] = buf[j * 32 + lane];
         mbar_arrive(&x.empty[slot]);
 #pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += own_bias;
+        act_gated_chunk<16>(p.ap, v, u);
+#pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int tok = c + j;
-          if (fok && tok < t.rows)
-            out_row<T>(p, t.r0 + tok)[f] = from_f<T>(fast_act_gated(p.ap, v[j] + own_bias, u[j]));
+          if (fok && tok < t.rows) out_row<T>(p, t.r0 + tok)[f] = from_f<T>(v[j]);
         }
       }
     }
@@ -506,9 +582,12 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
       const unsigned long long my_row =
           my_tok < t.rows ? reinterpret_cast<unsigned long long>(out_row<T>(p, t.r0 + my_tok)) : 0ull;
 #pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += b;
+      act_chunk<16>(p.ap.act, v);
+#pragma unroll
       for (int j = 0; j < 16; ++j) {
         T* row = reinterpret_cast<T*>(__shfl_sync(0xffffffffu, my_row, j));
-        if (fok && c + j < t.rows) row[f] = from_f<T>(fast_act_single(p.ap.act, v[j] + b));
+        if (fok && c + j < t.rows) row[f] = from_f<T>(v[j]);
       }
     }
   }
@@ -548,7 +627,8 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
   uint8_t* sA = smem;
   uint8_t* sB = smem + P_STAGES * A_BYTES;
   float* xbuf = reinterpret_cast<float*>(sB + P_STAGES * B_HALF);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + P_STAGES * B_HALF + XCH_BYTES);
+  uint8_t* epi_stage = sB + P_STAGES * B_HALF + XCH_BYTES;  // [EPI_WARPS][32 rows x 64 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + EPI_WARPS * EPI_STAGE_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + P_STAGES;
   uint64_t* tfull = bars + 2 * P_STAGES;
@@ -643,6 +723,7 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
           break;
         }
         if (L < 0) break;
+        trace(p, kTrClaim, L);
         if (p.test_stall) continue;
         const PairTile t = pair_tile(L, s_tiles, s_offs, p);
         const int e = t.e, n = t.n;
@@ -691,6 +772,7 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
           }
           if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
         }
+        trace(p, kTrProdDone, L);
       }
     }
   } else if (warp == 1) {
@@ -718,6 +800,7 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
           break;
         }
         tc_fence_after();
+        trace(p, kTrMmaStart, L);
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
@@ -728,6 +811,7 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
             break;
           }
           tc_fence_after();
+          if (kb == 0) trace(p, kTrMmaFirst, L);
           const uint32_t x_addr = smem_u32(sA + stage * A_BYTES);
           const uint32_t w_addr = smem_u32(sB + stage * B_HALF);
           const uint32_t a_addr = t.nt ? w_addr : x_addr;
@@ -743,6 +827,7 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
         }
         if (!ok) break;
         tc_commit_pair(&tfull[acc], 0x3);
+        trace(p, kTrMmaDone, L);
       }
       tc_commit_pair(done, 0x1);
       mbar_wait(done, 0);
@@ -774,6 +859,7 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
         break;
       }
       tc_fence_after();
+      if (warp == 2 && lane == 0) trace(p, kTrEpiStart, L);
       const PairTile t = pair_tile(L, s_tiles, s_offs, p);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       if (t.nt) {
@@ -787,10 +873,11 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
         const int row = t.r0 + r_in_tile;
         const bool valid = row < t.r0 + t.rows;
         epilogue_rows<T>(p, taddr, row, valid, t.e, p.gated ? t.n * (BN / 2) : t.n * BN, ec0,
-                         ec1);
+                         ec1, epi_stage + (warp - 2) * EPI_STAGE_BYTES, lane);
       }
       tc_fence_before();
       __syncwarp();
+      if (warp == 2 && lane == 0) trace(p, kTrEpiDone, L);
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
     }
   }
@@ -821,15 +908,16 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
 // slots of both CTAs with multicast commits.
 constexpr int QA = 4;
 constexpr int QB = 6;
-constexpr int QP = 6;
+// Packed ring depth: 6, or 5 for int8 so the epilogue staging still fits in 227 KB.
+template <int BITS> constexpr int qp_stages() { return BITS == 8 ? 5 : 6; }
 constexpr int Q_THREADS = 608;   // warps 0 A TMA, 1 MMA, 2..9 epilogue, 10..17 converters, 18 P TMA
 constexpr int CONV_WARPS = 8;
 constexpr int kConvGroups = 4;   // converter groups working on different k-blocks
 constexpr int Q_PWARP = 18;
 template <int BITS> constexpr int q_packed_bytes() { return BM * BK * BITS / 8; }
 template <int BITS> constexpr int q_smem_bytes() {
-  return 1024 + QA * A_BYTES + QB * B_HALF + QP * q_packed_bytes<BITS>() + 64 * 8 +
-         2 * (kMaxExperts + 1) * 4;
+  return 1024 + QA * A_BYTES + QB * B_HALF + qp_stages<BITS>() * q_packed_bytes<BITS>() +
+         EPI_WARPS * 2048 /*epilogue staging*/ + 64 * 8 + 2 * (kMaxExperts + 1) * 4;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -877,7 +965,9 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
   uint8_t* sA = smem;
   uint8_t* sB = sA + QA * A_BYTES;
   uint8_t* sP = sB + QB * B_HALF;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + QP * PB);
+  constexpr int QP = qp_stages<BITS>();
+  uint8_t* epi_stage = sP + QP * PB;  // [EPI_WARPS][32 rows x 64 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + EPI_WARPS * EPI_STAGE_BYTES);
   uint64_t* fullA = bars;                  // [QA]
   uint64_t* emptyA = fullA + QA;           // [QA]
   uint64_t* fullP = emptyA + QA;           // [QP]
@@ -1130,7 +1220,8 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
       const int row = s_offs[e] + m * P_BM + r_in_tile;
       const bool valid = row < s_offs[e + 1];
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      epilogue_rows<__half>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1);
+      epilogue_rows<__half>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1,
+                            epi_stage + (warp - 2) * EPI_STAGE_BYTES, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
@@ -1204,6 +1295,29 @@ bool make_map_b(CUtensorMap* m, int dt, const GemmOperandB& b, int K, int E,
          CUDA_SUCCESS;
 }
 
+// Appends CTA 0's trace of the launch just enqueued to `path` (diagnostics only:
+// synchronises the stream).  Lines: launch, K, event, tile, ns since the first entry.
+void dump_trace(const char* path, int K, cudaStream_t s) {
+  unsigned n = 0;
+  if (cudaStreamSynchronize(s) != cudaSuccess ||
+      cudaMemcpyFromSymbol(&n, g_trace_n, sizeof(n)) != cudaSuccess)
+    return;
+  n = std::min(n, kTraceCap);
+  std::vector<unsigned long long> buf(2 * static_cast<size_t>(n));
+  if (n == 0 || cudaMemcpyFromSymbol(buf.data(), g_tile_trace, buf.size() * 8) != cudaSuccess)
+    return;
+  unsigned long long t0 = ~0ull;
+  for (unsigned i = 0; i < n; ++i) t0 = std::min(t0, buf[2 * i]);
+  FILE* f = std::fopen(path, "a");
+  if (f == nullptr) return;
+  static int launch = 0;
+  for (unsigned i = 0; i < n; ++i)
+    std::fprintf(f, "%d,%d,%u,%u,%llu\n", launch, K, static_cast<unsigned>(buf[2 * i + 1] >> 32),
+                 static_cast<unsigned>(buf[2 * i + 1] & 0xffffffffu), buf[2 * i] - t0);
+  std::fclose(f);
+  ++launch;
+}
+
 template <typename T>
 cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) {
   CUtensorMap ma, mb1, mb3;
@@ -1242,6 +1356,14 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   p.nseg = g.nseg;
   p.remap_world = g.remap_world;
   for (int i = 0; i < kMaxEpRanks; ++i) p.out_peers[i] = g.out_peers[i];
+  const char* trace_path = pair ? std::getenv("MOE_B200_GEMM_TRACE") : nullptr;
+  p.trace = trace_path != nullptr ? 1 : 0;
+
+
+  if (p.trace) {
+    const unsigned zero = 0;
+    cudaMemcpyToSymbolAsync(g_trace_n, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
+  }
   CUtensorMap ma_sw = ma, mb1_sw = mb1, mb3_sw = mb3;
   if (p.swap_max > 0) {
     if (!make_map_a(&ma_sw, g.dtype, g.a, g.rows, g.K, SW_TOK_ROWS)) return cudaErrorInvalidValue;
@@ -1270,6 +1392,7 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
     const int64_t pairs = std::min<int64_t>(ub, num_sms / 2);
     tc_pair_grouped_gemm_kernel<T><<<static_cast<int>(2 * pairs), THREADS, P_SMEM_BYTES, s>>>(
         ma, mb1, mb3, ma_sw, mb1_sw, mb3_sw, p);
+    if (p.trace) dump_trace(trace_path, g.K, s);
   } else {
     const int grid = static_cast<int>(std::min<int64_t>(ub, num_sms));
     tc_grouped_gemm_kernel<T><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb1, mb3, p);
