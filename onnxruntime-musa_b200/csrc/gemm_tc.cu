@@ -140,26 +140,6 @@ __device__ __forceinline__ float bias_val(const void* bias, int e, int n, const 
                                           static_cast<int64_t>(n) * p.bias_stride]);
 }
 
-template <typename T>
-__device__ __forceinline__ void store16(T* dst, const float (&v)[16], int valid_cols) {
-  if (valid_cols >= 16) {
-    uint4 o0, o1;
-    uint32_t* w0 = reinterpret_cast<uint32_t*>(&o0);
-    uint32_t* w1 = reinterpret_cast<uint32_t*>(&o1);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      w0[q] = pack2<T>(v[2 * q], v[2 * q + 1]);
-      w1[q] = pack2<T>(v[8 + 2 * q], v[8 + 2 * q + 1]);
-    }
-    reinterpret_cast<uint4*>(dst)[0] = o0;
-    reinterpret_cast<uint4*>(dst)[1] = o1;
-  } else {
-#pragma unroll
-    for (int q = 0; q < 16; ++q)
-      if (q < valid_cols) dst[q] = from_f<T>(v[q]);
-  }
-}
-
 // Fast-math activations for the 16-bit epilogue (inputs and outputs are fp16/bf16,
 // so the few-ulp error of the approximate exp and reciprocal is far below the output
 // rounding).  The activation is dispatched once per chunk of n values, each variant a
@@ -1358,6 +1338,7 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   for (int i = 0; i < kMaxEpRanks; ++i) p.out_peers[i] = g.out_peers[i];
   const char* trace_path = pair ? std::getenv("MOE_B200_GEMM_TRACE") : nullptr;
   p.trace = trace_path != nullptr ? 1 : 0;
+
 
 
   if (p.trace) {
