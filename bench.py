@@ -74,7 +74,7 @@ CONFIGS = {
 
 # DRAM bytes (read + write) of one fc1(+fc3) launch of the default workload from the ncu
 # capture summarised in profiles/tc_pair_grouped_gemm_c2.md.
-FC1_TRAFFIC_BYTES = 2_488_566_000
+FC1_TRAFFIC_BYTES = 2_177_550_848
 
 
 def peaks():
