@@ -133,11 +133,46 @@ int decode_splits(const moe_b200_problem& p, int64_t N, int64_t K) {
 int fc1_splits(const moe_b200_problem& p) { return decode_splits(p, p.inter_size, p.hidden_size); }
 int fc2_splits(const moe_b200_problem& p) { return decode_splits(p, p.hidden_size, p.inter_size); }
 
-// Workspace of the decode path: fc1 partials [S1][R][2I] then fc2 partials [S2][R][H].
+// int4 with exact codes runs the biased-code kernel on pre-arranged activations
+// (launch_qdec_prep); MOE_B200_QDEC_RAW4=0 keeps the per-code conversion (comparison runs).
+bool raw4(const moe_b200_problem& p) {
+  const int bs = p.attrs.block_size;
+  if (p.attrs.expert_weight_bits != 4 || (bs != 0 && bs % 128 != 0)) return false;
+  const char* v = std::getenv("MOE_B200_QDEC_RAW4");
+  return v == nullptr || v[0] != '0';
+}
+
+// Workspace of the decode path: fc1 partials [S1][R][2I], fc2 partials [S2][R][H], and for
+// the biased-code int4 path the arranged activations and offset terms of fc1 ([T][H],
+// [T][H/128]) and fc2 ([R][I], [R][I/128]).
 size_t fc1_partial_bytes(const moe_b200_problem& p) {
   const int s1 = fc1_splits(p);
   if (s1 == 1) return 0;
   return align256(static_cast<size_t>(s1) * p.num_rows * p.attrs.k * 2 * p.inter_size * sizeof(float));
+}
+
+size_t fc2_partial_bytes(const moe_b200_problem& p) {
+  return align256(static_cast<size_t>(fc2_splits(p)) * p.num_rows * p.attrs.k * p.hidden_size *
+                  sizeof(float));
+}
+struct Raw4Ws {
+  size_t xp1, c1, xp2, c2, total;
+};
+Raw4Ws raw4_ws(const moe_b200_problem& p) {
+  Raw4Ws w{};
+  if (!raw4(p)) return w;
+  const size_t T = p.num_rows, R = p.num_rows * p.attrs.k, H = p.hidden_size, I = p.inter_size;
+  size_t o = fc1_partial_bytes(p) + fc2_partial_bytes(p);
+  w.xp1 = o;
+  o += align256(T * H * 2);
+  w.c1 = o;
+  o += align256(T * (H / 128) * 4);
+  w.xp2 = o;
+  o += align256(R * I * 2);
+  w.c2 = o;
+  o += align256(R * (I / 128) * 4);
+  w.total = o - fc1_partial_bytes(p) - fc2_partial_bytes(p);
+  return w;
 }
 
 }  // namespace
@@ -195,6 +230,16 @@ int qmoe_decode_fc1(const moe_b200_problem& p, const moe_b200_tensors& t, const 
     a.bias1 = t.fc1_bias;
   }
   a.splits = fc1_splits(p);
+  if (raw4(p)) {
+    const Raw4Ws w = raw4_ws(p);
+    auto* xp = reinterpret_cast<__half*>(ws + w.xp1);
+    auto* corr = reinterpret_cast<float*>(ws + w.c1);
+    cudaError_t st = launch_qdec_prep(a.x, p.num_rows, a.K, xp, corr, s);
+    if (st != cudaSuccess)
+      return set_error(MOE_B200_EP_FAIL, "QMoE fc1 activation prep: %s", cudaGetErrorString(st));
+    a.x = xp;
+    a.xcorr = corr;
+  }
   if (a.splits == 1) {
     a.out = static_cast<__half*>(act);
     a.ldo = I;
@@ -232,6 +277,16 @@ int qmoe_decode_fc2(const moe_b200_problem& p, const moe_b200_tensors& t, const 
   b.out_partial = reinterpret_cast<float*>(ws + fc1_partial_bytes(p));
   b.ldo = H;
   b.splits = fc2_splits(p);
+  if (raw4(p)) {
+    const Raw4Ws w = raw4_ws(p);
+    auto* xp = reinterpret_cast<__half*>(ws + w.xp2);
+    auto* corr = reinterpret_cast<float*>(ws + w.c2);
+    cudaError_t st = launch_qdec_prep(b.x, R, b.K, xp, corr, s);
+    if (st != cudaSuccess)
+      return set_error(MOE_B200_EP_FAIL, "QMoE fc2 activation prep: %s", cudaGetErrorString(st));
+    b.x = xp;
+    b.xcorr = corr;
+  }
   cudaError_t st = launch_qmoe_decode(b, static_cast<int>(E), s);
   if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "QMoE fc2 decode: %s", cudaGetErrorString(st));
   return MOE_B200_OK;
@@ -263,10 +318,7 @@ bool qmoe_use_fused(const moe_b200_problem& p) {
 
 size_t qmoe_workspace_bytes(const moe_b200_problem& p) {
   if (p.attrs.expert_weight_bits == 0 || qmoe_use_fused(p)) return 0;
-  if (qmoe_use_decode(p))
-    return fc1_partial_bytes(p) +
-           align256(static_cast<size_t>(fc2_splits(p)) * p.num_rows * p.attrs.k * p.hidden_size *
-                    sizeof(float));
+  if (qmoe_use_decode(p)) return fc1_partial_bytes(p) + fc2_partial_bytes(p) + raw4_ws(p).total;
   const size_t es = dtype_bytes(p.dtype);
   const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
   size_t b = align256(E * fc1_rows(p) * H * es) + align256(E * H * I * es);

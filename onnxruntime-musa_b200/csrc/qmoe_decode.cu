@@ -23,9 +23,15 @@
 // [32t, 32t+32) of a chunk and places 4 of them per MMA step in the fragment slots
 // {2t, 2t+1, 2t+8, 2t+9}; the B fragment is gathered with the same mapping:
 //   * int8, and int4 in kScaleElem: step j takes codes 32t+4j .. 32t+4j+3 in order;
-//   * int4 in the exact modes: word m (codes 8m..8m+7) is split by one shift + mask per
-//     half2 into pairs (c_i, c_{i+4}); steps 2m / 2m+1 take pairs (0,1) / (2,3), and the
-//     activations are permuted to match with prmt.
+//   * int4 in the exact modes: word m (codes 8m..8m+7) is split by one mask per half2 into
+//     pairs (c_i, c_{i+4}) (steps 2m / 2m+1 take pairs (0,1) / (2,3), after one shift for
+//     the second); the activations come pre-arranged in that order (launch_qdec_prep).
+//     The masked words are used as they are: low nibbles read as 1024 + q and high
+//     nibbles, masked in place, as 1024 + 16 q, whose activations are pre-scaled by 1/16;
+//     the constant part, 1032 * (sum of even-slot x) + 1152 * (sum of odd-slot x/16) per
+//     chunk and token (zero point 8 included), is subtracted from the chunk's sum.  This
+//     removes all per-code arithmetic but one logic op per half2; the products are exact
+//     in fp32 and the subtraction costs ~1e-3 absolute per chunk on sums of order 1e4.
 //
 // fc2 (long K = inter_size) is split over K across CTAs; each split writes fp32 partial
 // sums [split][row][col] and the combine kernel adds splits in a fixed order, so the
@@ -77,6 +83,14 @@ __device__ __forceinline__ uint32_t deq4_pair_hi(uint32_t shifted) {
   const uint32_t u = (shifted & 0x00F000F0u) | 0x64006400u;
   return h2_bits(__hfma2(bits_h2(u), h2c(0x2C00), h2c(0xD480)));
 }
+// Biased codes of the low nibbles i, i+4 (1024 + q) and, masked in place, of the high
+// nibbles i+1, i+5 (1024 + 16 q) of a word shifted right by 4i.
+__device__ __forceinline__ uint32_t raw4_lo(uint32_t shifted) {
+  return (shifted & 0x000F000Fu) | 0x64006400u;
+}
+__device__ __forceinline__ uint32_t raw4_hi(uint32_t shifted) {
+  return (shifted & 0x00F000F0u) | 0x64006400u;
+}
 // Bytes of a word selected by `sel` -> (b - 128) exact, optionally scaled.
 __device__ __forceinline__ uint32_t deq8(uint32_t word, uint32_t sel) {
   return h2_bits(__hsub2(bits_h2(__byte_perm(word, 0x64646464u, sel)), h2c(0x6480)));
@@ -103,7 +117,7 @@ __device__ __forceinline__ int64_t stored_row(const QOperand& b, int e, int n, i
          b.g;
 }
 
-template <int BITS, int NG, bool GATED, int kScale>
+template <int BITS, int NG, bool GATED, int kScale, bool RAW4>
 __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_begin, int cnt,
                                          int tok0, int n0, int c_begin, int c_end, int split,
                                          uint8_t* ring) {
@@ -162,6 +176,22 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
     const int64_t prow = row_begin + (tok_ok[gi] ? tok : 0);
     const int64_t xr = a.src_rows ? a.src_rows[prow] / a.k : prow;
     xrow[gi] = a.x + xr * a.K + 32 * t;
+  }
+  // Biased-code int4: offset terms of this thread's D columns (tokens 2t, 2t+1 of a group).
+  static_assert(!RAW4 || (BITS == 4 && kScale != kScaleElem), "biased codes: int4, exact modes");
+  constexpr bool kRaw4 = RAW4;
+  [[maybe_unused]] const int nch = a.K / QD_CHUNK;
+  const float* crow[NG][2];
+  if constexpr (kRaw4) {
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int tok = min(tok0 + gi * 8 + 2 * t + u, cnt - 1);
+        const int64_t prow = row_begin + tok;
+        const int64_t xr = a.src_rows ? a.src_rows[prow] / a.k : prow;
+        crow[gi][u] = a.xcorr + xr * nch;
+      }
   }
 
   __syncwarp();
@@ -230,10 +260,10 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
           for (int r = 0; r < 2; ++r) {  // r=0: row g -> a0/a2, r=1: row g+8 -> a1/a3
             const uint32_t* w = reinterpret_cast<const uint32_t*>(code[x][r]);
             uint32_t lo, hi;
-            if (BITS == 4 && kScale != kScaleElem) {
+            if (kRaw4) {
               const uint32_t word = w[m] >> (h * 8);  // pairs (0,4),(1,5) or (2,6),(3,7)
-              lo = deq4_pair(word);
-              hi = deq4_pair_hi(word);
+              lo = raw4_lo(word);
+              hi = raw4_hi(word);
             } else if (BITS == 4) {
               const uint32_t word = w[m] >> (h * 16);
               const __half2 s2 = r ? s8[x] : s0[x];
@@ -254,12 +284,10 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
 #pragma unroll
         for (int gi = 0; gi < NG; ++gi) {
           uint32_t b0, b1;
-          if (BITS == 4 && kScale != kScaleElem) {
-            // Regroup activations as (x_i, x_{i+4}) pairs to match the codes.
-            const uint32_t p0 = h ? xv[gi].y : xv[gi].x;
-            const uint32_t p1 = h ? xv[gi].w : xv[gi].z;
-            b0 = __byte_perm(p0, p1, 0x5410u);
-            b1 = __byte_perm(p0, p1, 0x7632u);
+          if (kRaw4) {
+            // Pre-arranged: (x_i, x_{i+4}) then (x_{i+1}/16, x_{i+5}/16).
+            b0 = h ? xv[gi].z : xv[gi].x;
+            b1 = h ? xv[gi].w : xv[gi].y;
           } else {
             b0 = h ? xv[gi].z : xv[gi].x;  // activations 4j, 4j+1
             b1 = h ? xv[gi].w : xv[gi].y;  // activations 4j+2, 4j+3
@@ -269,6 +297,20 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
             if (kScale == kScaleChunk) mma_f16_16816(part[x < PX ? x : 0][gi < PG ? gi : 0], af[x], b0, b1);
             else mma_f16_16816(acc[x][gi], af[x], b0, b1);
           }
+        }
+      }
+    }
+    if constexpr (kRaw4) {
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        const float o0 = __ldg(crow[gi][0] + c), o1 = __ldg(crow[gi][1] + c);
+#pragma unroll
+        for (int x = 0; x < NT; ++x) {
+          float* d = kScale == kScaleChunk ? part[x < PX ? x : 0][gi < PG ? gi : 0] : acc[x][gi];
+          d[0] -= o0;
+          d[1] -= o1;
+          d[2] -= o0;
+          d[3] -= o1;
         }
       }
     }
@@ -337,10 +379,37 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
   }
 }
 
+// One thread per group of 8 activations; the 16 threads of a 128-wide chunk sum the
+// chunk's offset term with a fixed butterfly (deterministic).
+__global__ void __launch_bounds__(256)
+qdec_prep_kernel(const __half* __restrict__ x, int64_t rows, int K, __half* __restrict__ xp,
+                 float* __restrict__ corr) {
+  const int64_t groups = rows * (K / 8);
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  float part = 0.f;
+  if (gid < groups) {
+    const uint4 v = reinterpret_cast<const uint4*>(x)[gid];
+    const __half2 q01 = bits_h2(v.x), q23 = bits_h2(v.y), q45 = bits_h2(v.z), q67 = bits_h2(v.w);
+    const __half2 sixteenth = __float2half2_rn(0.0625f);
+    const __half2 e04 = __lows2half2(q01, q45), e26 = __lows2half2(q23, q67);
+    const __half2 o15 = __hmul2(__highs2half2(q01, q45), sixteenth);
+    const __half2 o37 = __hmul2(__highs2half2(q23, q67), sixteenth);
+    reinterpret_cast<uint4*>(xp)[gid] = make_uint4(h2_bits(e04), h2_bits(o15), h2_bits(e26),
+                                                   h2_bits(o37));
+    const float2 fe04 = __half22float2(e04), fe26 = __half22float2(e26);
+    const float2 fo15 = __half22float2(o15), fo37 = __half22float2(o37);
+    part = 1032.0f * ((fe04.x + fe04.y) + (fe26.x + fe26.y)) +
+           1152.0f * ((fo15.x + fo15.y) + (fo37.x + fo37.y));
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (gid < groups && (gid & 15) == 0) corr[gid >> 4] = part;
+}
+
 template <int BITS, bool GATED>
 constexpr int ring_bytes() { return qd_stages<BITS>() * (GATED ? 2 : 1) * 16 * QD_CHUNK * BITS / 8; }
 
-template <int BITS, bool GATED, int kScale>
+template <int BITS, bool GATED, int kScale, bool RAW4>
 __global__ void __launch_bounds__(QD_WARPS * 32, 4) qmoe_decode_kernel(const QDecodeArgs a) {
   extern __shared__ __align__(128) uint8_t s_ring[];  // one ring per warp
   uint8_t* ring = s_ring + (threadIdx.x >> 5) * ring_bytes<BITS, GATED>();
@@ -375,13 +444,13 @@ __global__ void __launch_bounds__(QD_WARPS * 32, 4) qmoe_decode_kernel(const QDe
   for (int tok0 = 0; tok0 < cnt; tok0 += 8 * kMaxGroups) {
     const int groups = min(kMaxGroups, (cnt - tok0 + 7) / 8);
     if (groups <= 1)
-      run_pass<BITS, 1, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 1, GATED, kScale, RAW4>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
     else if (groups <= 2)
-      run_pass<BITS, 2, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 2, GATED, kScale, RAW4>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
     else if (groups <= 4 || kMaxGroups == 4)
-      run_pass<BITS, 4, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 4, GATED, kScale, RAW4>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
     else
-      run_pass<BITS, 8, GATED, kScale>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 8, GATED, kScale, RAW4>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
   }
 }
 
@@ -443,26 +512,35 @@ combine_partials_kernel(const float* __restrict__ part, int splits, int64_t rows
   out[static_cast<int64_t>(t) * H + c] = __float2half_rn(acc);
 }
 
-template <int BITS, bool GATED, int kScale>
+template <int BITS, bool GATED, int kScale, bool RAW4>
 cudaError_t launch_decode_t(const QDecodeArgs& a, cudaStream_t s) {
   constexpr int kSmem = QD_WARPS * ring_bytes<BITS, GATED>();
   static bool attr_set = false;  // idempotent; a race between first callers is benign
   if (!attr_set) {
-    cudaError_t st = cudaFuncSetAttribute(qmoe_decode_kernel<BITS, GATED, kScale>,
+    cudaError_t st = cudaFuncSetAttribute(qmoe_decode_kernel<BITS, GATED, kScale, RAW4>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (st != cudaSuccess) return st;
     attr_set = true;
   }
   const dim3 grid((a.N + QD_WARPS * 16 - 1) / (QD_WARPS * 16), a.E, a.splits);
-  qmoe_decode_kernel<BITS, GATED, kScale><<<grid, QD_WARPS * 32, kSmem, s>>>(a);
+  qmoe_decode_kernel<BITS, GATED, kScale, RAW4><<<grid, QD_WARPS * 32, kSmem, s>>>(a);
   return cudaGetLastError();
 }
 
+// The biased-code int4 kernels run exactly when the caller supplied the arranged
+// activations and offset terms (xcorr); every other combination runs per-code conversion.
 template <int BITS, bool GATED>
 cudaError_t launch_decode_b(const QDecodeArgs& a, cudaStream_t s) {
-  if (a.block_size == 0) return launch_decode_t<BITS, GATED, kScaleRow>(a, s);
-  if (a.block_size % QD_CHUNK == 0) return launch_decode_t<BITS, GATED, kScaleChunk>(a, s);
-  return launch_decode_t<BITS, GATED, kScaleElem>(a, s);
+  const bool raw = a.xcorr != nullptr;
+  if (BITS == 4 && raw && a.block_size % QD_CHUNK != 0 && a.block_size != 0)
+    return cudaErrorInvalidValue;
+  if (a.block_size == 0)
+    return raw ? launch_decode_t<BITS, GATED, kScaleRow, BITS == 4>(a, s)
+               : launch_decode_t<BITS, GATED, kScaleRow, false>(a, s);
+  if (a.block_size % QD_CHUNK == 0)
+    return raw ? launch_decode_t<BITS, GATED, kScaleChunk, BITS == 4>(a, s)
+               : launch_decode_t<BITS, GATED, kScaleChunk, false>(a, s);
+  return launch_decode_t<BITS, GATED, kScaleElem, false>(a, s);
 }
 
 }  // namespace
@@ -478,6 +556,15 @@ cudaError_t launch_qmoe_decode(const QDecodeArgs& a, int max_experts_touched, cu
   (void)max_experts_touched;
   if (a.bits == 4) return a.gated ? launch_decode_b<4, true>(a, s) : launch_decode_b<4, false>(a, s);
   return a.gated ? launch_decode_b<8, true>(a, s) : launch_decode_b<8, false>(a, s);
+}
+
+cudaError_t launch_qdec_prep(const __half* x, int64_t rows, int K, __half* xp, float* corr,
+                             cudaStream_t s) {
+  const int64_t groups = rows * (K / 8);
+  if (groups == 0) return cudaSuccess;
+  qdec_prep_kernel<<<static_cast<unsigned>((groups + 255) / 256), 256, 0, s>>>(x, rows, K, xp,
+                                                                                 corr);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s) {

@@ -36,6 +36,11 @@ struct QDecodeArgs {
                               // (gated: gate sums at [0, N), linear sums at [N, 2N))
   int64_t ldo;
   int splits;
+  // int4 with exact codes (block_size 0 or a multiple of 128): if set, `x` holds the
+  // activations arranged by launch_qdec_prep and xcorr[x row][chunk] the offset term, and
+  // the MMA runs on the biased codes (1024 + q in the low nibble, 1024 + 16 q in the high
+  // nibble) with no per-code arithmetic; the chunk sums subtract xcorr.
+  const float* xcorr = nullptr;
 };
 
 // Rows of T*k up to which the decode kernels replace dequantise + tensor-core GEMM.
@@ -45,6 +50,12 @@ constexpr int kQmoeMaxSplits = 8;
 constexpr int64_t kQmoeFusedMaxRows = 16384;
 
 bool qmoe_decode_supported(int dtype, int bits, int block_size, int64_t H, int64_t I);
+// Activations for the biased-code int4 path: x [rows, K] -> xp [rows, K] (each group of 8,
+// x0..x7, stored as (x0,x4)(x1/16,x5/16)(x2,x6)(x3/16,x7/16): the mma.sync B fragments of
+// the decode kernel's k order, odd slots scaled to match the in-place high nibbles) and
+// corr [rows, K/128] = per 128-wide chunk, 1032 * sum(even slots) + 1152 * sum(odd, scaled).
+cudaError_t launch_qdec_prep(const __half* x, int64_t rows, int K, __half* xp, float* corr,
+                             cudaStream_t s);
 cudaError_t launch_qmoe_decode(const QDecodeArgs& a, int max_experts_touched, cudaStream_t s);
 // act = activation(sum of fc1 partials + bias), fp16 [rows, N].
 cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s);
