@@ -322,10 +322,37 @@ def bench_ours(args, cfg, rank, world, dev):
         barrier()
         return max_over_ranks(e0.elapsed_time(e1)) / steps
 
-    # ---- device-resident throughput (plain layer calls: no events inside the timed loop)
+    # ---- device-resident throughput.  Inside the timed loop every call records CUDA
+    # events at the fc1 and fc2 boundaries only (three events, a few us per call), so the
+    # dominant kernel's roofline comes from the timed region itself.
+    i_fc1, i_fc2 = pkg.STAGES.index("fc1"), pkg.STAGES.index("fc2")
+    gemm_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)]
+               for _ in range(args.steps)]
+    for row in gemm_ev:
+        for ev in row:
+            ev.record(stream)  # creates the event handle
+    torch.cuda.synchronize(dev)
+    it_ev = iter(gemm_ev)
+
+    def timed_call():
+        row = next(it_ev)
+        evs = [None] * (len(pkg.STAGES) + 1)
+        evs[i_fc1], evs[i_fc2], evs[i_fc2 + 1] = row
+        return pkg.forward_staged(prob, tens, ws, evs, stream)
+
+    warm_left = [args.warmup]  # timed() runs the warm-up calls first
+
+    def step():
+        if warm_left[0] > 0:
+            warm_left[0] -= 1
+            return pkg.forward(prob, tens, ws, stream)
+        return timed_call()
+
     with ClockSampler(dev.index) as clk:
-        ms = timed(lambda: pkg.forward(prob, tens, ws, stream), args.steps)
+        ms = timed(step, args.steps)
     value = world * T / (ms / 1e3)
+    gemm_ms = {"fc1": statistics.median(r[0].elapsed_time(r[1]) for r in gemm_ev),
+               "fc2": statistics.median(r[1].elapsed_time(r[2]) for r in gemm_ev)}
 
     # ---- per-stage times: the same number of back-to-back calls right after the timed
     # loop, with the stage boundaries recorded as CUDA events on the stream (no
@@ -387,19 +414,19 @@ def bench_ours(args, cfg, rank, world, dev):
     alg = algorithmic(cfg, L, pkg)
     decode = cfg["kind"] == "qmoe" and T * cfg["k"] <= 512  # the library's decode threshold
     if decode:
-        achieved = alg["bytes_fc1"] / (stage_ms["fc1"] / 1e3) / 1e9
+        achieved = alg["bytes_fc1"] / (gemm_ms["fc1"] / 1e3) / 1e9
         roof = {"bound": "hbm", "kernel": "qmoe_decode_kernel (fc1+fc3 pass)",
                 "achieved": round(achieved, 1), "peak": pk["hbm"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm"], 4), "traffic": None,
                 "peak_source": f"{pk['src']} HBM copy (MEASURED_PEAKS.json)",
                 "alg_bytes_per_launch": int(alg["bytes_fc1"]),
-                "fc2": {"achieved": round(alg["bytes_fc2"] / (stage_ms["fc2"] / 1e3) / 1e9, 1)},
+                "fc2": {"achieved": round(alg["bytes_fc2"] / (gemm_ms["fc2"] / 1e3) / 1e9, 1)},
                 "experts_touched": alg["touched"],
                 "layer_frac": round((alg["bytes"] / pk["hbm"] / 1e9) / (ms / 1e3), 4)}
     else:
         k_name = ("simt_gemm_kernel (FFMA)" if cfg["kind"] == "moe" and cfg["dtype"] == "float32"
                   else "tc_pair_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)")
-        achieved = alg["flops_fc1"] / (stage_ms["fc1"] / 1e3) / 1e12
+        achieved = alg["flops_fc1"] / (gemm_ms["fc1"] / 1e3) / 1e12
         roof_t = max(alg["flops"] / (pk["tflops"] * 1e12), alg["bytes"] / (pk["hbm"] * 1e9))
         roof = {"bound": "tensor", "kernel": k_name, "achieved": round(achieved, 1),
                 "peak": pk["tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["tflops"], 4),
@@ -407,7 +434,7 @@ def bench_ours(args, cfg, rank, world, dev):
                 "frac_of_sustained": round(achieved / pk["tflops_sus"], 4) if pk["tflops_sus"] else None,
                 "traffic": FC1_TRAFFIC_BYTES if (args.config == "c2" and T == 4096) else None,
                 "alg_flops_per_launch": alg["flops_fc1"],
-                "fc2": {"achieved": round(alg["flops_fc2"] / (stage_ms["fc2"] / 1e3) / 1e12, 1)},
+                "fc2": {"achieved": round(alg["flops_fc2"] / (gemm_ms["fc2"] / 1e3) / 1e12, 1)},
                 "layer_frac": round(roof_t / (ms / 1e3), 4)}
     # Launches per layer call: route, scan, permute, gather, fc1, fc2, combine; QMoE
     # prefill adds three dequantisation launches.
@@ -425,6 +452,7 @@ def bench_ours(args, cfg, rank, world, dev):
                          if alg["bytes"] > 126e6 else "inputs smaller than L2 (not flushed)"},
         "e2e": e2e, "roofline": roof,
         "stage_ms": {s: round(v, 4) for s, v in stage_ms.items()},
+        "gemm_ms_in_timed_loop": {s: round(v, 4) for s, v in gemm_ms.items()},
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }

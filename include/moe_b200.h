@@ -161,8 +161,8 @@ int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tenso
                            float* stage_ms, int32_t num_stages);
 
 /* moe_b200_forward that also records the caller's CUDA events (cudaEvent_t handles,
- * num_events >= 8) on `stream` at the stage boundaries: events[i] .. events[i+1] brackets
- * stage i in the order of moe_b200_forward_timed.  No synchronisation, so back-to-back
+ * num_events >= 8; NULL entries are skipped) on `stream` at the stage boundaries:
+ * events[i] .. events[i+1] brackets stage i in the order of moe_b200_forward_timed.  No synchronisation, so back-to-back
  * calls keep the device busy and the stage times are those of a steady stream of calls.
  * A measurement aid; it has no counterpart in the reference. */
 int moe_b200_forward_staged(const moe_b200_problem* problem, const moe_b200_tensors* t,

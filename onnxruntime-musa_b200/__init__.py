@@ -458,13 +458,14 @@ def forward_timed(problem: Problem, tensors: Mapping[str, Any], workspace, strea
 def forward_staged(problem: Problem, tensors: Mapping[str, Any], workspace, events,
                    stream=None) -> None:
     """``forward`` that records ``events`` (len(STAGES) + 1 ``torch.cuda.Event`` objects
-    with timing, each recorded at least once before) at the stage boundaries, without
-    synchronising; ``events[i].elapsed_time(events[i + 1])`` is stage i."""
+    with timing, each recorded at least once before, or None to skip a boundary) at the
+    stage boundaries, without synchronising; ``events[i].elapsed_time(events[i + 1])`` is
+    stage i."""
     t = Tensors()
     for name, _ in Tensors._fields_:
         v = tensors.get(name)
         setattr(t, name, None if v is None else (v if isinstance(v, int) else v.data_ptr()))
-    handles = (_VP * len(events))(*[ev.cuda_event for ev in events])
+    handles = (_VP * len(events))(*[None if ev is None else ev.cuda_event for ev in events])
     check(lib().moe_b200_forward_staged(ctypes.byref(problem), ctypes.byref(t),
                                         workspace.data_ptr(), workspace.numel(),
                                         _stream_handle(stream), handles, len(events)))

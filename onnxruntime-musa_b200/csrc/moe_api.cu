@@ -274,7 +274,7 @@ enum Stage { kStRoute = 0, kStPlan, kStGather, kStDequant, kStFc1, kStFc2, kStCo
 int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
                  size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev = nullptr,
                  const int32_t* given_idx = nullptr) {
-  auto mark = [&](int i) { if (ev) cudaEventRecord(ev[i], s); };
+  auto mark = [&](int i) { if (ev && ev[i]) cudaEventRecord(ev[i], s); };
   const WsLayout L = plan_workspace(p);
   if (ws_bytes < L.total)
     return fail(MOE_B200_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than %zu",
@@ -674,14 +674,12 @@ int moe_b200_forward_staged(const moe_b200_problem* problem, const moe_b200_tens
     return fail(MOE_B200_INVALID_ARGUMENT, "tensors/events NULL or num_events < %d",
                 kNumStages + 1);
   cudaEvent_t ev[kNumStages + 1];
-  for (int i = 0; i <= kNumStages; ++i) {
-    if (events[i] == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "events[%d] is NULL", i);
-    ev[i] = static_cast<cudaEvent_t>(events[i]);
-  }
+  for (int i = 0; i <= kNumStages; ++i) ev[i] = static_cast<cudaEvent_t>(events[i]);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = forward_impl(*problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes, s, ev);
   if (st == MOE_B200_OK && problem->num_rows == 0)
-    for (int i = 0; i <= kNumStages; ++i) MOE_CUDA_CHECK(cudaEventRecord(ev[i], s), "event");
+    for (int i = 0; i <= kNumStages; ++i)
+      if (ev[i]) MOE_CUDA_CHECK(cudaEventRecord(ev[i], s), "event");
   return st;
 }
 

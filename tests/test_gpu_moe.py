@@ -411,3 +411,12 @@ def test_stage_timing_entries(pkg, orc, dev):
     np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
     with pytest.raises(pkg.InvalidArgument):
         pkg.forward_staged(prob, tens, ws, evs[:3], stream)
+    # Only the fc1 boundaries recorded (None entries are skipped).
+    i1 = pkg.STAGES.index("fc1")
+    sparse = [None] * (len(pkg.STAGES) + 1)
+    sparse[i1], sparse[i1 + 1] = evs[0], evs[1]
+    out.zero_()
+    pkg.forward_staged(prob, tens, ws, sparse, stream)
+    torch.cuda.synchronize(dev)
+    assert evs[0].elapsed_time(evs[1]) > 0
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
