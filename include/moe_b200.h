@@ -62,7 +62,8 @@ typedef struct moe_b200_attrs {
   int32_t activation_type;          /* MOE_B200_ACT_* */
   int32_t k;                        /* experts per token */
   int32_t normalize_routing_weights;
-  int32_t use_sparse_mixer;         /* must be 0 */
+  int32_t use_sparse_mixer;         /* 1: sparse-mixer top-2 routing (k must be 2;
+                                       normalize_routing_weights is then ignored) */
   int32_t swiglu_fusion;            /* 0: fc3 is the linear half; 1 interleaved; 2 halves */
   float swiglu_limit;               /* +inf disables clamping */
   float activation_alpha;
@@ -197,7 +198,10 @@ int moe_b200_ep_combine(int32_t dtype, int64_t num_rows, int64_t hidden_size, in
 
 /* Router: softmax + top-k (+ renormalisation) of every row of router_probs
  * [T, E] (dtype FLOAT/FLOAT16/BFLOAT16).  expert_idx int32 [T, k],
- * route_weight float [T, k].  Analog of the reference's Softmax + TopK
+ * route_weight float [T, k].  normalize_routing_weights: 0 = probabilities of the full
+ * softmax, 1 = softmax over the k selected, 2 = sparse-mixer top-2 (k = 2: each pick's
+ * weight is its softmax probability over the experts within 2 * 0.01 relative distance
+ * of the pick's logit).  Analog of the reference's Softmax + TopK
  * (musa/ep/src/kernels/math/softmax_impl.mu:49, topk_impl.mu:46-65). */
 int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
                    int64_t num_experts, int32_t k, int32_t normalize_routing_weights,

@@ -121,6 +121,11 @@ WsLayout plan_workspace(const moe_b200_problem& p) {
   return L;
 }
 
+// Routing mode of a layer call (launch_route's `normalize` argument).
+int route_mode(const moe_b200_problem& p) {
+  return p.attrs.use_sparse_mixer ? kRouteSparseMixer : (p.attrs.normalize_routing_weights ? 1 : 0);
+}
+
 int validate_problem(const moe_b200_problem* p) {
   if (p == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "problem is NULL");
   if (!is_float_type(p->dtype))
@@ -139,8 +144,10 @@ int validate_problem(const moe_b200_problem* p) {
                 kMaxK);
   if (a.activation_type < MOE_B200_ACT_RELU || a.activation_type > MOE_B200_ACT_SWIGLU)
     return fail(MOE_B200_INVALID_ARGUMENT, "invalid activation_type %d", a.activation_type);
-  if (a.use_sparse_mixer != 0)
-    return fail(MOE_B200_NOT_IMPLEMENTED, "use_sparse_mixer=1 is not supported");
+  if (a.use_sparse_mixer != 0 && a.use_sparse_mixer != 1)
+    return fail(MOE_B200_INVALID_ARGUMENT, "use_sparse_mixer=%d must be 0 or 1", a.use_sparse_mixer);
+  if (a.use_sparse_mixer != 0 && a.k != 2)
+    return fail(MOE_B200_INVALID_ARGUMENT, "use_sparse_mixer=1 routes top-2: k=%d must be 2", a.k);
   if (a.swiglu_fusion < 0 || a.swiglu_fusion > 2)
     return fail(MOE_B200_INVALID_ARGUMENT, "swiglu_fusion=%d must be 0, 1 or 2", a.swiglu_fusion);
   if (a.activation_type == MOE_B200_ACT_SWIGLU && a.swiglu_fusion == 0 && !p->has_fc3)
@@ -347,7 +354,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
     // touched experts are streamed once (token rows are read in place: no gather).
     mark(kStRoute);
     MOE_CUDA_CHECK(launch_small_dispatch(p.dtype, t.router_probs, T, E, k,
-                                         p.attrs.normalize_routing_weights, idx, w, offs, pos,
+                                         route_mode(p), idx, w, offs, pos,
                                          src, s, err),
                    "route");
     mark(kStPlan);
@@ -368,7 +375,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   if (given_idx == nullptr) {
     mark(kStRoute);
     MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
-                                p.attrs.normalize_routing_weights, idx, w, cc, s, chunk, err),
+                                route_mode(p), idx, w, cc, s, chunk, err),
                    "route");
     mark(kStPlan);
     MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s, chunk),
@@ -540,7 +547,7 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
 
   // Route and plan over all E experts (expert-ordered rows of this rank's tokens).
   MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
-                              p.attrs.normalize_routing_weights, i32(L.idx),
+                              route_mode(p), i32(L.idx),
                               reinterpret_cast<float*>(ws + L.w), i32(L.cc), s, chunk),
                  "route");
   if (T > 0)
@@ -714,7 +721,7 @@ int moe_b200_ep_dispatch(const moe_b200_problem* problem, const void* router_pro
   auto* t256 = reinterpret_cast<int32_t*>(ws + L.tiles256);
   auto* src = reinterpret_cast<int32_t*>(ws + L.src);
   const int chunk = layer_route_chunk(T);
-  MOE_CUDA_CHECK(launch_route(p.dtype, router_probs, T, E, k, p.attrs.normalize_routing_weights,
+  MOE_CUDA_CHECK(launch_route(p.dtype, router_probs, T, E, k, route_mode(p),
                               idx, route_weight, cc, s, chunk),
                  "route");
   MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, expert_offsets, t128, t64, t256, permuted_pos,
@@ -758,6 +765,10 @@ int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
   if (num_experts < 1 || num_experts > kMaxExperts || k < 1 || k > num_experts || k > kMaxK ||
       num_rows < 0)
     return fail(MOE_B200_INVALID_ARGUMENT, "invalid routing shape");
+  if (normalize_routing_weights < 0 || normalize_routing_weights > kRouteSparseMixer ||
+      (normalize_routing_weights == kRouteSparseMixer && k != 2))
+    return fail(MOE_B200_INVALID_ARGUMENT,
+                "routing mode %d: 0, 1, or 2 (sparse mixer, k = 2)", normalize_routing_weights);
   if (num_rows == 0) return MOE_B200_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int32_t* cc = nullptr;

@@ -21,6 +21,10 @@ inline int dtype_bytes(int dt) { return dt == kDtF32 ? 4 : (dt == kDtU8 ? 1 : 2)
 // Routing chunk: rows handled by one CTA of the router / permutation kernels (the
 // standalone stage entry points use kRouteChunk; a layer call sizes chunks to the GPU).
 constexpr int kRouteThreads = 256;
+// Routing mode passed as launch_route's `normalize`: 0 / 1 = softmax top-k without / with
+// renormalisation over the k selected; kRouteSparseMixer = the sparse-mixer top-2.
+constexpr int kRouteSparseMixer = 2;
+constexpr float kSparseMixerJitterEps = 0.01f;
 constexpr int kRouteChunk = 256;
 inline int num_route_chunks(int64_t rows, int chunk = kRouteChunk) {
   return static_cast<int>((rows + chunk - 1) / chunk);

@@ -19,6 +19,50 @@ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ?
 // Routes one row with one warp; lane l holds logits l, l+32, ...  Selection compares
 // fp32 values, ties to the lower index; NaN logits are read as -inf.  Lanes r < k
 // receive the r-th selected expert and its weight.
+// Sparse-mixer top-2 (the router of Phi-3.5-MoE, inference form): for each of the two
+// picks, m = the largest remaining logit, e* its expert (ties -> lower index); experts with
+// (m - s_e) / max(|s_e|, m) > 2 * jitter_eps are dropped and the pick's weight is its
+// softmax probability over the experts kept (the second pick also excludes the first).
+// The mask tests are IEEE fp32 operations, so the kept sets are reproducible.
+template <int kPerLane>
+__device__ __forceinline__ void sparse_mixer_row(const float (&v)[kPerLane], int E, int lane,
+                                                 int& my_idx, float& my_w) {
+  uint32_t taken = 0;
+  for (int r = 0; r < 2; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !(taken & (1u << j)) && (v[j] > bv || (v[j] == bv && e < bi))) {
+        bv = v[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int e = lane + 32 * j;
+      if (e >= E || (taken & (1u << j))) continue;
+      const float ratio = (bv - v[j]) / fmaxf(fabsf(v[j]), bv);
+      if (!(ratio > 2.0f * kSparseMixerJitterEps)) sum += expf(v[j] - bv);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == r) {
+      my_idx = bi;
+      my_w = 1.0f / sum;
+    }
+  }
+}
+
 template <typename T, int kPerLane>
 __device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int k, int normalize,
                                           int lane, int& my_idx, float& my_w) {
@@ -32,6 +76,12 @@ __device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int 
       if (x != x) x = -INFINITY;
     }
     v[j] = x;
+  }
+  if (normalize == kRouteSparseMixer) {
+    my_idx = 0;
+    my_w = 0.f;
+    sparse_mixer_row<kPerLane>(v, E, lane, my_idx, my_w);
+    return;
   }
   // Row max and softmax denominator (fixed butterfly order: deterministic).
   float m = v[0];

@@ -70,6 +70,11 @@ extern "C" int moe_b200_route_noalloc(const void* router_probs, int32_t dtype,
   if (num_experts < 1 || num_experts > moe::kMaxExperts || k < 1 || k > num_experts ||
       k > moe::kMaxK || num_rows < 0)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT, "invalid routing shape");
+  if (normalize_routing_weights < 0 || normalize_routing_weights > moe::kRouteSparseMixer ||
+      (normalize_routing_weights == moe::kRouteSparseMixer && k != 2))
+    return moe::set_error(MOE_B200_INVALID_ARGUMENT,
+                          "routing mode %d: 0, 1, or 2 (sparse mixer, k = 2)",
+                          normalize_routing_weights);
   const int64_t need = static_cast<int64_t>(moe::num_route_chunks(num_rows)) * num_experts;
   if (need > kNoallocScratchInts)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT,

@@ -23,6 +23,9 @@ Conventions fixed here (and by the CUDA kernels, bit for bit where integer):
   taken over the k selected logits; without it, over all E logits and the k
   selected probabilities are returned (softmax over the row, analog
   ``musa/ep/src/kernels/math/softmax_impl.mu:49-84``, fp32-or-wider accumulation).
+  ``use_sparse_mixer=1`` (k = 2) is the sparse-mixer router published with Phi-3.5-MoE
+  (``sparsemixer``, inference form, jitter_eps = 0.01), restated in
+  ``route_sparse_mixer``; the ORT 1.26.0 source that would pin its details is absent.
 * Permutation (``permutation``): rows routed to expert e are laid out contiguously,
   experts ascending; inside one expert, by token then by slot j.  ``offsets[e]`` is the
   exclusive prefix sum of the per-expert counts (analog: the reference's CumSum,
@@ -54,7 +57,41 @@ ACTIVATIONS = ("relu", "gelu", "silu", "identity", "swiglu")
 
 # ----------------------------------------------------------------------------- routing
 
-def route(router_probs: np.ndarray, k: int, normalize_routing_weights: int):
+SPARSE_MIXER_JITTER_EPS = 0.01
+
+
+def route_sparse_mixer(router_probs: np.ndarray, jitter_eps: float = SPARSE_MIXER_JITTER_EPS):
+    """Sparse-mixer top-2 routing.  For each of two picks: m = the largest remaining
+    logit and e* its expert (ties to the lower index; the second pick excludes the first);
+    experts with ``(m - s_e) / max(|s_e|, m) > 2 * jitter_eps`` are dropped, and the pick's
+    weight is ``1 / sum over kept e of exp(s_e - m)`` (its softmax probability over the
+    kept experts).  The mask tests are evaluated in IEEE float32, as the kernel does."""
+    s = np.asarray(router_probs).astype(np.float32)
+    s = np.where(np.isnan(s), np.float32(-np.inf), s)
+    T, E = s.shape
+    if E < 2:
+        raise ValueError("the sparse mixer needs at least two experts")
+    idx = np.zeros((T, 2), dtype=np.int32)
+    w = np.zeros((T, 2), dtype=np.float32)
+    thr = np.float32(2.0) * np.float32(jitter_eps)
+    avail = np.ones((T, E), dtype=bool)
+    rows = np.arange(T)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        for r in range(2):
+            cand = np.where(avail, s, np.float32(-np.inf))
+            pick = np.argmax(cand, axis=1)          # first maximum: the lower index
+            m = cand[rows, pick][:, None]
+            ratio = (m - s) / np.maximum(np.abs(s), m)   # float32 throughout
+            keep = avail & ~(ratio > thr)
+            den = np.where(keep, np.exp(s.astype(np.float64) - m.astype(np.float64)), 0.0)
+            idx[:, r] = pick
+            w[:, r] = (1.0 / den.sum(axis=1)).astype(np.float32)
+            avail[rows, pick] = False
+    return idx, w
+
+
+def route(router_probs: np.ndarray, k: int, normalize_routing_weights: int,
+          use_sparse_mixer: int = 0):
     """Top-k routing of every row.  Returns (expert_idx int32 [T,k], weight f32 [T,k]).
 
     The tie rule (value descending, lower index first) follows
@@ -62,6 +99,10 @@ def route(router_probs: np.ndarray, k: int, normalize_routing_weights: int):
     ``musa/ep/src/kernels/math/softmax_impl.mu:49-84`` (max-subtracted exp, sum,
     divide), evaluated here in float64.
     """
+    if use_sparse_mixer:
+        if k != 2:
+            raise ValueError("use_sparse_mixer routes top-2 (k must be 2)")
+        return route_sparse_mixer(router_probs)
     logits = np.asarray(router_probs).astype(np.float32)
     logits = np.where(np.isnan(logits), np.float32(-np.inf), logits)  # NaN reads as -inf
     T, E = logits.shape
@@ -201,7 +242,7 @@ def expert_ffn(xe, W1, b1, W2, b2, W3=None, b3=None, *, activation_type="relu",
 def moe(x, router_probs, fc1_w, fc1_b, fc2_w, fc2_b, fc3_w=None, fc3_b=None, *,
         activation_type="relu", k=1, normalize_routing_weights=0, swiglu_fusion=0,
         activation_alpha=1.0, activation_beta=0.0, swiglu_limit=math.inf,
-        return_routing=False):
+        use_sparse_mixer=0, return_routing=False):
     """float64 reference of one MoE layer call.  ``x`` is [T,H] (or [B,S,H]);
     ``fc*_w`` are [E, N, K] (already dequantised for QMoE)."""
     x = np.asarray(x)
@@ -209,7 +250,8 @@ def moe(x, router_probs, fc1_w, fc1_b, fc2_w, fc2_b, fc3_w=None, fc3_b=None, *,
     X = x.reshape(-1, shape[-1]).astype(np.float64)
     T, H = X.shape
     E = fc1_w.shape[0]
-    idx, w = route(np.asarray(router_probs).reshape(T, E), k, normalize_routing_weights)
+    idx, w = route(np.asarray(router_probs).reshape(T, E), k, normalize_routing_weights,
+                   use_sparse_mixer)
     out = np.zeros((T, H), dtype=np.float64)
     sel = lambda a, e: None if a is None else np.asarray(a)[e]
     for e in range(E):

@@ -69,7 +69,8 @@ def test_workspace_planning(pkg):
 
 @pytest.mark.parametrize("kw,exc,msg", [
     (dict(k=9), "InvalidArgument", "k=9"),
-    (dict(use_sparse_mixer=1), "NotImplementedByEP", "sparse_mixer"),
+    (dict(use_sparse_mixer=1, k=3), "InvalidArgument", "must be 2"),
+    (dict(use_sparse_mixer=2), "InvalidArgument", "use_sparse_mixer=2"),
     (dict(activation_type="swiglu"), "InvalidArgument", "needs fc3"),
     (dict(activation_type="swiglu", swiglu_fusion=3), "InvalidArgument", "swiglu_fusion"),
     (dict(expert_weight_bits=4, block_size=24), "InvalidArgument", "block_size"),
@@ -80,6 +81,12 @@ def test_problem_validation(pkg, kw, exc, msg):
     p = pkg.make_problem(16, 64, 64, 8, pkg.FLOAT16, **base)
     with pytest.raises(getattr(pkg, exc), match=msg):
         pkg.workspace_size(p)
+
+
+def test_sparse_mixer_problem_accepted(pkg):
+    p = pkg.make_problem(16, 64, 64, 8, pkg.FLOAT16, k=2, activation_type="silu",
+                         use_sparse_mixer=1)
+    assert pkg.workspace_size(p) > 0
 
 
 def test_no_device_is_zero_devices(pkg):

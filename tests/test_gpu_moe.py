@@ -420,3 +420,31 @@ def test_stage_timing_entries(pkg, orc, dev):
     torch.cuda.synchronize(dev)
     assert evs[0].elapsed_time(evs[1]) > 0
     np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+
+
+@pytest.mark.parametrize("case", ["fp16_gated", "bf16_plain_bias", "fp32_simt"])
+def test_moe_sparse_mixer(pkg, orc, dev, case):
+    """use_sparse_mixer=1 through the whole layer (tensor-core and FFMA GEMM paths)."""
+    dtype_name = {"fp16_gated": "float16", "bf16_plain_bias": "bfloat16",
+                  "fp32_simt": "float32"}[case]
+    gated = case == "fp16_gated"
+    inp = orc.make_moe_inputs(T=300, H=256, I=384, E=8, k=2, act="silu" if gated else "gelu",
+                              gated=gated, dtype="float32", bias=case != "fp16_gated",
+                              normalize=1, seed=101)
+    inp["router_probs"] *= 0.05  # close logits: the 2% band keeps several experts
+    d, h = moe_inputs_on(dev, inp, dtype_name)
+    attrs = dict(inp["attrs"], use_sparse_mixer=1)
+    out = run_moe(pkg, d, attrs)
+    np.testing.assert_allclose(as_np(out), oracle_out(orc, h, attrs), **TOL[dtype_name])
+
+
+@pytest.mark.parametrize("T", [5, 300])  # decode kernels; dequantise + GEMM
+def test_qmoe_sparse_mixer(pkg, orc, dev, T):
+    q = orc.make_qmoe_inputs(T=T, H=256, I=256, E=8, k=2, bits=4, block_size=128,
+                             scale_mu=-5.0, scale_sigma=0.3, seed=T + 5)
+    q["router_probs"] = (q["router_probs"].astype(np.float32) * 0.05).astype(np.float16)
+    attrs = dict(q["attrs"], use_sparse_mixer=1)
+    out = _qmoe_run(pkg, dev, q, attrs)
+    ref = orc.qmoe(q["x"], q["router_probs"], q["fc1_q"], q["fc1_scales"], None, q["fc2_q"],
+                   q["fc2_scales"], None, q["fc3_q"], q["fc3_scales"], None, **attrs)
+    np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])

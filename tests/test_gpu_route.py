@@ -75,3 +75,20 @@ def test_route_deterministic(pkg, dev):
     a = pkg.route(lg, 8, 1)
     b = pkg.route(lg, 8, 1)
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("dtype_name", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("E", [2, 8, 64, 256])
+@pytest.mark.parametrize("ties", [False, True])
+def test_route_sparse_mixer(pkg, orc, dev, dtype_name, E, ties):
+    """Routing mode 2 (sparse-mixer top-2): indices bit-exact, weights to fp32 rounding."""
+    T = 1000
+    lg = _logits(T, E, E * 7 + 3, ties, dtype_name)
+    lg[::7] *= 0.01  # logits close together: many experts inside the 2% band
+    d = to_dev(lg, dev, torch_dtype(dtype_name))
+    idx, w = pkg.route(d, 2, 2)
+    ridx, rw = orc.route(as_np(d).astype(np.float32), 2, 0, use_sparse_mixer=1)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    with pytest.raises(pkg.InvalidArgument):
+        pkg.route(d, 3, 2)

@@ -182,3 +182,25 @@ def test_golden_fixture(orc, path):
     np.testing.assert_array_equal(idx, d["expert_idx"])
     np.testing.assert_allclose(w, d["route_w"], rtol=0, atol=0)
     np.testing.assert_allclose(out, d["output"], rtol=1e-12, atol=1e-12)
+
+
+def test_sparse_mixer_known_answer(orc):
+    """Sparse-mixer top-2 on hand-computed rows: experts within 2 * 0.01 relative distance
+    of a pick's logit share its softmax; the second pick excludes the first."""
+    s = np.array([[2.0, 1.99, 0.0, 1.0],
+                  [-1.0, -1.01, -3.0, -1.015],
+                  [1.0, 1.0, 1.0, 1.0]], dtype=np.float32)
+    idx, w = orc.route(s, 2, 0, use_sparse_mixer=1)
+    assert idx.tolist() == [[0, 1], [0, 1], [0, 1]]
+    f = lambda d: math.exp(float(np.float32(d)))
+    # row 0: pick e0 keeps e1 (0.01 / 2 = 0.005); pick e1 keeps only itself.
+    np.testing.assert_allclose(w[0], [1 / (1 + f(1.99 - 2.0)), 1.0], rtol=1e-6)
+    # row 1 (negative logits: the factor is |s_e|): pick e0 keeps e1 (0.0099) and e3
+    # (0.0148); pick e1 keeps e3 (0.0049).
+    np.testing.assert_allclose(
+        w[1], [1 / (1 + f(-1.01 + 1.0) + f(-1.015 + 1.0)), 1 / (1 + f(-1.015 + 1.01))],
+        rtol=1e-6)
+    # row 2: all equal -> e0 over 4 kept, e1 over the 3 left.
+    np.testing.assert_allclose(w[2], [0.25, 1 / 3], rtol=1e-6)
+    with pytest.raises(ValueError):
+        orc.route(s, 3, 0, use_sparse_mixer=1)
