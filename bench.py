@@ -285,6 +285,38 @@ def cpu_baseline(cfg, L, budget_s=12.0):
 
 
 # ------------------------------------------------------------------ our arm
+def adjacent_ops(pkg, cfg, L, dev, stream, args, pk):
+    """The pre-MoE rows of the same tokens (residual add + RMS norm + router MatMul,
+    moe_b200_norm_router), timed with CUDA events against the HBM roofline."""
+    import torch
+    if cfg["kind"] != "moe" or cfg["dtype"] == "float32":
+        return None
+    x = L["x"]
+    T, H = x.shape
+    E = cfg["E"]
+    g = torch.Generator(device=dev).manual_seed(99)
+    skip = torch.randn(T, H, device=dev, generator=g).to(x.dtype)
+    gamma = 1.0 + 0.1 * torch.randn(H, device=dev, generator=g)
+    wr = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(x.dtype)
+    for _ in range(max(3, args.warmup)):
+        pkg.norm_router(x, gamma, 1e-6, wr, skip=skip, stream=stream)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        pkg.norm_router(x, gamma, 1e-6, wr, skip=skip, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    es = x.element_size()
+    # read x and skip once, write residual and normed, logits; gamma and the router weights
+    alg = 4 * T * H * es + T * E * es + H * 4 + E * H * es
+    gbs = alg / (ms / 1e3) / 1e9
+    return {"norm_router": {"ms": round(ms, 4), "alg_bytes": alg, "achieved_gbs": round(gbs, 1),
+                            "frac_of_hbm": round(gbs / pk["hbm"], 4),
+                            "what": "h = x + skip; rms-normalised h * gamma; router logits [T, E]"}}
+
+
 def bench_ours(args, cfg, rank, world, dev):
     import torch
     import __graft_entry__ as ge
@@ -411,6 +443,7 @@ def bench_ours(args, cfg, rank, world, dev):
            "serial_api": "moe_b200_kernel_compute, one call at a time (H2D, layer, D2H)"}
 
     pk = peaks()
+    adjacent = adjacent_ops(pkg, cfg, L, dev, stream, args, pk)
     alg = algorithmic(cfg, L, pkg)
     decode = cfg["kind"] == "qmoe" and T * cfg["k"] <= 512  # the library's decode threshold
     if decode:
@@ -452,6 +485,7 @@ def bench_ours(args, cfg, rank, world, dev):
                          if alg["bytes"] > 126e6 else "inputs smaller than L2 (not flushed)"},
         "e2e": e2e, "roofline": roof,
         "stage_ms": {s: round(v, 4) for s, v in stage_ms.items()},
+        "adjacent_ops": adjacent,
         "gemm_ms_in_timed_loop": {s: round(v, 4) for s, v in gemm_ms.items()},
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),

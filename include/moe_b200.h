@@ -268,6 +268,19 @@ int moe_b200_notification_destroy(void* event);
 int moe_b200_copy(void* dst, const void* src, size_t bytes, int32_t kind,
                   void* stream);
 
+/* Pre-MoE rows in one pass: h = input (+ skip), stored as residual_out when skip is set;
+ * normed = h * rsqrt(mean(h^2) + epsilon) * gamma (gamma fp32 [H]); router_logits [T, E]
+ * = normed . router_weight[e] (router_weight [E, H], fp32 accumulation over the rounded
+ * normed values).  The steps that produce an MoE node's input and router_probs in a
+ * transformer block: the plugin's fused RMS normalisation
+ * (musa/ep/src/fusion/rms_norm_fusion.cc:185, kernels/nn/rms_norm_impl.mu:10-45) and the
+ * router MatMul (kernels/math/matmul.cc:239-332).  hidden_size % 8 == 0; buffers 16-byte
+ * aligned; skip, residual_out and normed may be NULL. */
+int moe_b200_norm_router(int32_t dtype, int64_t num_rows, int64_t hidden_size,
+                         int64_t num_experts, const void* input, const void* skip,
+                         const float* gamma, float epsilon, const void* router_weight,
+                         void* residual_out, void* normed, void* router_logits, void* stream);
+
 /* --------------------------------------- device-side expert parallelism (P2P) */
 
 /* Expert-parallel layer over the GPUs of one node with no host synchronisation and no

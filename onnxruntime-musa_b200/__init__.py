@@ -124,6 +124,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                                   ctypes.POINTER(_SZ)]),
     "moe_b200_ep_forward": (ctypes.c_int, [_VP, ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                            _VP, _SZ, _VP]),
+    "moe_b200_norm_router": (ctypes.c_int, [_I32, _I64, _I64, _I64, _VP, _VP, _VP,
+                                            ctypes.c_float, _VP, _VP, _VP, _VP, _VP]),
     "moe_b200_pipeline_create": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                                 _I32, ctypes.POINTER(_VP)]),
     "moe_b200_pipeline_submit": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I64]),
@@ -568,6 +570,23 @@ class Pipeline:
 
 
 # ------------------------------------------------------------------ stages
+
+def norm_router(x, gamma, epsilon: float, router_weight, skip=None, stream=None):
+    """Pre-MoE rows on the GPU: (normed [T,H], router_logits [T,E], residual [T,H] or None).
+    ``residual`` = x + skip when ``skip`` is given; ``gamma`` is fp32 [H]."""
+    torch = _torch()
+    T, H = x.shape
+    E = router_weight.shape[0]
+    normed = torch.empty_like(x)
+    logits = torch.empty((T, E), dtype=x.dtype, device=x.device)
+    residual = torch.empty_like(x) if skip is not None else None
+    ptr = lambda t: None if t is None else t.data_ptr()
+    check(lib().moe_b200_norm_router(elem_type_of(x), T, H, E, x.data_ptr(), ptr(skip),
+                                     gamma.data_ptr(), float(epsilon), router_weight.data_ptr(),
+                                     ptr(residual), normed.data_ptr(), logits.data_ptr(),
+                                     _stream_handle(stream)))
+    return normed, logits, residual
+
 
 def route(router_probs, k: int, normalize_routing_weights: int, stream=None):
     """Top-k routing on the GPU: (expert_idx int32 [T,k], route_weight f32 [T,k])."""

@@ -783,6 +783,33 @@ int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
   return MOE_B200_OK;
 }
 
+int moe_b200_norm_router(int32_t dtype, int64_t num_rows, int64_t hidden_size,
+                         int64_t num_experts, const void* input, const void* skip,
+                         const float* gamma, float epsilon, const void* router_weight,
+                         void* residual_out, void* normed, void* router_logits, void* stream) {
+  if (!is_float_type(dtype)) return fail(MOE_B200_NOT_IMPLEMENTED, "unsupported dtype %d", dtype);
+  if (num_rows < 0 || hidden_size < 8 || hidden_size % 8 != 0 || num_experts < 1)
+    return fail(MOE_B200_INVALID_ARGUMENT,
+                "norm_router: rows >= 0, hidden_size a multiple of 8 and num_experts >= 1");
+  if (norm_router_smem_bytes(dtype, hidden_size) > 227 * 1024)
+    return fail(MOE_B200_NOT_IMPLEMENTED, "norm_router: hidden_size=%lld too large",
+                (long long)hidden_size);
+  if (num_rows == 0) return MOE_B200_OK;
+  if (input == nullptr || gamma == nullptr || router_weight == nullptr || router_logits == nullptr)
+    return fail(MOE_B200_INVALID_ARGUMENT, "norm_router: input, gamma, router_weight and "
+                                           "router_logits must be non-NULL");
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (!a16(input) || !a16(skip) || !a16(gamma) || !a16(router_weight) || !a16(residual_out) ||
+      !a16(normed))
+    return fail(MOE_B200_INVALID_ARGUMENT, "norm_router: buffers must be 16-byte aligned");
+  MOE_CUDA_CHECK(launch_norm_router(dtype, input, skip, gamma, epsilon, router_weight, num_rows,
+                                    static_cast<int>(hidden_size), static_cast<int>(num_experts),
+                                    skip != nullptr ? residual_out : nullptr, normed,
+                                    router_logits, static_cast<cudaStream_t>(stream)),
+                 "norm_router");
+  return MOE_B200_OK;
+}
+
 size_t moe_b200_permute_workspace_size(int64_t num_rows, int32_t k, int64_t num_experts) {
   (void)k;
   const size_t chunks = std::max<int64_t>(num_route_chunks(num_rows), 1);

@@ -67,6 +67,12 @@ cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s,
                             int* clear = nullptr);
 cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
                            int T, int k, int H, void* out, cudaStream_t s);
+// Residual add + RMS normalisation + router MatMul of the rows feeding an MoE node
+// (norm_router.cu); H % 8 == 0, 16-byte aligned rows.
+size_t norm_router_smem_bytes(int dtype, int64_t H);
+cudaError_t launch_norm_router(int dtype, const void* x, const void* skip, const float* gamma,
+                               float eps, const void* wr, int64_t rows, int H, int E,
+                               void* residual_out, void* normed, void* logits, cudaStream_t s);
 
 // One grouped GEMM pass over all experts:
 //   out[r, n] = epilogue( sum_k A[r, k] * B1[e(r), n, k] [, sum_k A[r, k] * B3[e(r), n, k]] )

@@ -125,6 +125,24 @@ def route(router_probs: np.ndarray, k: int, normalize_routing_weights: int,
     return idx, w.astype(np.float32)
 
 
+def norm_router(x, gamma, epsilon, router_weight, skip=None, dtype=np.float16):
+    """Pre-MoE rows: h = x (+ skip) summed in float32; residual = h in ``dtype``;
+    normed = dtype(h * 1/sqrt(mean(h^2) + eps) * gamma) (the reference's RmsNormKernel,
+    ``musa/ep/src/kernels/nn/rms_norm_impl.mu:10-45``: fp32 gamma, value * inv * gamma);
+    logits = dtype(normed . router_weight[e]) over the ROUNDED normed values (the router
+    MatMul consumes the stored tensor).  Norm and dot products in float64."""
+    h = np.asarray(x).astype(np.float32)
+    if skip is not None:
+        h = h + np.asarray(skip).astype(np.float32)
+    cast = (lambda a: a.astype(np.float32)) if dtype == "bfloat16" else (lambda a: a.astype(dtype))
+    residual = cast(h) if skip is not None else None
+    hd = h.astype(np.float64)
+    inv = 1.0 / np.sqrt((hd * hd).mean(axis=1, keepdims=True) + float(epsilon))
+    normed = cast(hd * inv * np.asarray(gamma, dtype=np.float64)[None, :])
+    logits = cast(normed.astype(np.float64) @ np.asarray(router_weight).astype(np.float64).T)
+    return normed, logits, residual
+
+
 def permutation(expert_idx: np.ndarray, num_experts: int):
     """Canonical dispatch order.  Returns (offsets int32 [E+1], pos int32 [T,k],
     src int32 [T*k]) where ``src[p]`` is the flat (t*k + j) routed row at permuted

@@ -204,3 +204,19 @@ def test_sparse_mixer_known_answer(orc):
     np.testing.assert_allclose(w[2], [0.25, 1 / 3], rtol=1e-6)
     with pytest.raises(ValueError):
         orc.route(s, 3, 0, use_sparse_mixer=1)
+
+
+def test_norm_router_known_answer(orc):
+    x = np.array([[3.0, 4.0, 0.0, 0.0]], dtype=np.float32)     # mean(x^2) = 25/4
+    skip = np.array([[1.0, -4.0, 0.0, 2.0]], dtype=np.float32)  # h = [4, 0, 0, 2], mean 5
+    gamma = np.array([1.0, 2.0, 1.0, 0.5], dtype=np.float32)
+    wr = np.array([[1.0, 0.0, 0.0, 0.0], [0.0, 0.0, 0.0, 1.0]], dtype=np.float32)
+    n, lg, res = orc.norm_router(x, gamma, 0.0, wr, dtype=np.float32)
+    np.testing.assert_allclose(n, [[3 / 2.5, 8 / 2.5, 0, 0]], rtol=1e-6)
+    np.testing.assert_allclose(lg, [[1.2, 0.0]], rtol=1e-6, atol=1e-7)
+    assert res is None
+    n, lg, res = orc.norm_router(x, gamma, 0.0, wr, skip=skip, dtype=np.float32)
+    r = math.sqrt(5.0)
+    np.testing.assert_allclose(res, [[4, 0, 0, 2]])
+    np.testing.assert_allclose(n, [[4 / r, 0, 0, 1 / r]], rtol=1e-6)
+    np.testing.assert_allclose(lg, [[4 / r, 1 / r]], rtol=1e-6)
