@@ -125,6 +125,14 @@ def route(router_probs: np.ndarray, k: int, normalize_routing_weights: int,
     return idx, w.astype(np.float32)
 
 
+def round_bf16(a) -> np.ndarray:
+    """float32 values rounded to the nearest bfloat16 (ties to even), kept as float32."""
+    u = np.ascontiguousarray(np.asarray(a, dtype=np.float32)).view(np.uint32)
+    r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    out = r.view(np.float32)
+    return np.where(np.isnan(a), np.float32(np.nan), out)
+
+
 def norm_router(x, gamma, epsilon, router_weight, skip=None, dtype=np.float16):
     """Pre-MoE rows: h = x (+ skip) summed in float32; residual = h in ``dtype``;
     normed = dtype(h * 1/sqrt(mean(h^2) + eps) * gamma) (the reference's RmsNormKernel,
@@ -134,7 +142,8 @@ def norm_router(x, gamma, epsilon, router_weight, skip=None, dtype=np.float16):
     h = np.asarray(x).astype(np.float32)
     if skip is not None:
         h = h + np.asarray(skip).astype(np.float32)
-    cast = (lambda a: a.astype(np.float32)) if dtype == "bfloat16" else (lambda a: a.astype(dtype))
+    cast = ((lambda a: round_bf16(np.asarray(a, dtype=np.float32))) if dtype == "bfloat16"
+            else (lambda a: a.astype(dtype)))
     residual = cast(h) if skip is not None else None
     hd = h.astype(np.float64)
     inv = 1.0 / np.sqrt((hd * hd).mean(axis=1, keepdims=True) + float(epsilon))

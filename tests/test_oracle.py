@@ -220,3 +220,10 @@ def test_norm_router_known_answer(orc):
     np.testing.assert_allclose(res, [[4, 0, 0, 2]])
     np.testing.assert_allclose(n, [[4 / r, 0, 0, 1 / r]], rtol=1e-6)
     np.testing.assert_allclose(lg, [[4 / r, 1 / r]], rtol=1e-6)
+
+
+def test_round_bf16_matches_torch(orc):
+    import torch
+    a = np.random.default_rng(0).standard_normal(20000).astype(np.float32) * 37
+    a[:4] = [0.0, -0.0, 1e-40, 3.3895313892515355e38]
+    assert np.array_equal(orc.round_bf16(a), torch.from_numpy(a).to(torch.bfloat16).float().numpy())
