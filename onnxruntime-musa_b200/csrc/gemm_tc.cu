@@ -85,6 +85,13 @@ struct TcParams {
   int remap_world;
   void* out_peers[kMaxEpRanks];
   int trace;   // diagnostics: CTA 0 records per-tile phase timestamps (MOE_B200_GEMM_TRACE)
+  // Packed operands with one scale per row (block_size 0): 0 = the converters apply
+  // (q - zp) * s; 1 = they write exact q - zp and the epilogue multiplies column n by its
+  // scale; 2 = they write the biased codes 1024 + q and the epilogue applies
+  // s_n * (acc - qbias * rowsum[row]) with qbias = 1024 + zp.
+  int qepi;
+  float qbias;
+  const float* rowsum;
 };
 
 // Per-tile phase trace of CTA 0 (diagnostics only).  Entry i: [2i] = %globaltimer ns,
@@ -209,46 +216,67 @@ __device__ __forceinline__ void add_bias(float (&v)[n], const void* bias, int e,
 constexpr int EPI_CHUNK = 32;                 // output columns per staged chunk
 constexpr int EPI_STAGE_BYTES = 32 * EPI_CHUNK * 2;  // per epilogue warp
 
+// Per-row-scaled packed operands (qepi 1 / 2): v[j] = s(col0 + j) * (v[j] - off), s the
+// scale of output column col0 + j of expert e in the operand's stored-row addressing.
+template <int n>
+__device__ __forceinline__ void q_scale_cols(float (&v)[n], const __half* scales, int rows_e,
+                                             int G, int g, int noff, int e, int col0, int N,
+                                             float off) {
+#pragma unroll
+  for (int j = 0; j < n; ++j) {
+    const int64_t srow = static_cast<int64_t>(e) * rows_e +
+                         static_cast<int64_t>(min(col0 + j, N - 1) + noff) * G + g;
+    v[j] = __half2float(__ldg(scales + srow)) * (v[j] - off);
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void epilogue_rows(const TcParams& p, uint32_t taddr, int row,
                                               bool valid, int e, int n0, int c0, int c1,
                                               uint8_t* stage, int lane) {
   const unsigned long long my_row =
       valid ? reinterpret_cast<unsigned long long>(out_row<T>(p, row)) : 0ull;
+  const float qoff = (p.qepi == 2 && valid) ? p.qbias * __ldg(p.rowsum + row) : 0.f;
   uint4* st_row = reinterpret_cast<uint4*>(stage + lane * (EPI_CHUNK * 2));
   const int wsw = (lane >> 1) & 3;
 #pragma unroll 1
   for (int c = c0; c < c1; c += EPI_CHUNK) {
     const int col = n0 + c;
-    float v[EPI_CHUNK];
-    if (p.gated) {
-      float g[EPI_CHUNK], u[EPI_CHUNK];
-      tmem_ld16(taddr + c, *reinterpret_cast<float(*)[16]>(&g[0]));
-      tmem_ld16(taddr + c + 16, *reinterpret_cast<float(*)[16]>(&g[16]));
-      tmem_ld16(taddr + BN / 2 + c, *reinterpret_cast<float(*)[16]>(&u[0]));
-      tmem_ld16(taddr + BN / 2 + c + 16, *reinterpret_cast<float(*)[16]>(&u[16]));
-      tmem_ld_wait();
-      add_bias<T, EPI_CHUNK>(g, p.bias1, e, col, p);
-      add_bias<T, EPI_CHUNK>(u, p.bias3, e, col, p);
-      act_gated_chunk<EPI_CHUNK>(p.ap, g, u);
+    // Two halves of 16 columns (fewer live registers), each packed into two granules.
 #pragma unroll
-      for (int j = 0; j < EPI_CHUNK; ++j) v[j] = g[j];
-    } else {
-      tmem_ld16(taddr + c, *reinterpret_cast<float(*)[16]>(&v[0]));
-      tmem_ld16(taddr + c + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
-      tmem_ld_wait();
-      add_bias<T, EPI_CHUNK>(v, p.bias1, e, col, p);
-      act_chunk<EPI_CHUNK>(p.ap.act, v);
-
-    }
+    for (int hs = 0; hs < 2; ++hs) {
+      const int ch = c + 16 * hs, colh = col + 16 * hs;
+      float v[16];
+      if (p.gated) {
+        float u[16];
+        tmem_ld16(taddr + ch, v);
+        tmem_ld16(taddr + BN / 2 + ch, u);
+        tmem_ld_wait();
+        if (p.qepi) {
+          q_scale_cols<16>(v, p.scales1, p.b1_rows, p.b1_G, p.b1_g, p.b1_noff, e, colh, p.N, qoff);
+          q_scale_cols<16>(u, p.scales3, p.b3_rows, p.b3_G, p.b3_g, p.b3_noff, e, colh, p.N, qoff);
+        }
+        add_bias<T, 16>(v, p.bias1, e, colh, p);
+        add_bias<T, 16>(u, p.bias3, e, colh, p);
+        act_gated_chunk<16>(p.ap, v, u);
+      } else {
+        tmem_ld16(taddr + ch, v);
+        tmem_ld_wait();
+        if (p.qepi)
+          q_scale_cols<16>(v, p.scales1, p.b1_rows, p.b1_G, p.b1_g, p.b1_noff, e, colh, p.N, qoff);
+        add_bias<T, 16>(v, p.bias1, e, colh, p);
+        act_chunk<16>(p.ap.act, v);
+      }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      w.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
-      w.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
-      w.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
-      w.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
-      st_row[q ^ wsw] = w;
+      for (int qq = 0; qq < 2; ++qq) {
+        const int q = 2 * hs + qq;
+        uint4 w;
+        w.x = pack2<T>(v[8 * qq + 0], v[8 * qq + 1]);
+        w.y = pack2<T>(v[8 * qq + 2], v[8 * qq + 3]);
+        w.z = pack2<T>(v[8 * qq + 4], v[8 * qq + 5]);
+        w.w = pack2<T>(v[8 * qq + 6], v[8 * qq + 7]);
+        st_row[q ^ wsw] = w;
+      }
     }
     __syncwarp();
 #pragma unroll
@@ -907,32 +935,37 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// 8 codes (one 16-byte output chunk, natural order) -> fp16 (q - zp) * s.
-template <int BITS>
+// 8 codes (one 16-byte output chunk, natural order) -> fp16: (q - zp) * s (QEPI 0),
+// q - zp (QEPI 1, scale applied in the epilogue) or the biased code 1024 + q (QEPI 2).
+template <int BITS, int QEPI>
 __device__ __forceinline__ uint4 convert8(const uint8_t* codes, __half2 s2) {
   uint4 o;
   uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+  auto fin = [&](uint32_t biased, __half2 zp) -> uint32_t {
+    if (QEPI == 2) return biased;
+    const __half2 d = __hsub2(u2h(biased), zp);
+    return h2u(QEPI == 1 ? d : __hmul2(d, s2));
+  };
   if (BITS == 8) {
     const uint2 w = *reinterpret_cast<const uint2*>(codes);
     const __half2 zp = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
-    ow[0] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w.x, 0x64646464u, 0x4140u)), zp), s2));
-    ow[1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w.x, 0x64646464u, 0x4342u)), zp), s2));
-    ow[2] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w.y, 0x64646464u, 0x4140u)), zp), s2));
-    ow[3] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w.y, 0x64646464u, 0x4342u)), zp), s2));
+    ow[0] = fin(__byte_perm(w.x, 0x64646464u, 0x4140u), zp);
+    ow[1] = fin(__byte_perm(w.x, 0x64646464u, 0x4342u), zp);
+    ow[2] = fin(__byte_perm(w.y, 0x64646464u, 0x4140u), zp);
+    ow[3] = fin(__byte_perm(w.y, 0x64646464u, 0x4342u), zp);
   } else {
     const uint32_t w = *reinterpret_cast<const uint32_t*>(codes);
     const __half2 zp = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t b = (w >> (8 * i)) & 0xFFu;
-      const uint32_t u = (b & 0xFu) | ((b & 0xF0u) << 12) | 0x64006400u;
-      ow[i] = h2u(__hmul2(__hsub2(u2h(u), zp), s2));
+      ow[i] = fin((b & 0xFu) | ((b & 0xF0u) << 12) | 0x64006400u, zp);
     }
   }
   return o;
 }
 
-template <int BITS>
+template <int BITS, int QEPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Q_THREADS, 1)
 tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_q1,
@@ -1165,7 +1198,7 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
             const __half2 s2 =
                 p.qblock ? __half2half2(srs[j][min(kb * BK + 8 * c, p.K - 1) / p.qblock])
                          : row_scale[j];
-            const uint4 o = convert8<BITS>(codes, s2);
+            const uint4 o = convert8<BITS, QEPI>(codes, s2);
             *reinterpret_cast<uint4*>(brow_s + ((c ^ (r & 7)) * 16)) = o;
           }
         }
@@ -1308,7 +1341,7 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   } else {
     mb3 = mb1;
   }
-  TcParams p;
+  TcParams p{};
   p.offsets = g.offsets;
   p.tiles = pair ? g.tiles256 : g.tiles128;
   p.E = g.E;
@@ -1401,7 +1434,7 @@ bool make_map_q(CUtensorMap* m, const GemmOperandB& b, int K, int bits, int E) {
          CUDA_SUCCESS;
 }
 
-template <int BITS>
+template <int BITS, int QEPI>
 cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   CUtensorMap ma, mq1, mq3;
   if (!make_map_a(&ma, g.dtype, g.a, g.rows, g.K)) return cudaErrorInvalidValue;
@@ -1439,9 +1472,12 @@ cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.b3_G = g.gated ? g.b3.G : 1;
   p.b1_rows = g.b1.n_rows;
   p.b3_rows = g.gated ? g.b3.n_rows : g.b1.n_rows;
+  p.qepi = QEPI;
+  p.qbias = 1024.0f + static_cast<float>(1 << (BITS - 1));
+  p.rowsum = g.rowsum;
   static bool attr_set = false;  // idempotent; a race between first callers is benign
   if (!attr_set) {
-    cudaError_t st = cudaFuncSetAttribute(tc_pair_qgemm_kernel<BITS>,
+    cudaError_t st = cudaFuncSetAttribute(tc_pair_qgemm_kernel<BITS, QEPI>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           q_smem_bytes<BITS>());
     if (st != cudaSuccess) return st;
@@ -1449,7 +1485,7 @@ cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   }
   const int64_t ub = ((g.rows + P_BM - 1) / P_BM + g.E) * p.n_tiles;
   const int64_t pairs = std::min<int64_t>(ub, num_sms / 2);
-  tc_pair_qgemm_kernel<BITS><<<static_cast<int>(2 * pairs), Q_THREADS, q_smem_bytes<BITS>(), s>>>(
+  tc_pair_qgemm_kernel<BITS, QEPI><<<static_cast<int>(2 * pairs), Q_THREADS, q_smem_bytes<BITS>(), s>>>(
       ma, mq1, mq3, p);
   return cudaGetLastError();
 }
@@ -1470,7 +1506,17 @@ bool tc_q_supported(const GemmArgs& g) {
 
 cudaError_t launch_gemm_tc_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.rows == 0 || g.N == 0) return cudaSuccess;
-  return g.qbits == 4 ? launch_q<4>(g, num_sms, s) : launch_q<8>(g, num_sms, s);
+  // Epilogue-side scaling needs one scale per stored row (block_size 0); the biased codes
+  // also need the A row sums.
+  const int mode = g.qblock != 0 ? 0 : (g.qepi == 2 && g.rowsum == nullptr ? 1 : g.qepi);
+  if (g.qbits == 4) {
+    if (mode == 2) return launch_q<4, 2>(g, num_sms, s);
+    if (mode == 1) return launch_q<4, 1>(g, num_sms, s);
+    return launch_q<4, 0>(g, num_sms, s);
+  }
+  if (mode == 2) return launch_q<8, 2>(g, num_sms, s);
+  if (mode == 1) return launch_q<8, 1>(g, num_sms, s);
+  return launch_q<8, 0>(g, num_sms, s);
 }
 
 namespace {

@@ -88,7 +88,7 @@ bool is_float_type(int dt) {
 // ------------------------------------------------------------ workspace plan
 struct WsLayout {
   size_t idx, w, chunk_counts, chunk_base, offsets, tiles128, tiles64, tiles256, pos, src, err;
-  size_t xp, act, qmoe, total;
+  size_t rowsum, xp, act, qmoe, total;
 };
 
 bool swiglu_fused(const moe_b200_problem& p) {
@@ -114,6 +114,7 @@ WsLayout plan_workspace(const moe_b200_problem& p) {
   L.pos = take(R * 4);
   L.src = take(R * 4);
   L.err = take(16);
+  L.rowsum = take(R * 4);                // A row sums of the packed (QMoE) GEMMs
   L.xp = take(R * p.hidden_size * es);   // gathered input, later fc2 output
   L.act = take(R * p.inter_size * es);
   L.qmoe = take(qmoe_workspace_bytes(p));
@@ -416,10 +417,22 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   // bounded waits expire and the call reports the device error instead of hanging.
   g1.test_stall = env_flag("MOE_B200_TEST_STALL") ? 1 : 0;
   if (fused_q) set_quantized(p, g1, t.fc1_scales, t.fc3_scales);
+  // Per-row scales (block_size 0): the packed GEMMs take biased codes and fix the result
+  // in the epilogue from the A row sums (MOE_B200_QGEMM_EPI=0/1 selects the converter-side
+  // scale / the exact codes instead, for comparison).
+  auto* rowsum = reinterpret_cast<float*>(ws + L.rowsum);
+  int qepi = 0;
+  if (fused_q && p.attrs.block_size == 0) {
+    const char* v = std::getenv("MOE_B200_QGEMM_EPI");
+    qepi = v != nullptr ? std::atoi(v) : 2;
+  }
+  g1.qepi = qepi;
+  g1.rowsum = qepi == 2 ? rowsum : nullptr;
   mark(kStFc1);
   if (fused_q) {
     if (!tc_q_supported(g1))
       return fail(MOE_B200_NOT_IMPLEMENTED, "QMoE fc1: operands not 16-byte aligned");
+    if (qepi == 2) MOE_CUDA_CHECK(launch_row_sums(xp, R, H, rowsum, s), "fc1 row sums");
     MOE_CUDA_CHECK(launch_gemm_tc_q(g1, device_sm_count(), s), "fc1 grouped GEMM (packed)");
   } else {
     MOE_CUDA_CHECK(run_gemm(g1, s), "fc1 grouped GEMM");
@@ -438,10 +451,13 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g2.tile_counter = err + 2;
   g2.test_stall = g1.test_stall;
   if (fused_q) set_quantized(p, g2, t.fc2_scales, nullptr);
+  g2.qepi = qepi;
+  g2.rowsum = qepi == 2 ? rowsum : nullptr;
   mark(kStFc2);
   if (fused_q) {
     if (!tc_q_supported(g2))
       return fail(MOE_B200_NOT_IMPLEMENTED, "QMoE fc2: operands not 16-byte aligned");
+    if (qepi == 2) MOE_CUDA_CHECK(launch_row_sums(act, R, I, rowsum, s), "fc2 row sums");
     MOE_CUDA_CHECK(launch_gemm_tc_q(g2, device_sm_count(), s), "fc2 grouped GEMM (packed)");
   } else {
     MOE_CUDA_CHECK(run_gemm(g2, s), "fc2 grouped GEMM");

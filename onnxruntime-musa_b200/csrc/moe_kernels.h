@@ -63,6 +63,8 @@ cudaError_t launch_plan(const int32_t* idx, int T, int k, int E, const int32_t* 
                         cudaStream_t s, int chunk = kRouteChunk);
 cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
                           int64_t rows, void* xp, cudaStream_t s);
+// out[r] = sum over k of a[r, k] (fp16 rows, fp32 sum in a fixed order).
+cudaError_t launch_row_sums(const void* a, int64_t rows, int K, float* out, cudaStream_t s);
 cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s,
                             int* clear = nullptr);
 cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
@@ -119,6 +121,12 @@ struct GemmArgs {
   // CTA-pair kernel: a zeroed int from which CTA pairs claim tiles in order (dynamic
   // schedule); nullptr = static round-robin.
   int* tile_counter = nullptr;
+  // Packed operands with one scale per row (qblock 0): 0 = scale in the converters,
+  // 1 = exact codes with the scale applied in the epilogue, 2 = biased codes (1024 + q) with
+  // the epilogue subtracting (1024 + zp) * rowsum[row] before scaling (rowsum: fp32 sums of
+  // the A rows over K; without it mode 2 runs as 1).
+  int qepi = 0;
+  const float* rowsum = nullptr;
   // Tensor-core kernels: output row remap for the expert-parallel return (row p of
   // segment q, seg_start[q] <= p < seg_start[q+1], is stored at row seg_dst[q] + p -
   // seg_start[q] of out_peers[q % remap_world]); seg_start == nullptr: rows of `out`.

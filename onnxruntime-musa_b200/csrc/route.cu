@@ -390,7 +390,36 @@ __global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n,
     dst[i] = v;
 }
 
+// One warp per row: fp32 sum of an fp16 row, lanes over 16-byte pieces, fixed butterfly.
+__global__ void __launch_bounds__(256)
+row_sums_kernel(const __half* __restrict__ a, int64_t rows, int K, float* __restrict__ out) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const __half* row = a + r * K;
+  float acc = 0.f;
+  for (int c = lane * 8; c < K; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      acc += f.x + f.y;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) out[r] = acc;
+}
+
 // ------------------------------------------------------------------ launchers
+cudaError_t launch_row_sums(const void* a, int64_t rows, int K, float* out, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  row_sums_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(
+      static_cast<const __half*>(a), rows, K, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s, int* clear) {
   if (n == 0) return cudaSuccess;
   const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 1184));
