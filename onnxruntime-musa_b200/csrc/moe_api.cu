@@ -417,14 +417,17 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   // bounded waits expire and the call reports the device error instead of hanging.
   g1.test_stall = env_flag("MOE_B200_TEST_STALL") ? 1 : 0;
   if (fused_q) set_quantized(p, g1, t.fc1_scales, t.fc3_scales);
-  // Per-row scales (block_size 0): the packed GEMMs take biased codes and fix the result
-  // in the epilogue from the A row sums (MOE_B200_QGEMM_EPI=0/1 selects the converter-side
-  // scale / the exact codes instead, for comparison).
+  // Per-row scales (block_size 0): the scale moves to the epilogue.  int8 codes go to the
+  // tensor cores biased (1024 + q) and the epilogue subtracts (1024 + 128) * rowsum: the
+  // constant part is ~15x the signal (|q - 128| ~ 74), within what the fp32 accumulation
+  // carries.  int4 codes stay exact (q - 8): their constant part would be ~220x the signal
+  // (|q - 8| ~ 4.6), and over a full-K accumulation that pushed a few outputs past the
+  // fp16 tolerance.  MOE_B200_QGEMM_EPI=0/1/2 forces a mode (comparison runs).
   auto* rowsum = reinterpret_cast<float*>(ws + L.rowsum);
   int qepi = 0;
   if (fused_q && p.attrs.block_size == 0) {
     const char* v = std::getenv("MOE_B200_QGEMM_EPI");
-    qepi = v != nullptr ? std::atoi(v) : 2;
+    qepi = v != nullptr ? std::atoi(v) : (p.attrs.expert_weight_bits == 8 ? 2 : 1);
   }
   g1.qepi = qepi;
   g1.rowsum = qepi == 2 ? rowsum : nullptr;

@@ -12,11 +12,11 @@
 // (musa/ep/src/kernels/math/matmul.cc:239-332).  The logits use the rounded normalised
 // values, as the unfused MatMul would.
 //
-// One warp per row: a first pass sums the squares (16-byte loads), a second writes the
-// normalised row (global and a shared-memory copy); the router MatMul then runs on the
-// tensor cores over 16-row tiles for fp16/bf16 (norm_router_tc_kernel) or as 16 expert
-// dot products at a time per row otherwise.  HBM-bound: x (+ skip) read twice (the second
-// read mostly from L2), normed (+ residual) written once.
+// fp16/bf16: norm_router_tc_kernel (16-row CTAs, K in chunks, the router MatMul on the
+// tensor cores).  fp32: one warp per row: a first pass sums the squares, a second writes
+// the normalised row (global and a shared-memory copy), then 16 expert dot products at a
+// time.  HBM-bound: x (+ skip) read twice (the second read mostly from L2), normed
+// (+ residual) written once.
 #include <type_traits>
 
 #include "moe_kernels.h"
@@ -144,18 +144,20 @@ norm_router_kernel(const T* __restrict__ x, const T* __restrict__ skip,
   }
 }
 
-// 16-bit types: a CTA of 8 warps takes 16 rows.  Each warp normalises two rows into a
-// shared [16][H + 8] tile (8 elements of padding per row: conflict-free fragment loads,
-// zero-filled K tail); then the router MatMul runs on the tensor cores (mma.sync
-// m16n8k16, fp32 accumulation), warp w taking expert columns [8j, 8j + 8) for
-// j = w, w + 8, ..., so the router weights are read once per 16 rows instead of once per
-// row.
+// 16-bit types: a CTA of 8 warps takes 16 rows.  A first pass gives each row its
+// 1/rms (warp per two rows); then K is walked in chunks of NR_KC columns: the CTA
+// normalises the chunk of its 16 rows (writing normed and residual), stages it in shared
+// memory ([16][NR_KC + 8]: 8 elements of padding make the fragment loads conflict-free)
+// and the warps run the router MatMul on it with mma.sync m16n8k16 (fp32 accumulation),
+// keeping their expert tiles' accumulators in registers across chunks.  Warp w owns
+// expert columns [8j, 8j + 8) for j = w / wpt, ...; with fewer than 8 tiles `wpt` warps
+// share a tile by splitting each chunk's k-steps and sum their partials at the end in warp
+// order (deterministic).  ~13 KB of shared memory per CTA: several CTAs per SM.
 constexpr int NR_TC_ROWS = 16;
 constexpr int NR_TC_WARPS = 8;
-
-__host__ __device__ constexpr size_t tc_tile_bytes(int64_t H) {
-  return static_cast<size_t>(NR_TC_ROWS) * (H + 8) * 2;  // 16-byte multiple (H % 8 == 0)
-}
+constexpr int NR_KC = 256;                 // K columns per chunk
+constexpr int NR_LD = NR_KC + 8;           // padded tile row (elements)
+constexpr int NR_MAX_TPW = 4;              // expert tiles per warp (E <= 256)
 
 __device__ __forceinline__ void nr_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                        uint32_t b1, bool bf16) {
@@ -179,111 +181,125 @@ norm_router_tc_kernel(const T* __restrict__ x, const T* __restrict__ skip,
                       const float* __restrict__ gamma, float eps, const T* __restrict__ wr,
                       int64_t rows, int H, int E, T* __restrict__ residual_out,
                       T* __restrict__ normed, T* __restrict__ logits) {
-  extern __shared__ __align__(16) uint8_t nr_smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ld = H + 8;                  // padded row (elements)
-  const int Kp = (H + 15) & ~15;         // K rounded up to the MMA depth
-  T* tile = reinterpret_cast<T*>(nr_smem);
+  __shared__ __align__(16) T tile[NR_TC_ROWS * NR_LD];
+  __shared__ float s_inv[NR_TC_ROWS];
+  __shared__ float red[NR_TC_WARPS * 32 * 4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * NR_TC_ROWS;
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
 
+  // 1/rms of each row.
   for (int rr = warp; rr < NR_TC_ROWS; rr += NR_TC_WARPS) {
     const int64_t row = row0 + rr;
-    T* srow = tile + rr * ld;
-    if (row >= rows) {
-      for (int c = lane; c < Kp; c += 32) srow[c] = from_f<T>(0.f);
-      continue;
-    }
-    const T* xr = x + row * H;
-    const T* sr = skip != nullptr ? skip + row * H : nullptr;
     float ss = 0.f;
+    if (row < rows) {
+      const T* xr = x + row * H;
+      const T* sr = skip != nullptr ? skip + row * H : nullptr;
 #pragma unroll 4
-    for (int c = lane * 8; c < H; c += 256) {
-      float h[8];
-      load_h<T>(xr, sr, c, h);
+      for (int c = lane * 8; c < H; c += 256) {
+        float h[8];
+        load_h<T>(xr, sr, c, h);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(h[j], h[j], ss);
-      if (residual_out != nullptr) store8<T>(residual_out + row * H + c, h);
+        for (int j = 0; j < 8; ++j) ss = fmaf(h[j], h[j], ss);
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss / static_cast<float>(H) + eps);
-#pragma unroll 4
-    for (int c = lane * 8; c < H; c += 256) {
-      float h[8];
-      load_h<T>(xr, sr, c, h);
-      const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + c));
-      const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + c + 4));
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-      float n[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) n[j] = h[j] * inv * g[j];
-      if (normed != nullptr) store8<T>(normed + row * H + c, n);
-      store8<T>(srow + c, n);
-    }
-    for (int c = H + lane; c < Kp; c += 32) srow[c] = from_f<T>(0.f);
+    if (lane == 0) s_inv[rr] = row < rows ? rsqrtf(ss / static_cast<float>(H) + eps) : 0.f;
   }
-  __syncthreads();
 
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t* tw = reinterpret_cast<const uint32_t*>(tile);
-  const int ldw = ld / 2;  // padded row in 32-bit words
-  // With fewer than 8 expert tiles, `wpt` warps share a tile by splitting K; their
-  // partial tiles are summed in shared memory in warp order (deterministic).
   const int ntile = (E + 7) / 8;
   const int wpt = ntile >= 8 ? 1 : (ntile >= 4 ? 2 : (ntile >= 2 ? 4 : 8));
   const int kslice = warp % wpt;
-  const int ksteps = Kp / 16;
-  const int kper = (ksteps + wpt - 1) / wpt;
-  float* red = reinterpret_cast<float*>(nr_smem + tc_tile_bytes(H));  // [8][32][4]
-  for (int j = warp / wpt; j < ntile; j += NR_TC_WARPS / wpt) {
-    const int e = min(j * 8 + g, E - 1);     // B column of this thread
-    const T* wrow = wr + static_cast<int64_t>(e) * H;
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    const int kb = kslice * kper * 16, ke = min(Kp, (kslice + 1) * kper * 16);
-    for (int k0 = kb; k0 < ke; k0 += 16) {
-      uint32_t a[4];
-      a[0] = tw[g * ldw + (k0 >> 1) + t];
-      a[1] = tw[(g + 8) * ldw + (k0 >> 1) + t];
-      a[2] = tw[g * ldw + (k0 >> 1) + 4 + t];
-      a[3] = tw[(g + 8) * ldw + (k0 >> 1) + 4 + t];
-      const int ka = k0 + 2 * t, kb = k0 + 8 + 2 * t;
-      const uint32_t b0 = ka < H ? __ldg(reinterpret_cast<const uint32_t*>(wrow + ka)) : 0u;
-      const uint32_t b1 = kb < H ? __ldg(reinterpret_cast<const uint32_t*>(wrow + kb)) : 0u;
-      nr_mma(d, a, b0, b1, sizeof(T) == 2 && !std::is_same<T, __half>::value);
-    }
-    if (wpt > 1) {
-      // One tile per warp group: publish the partial tile, sum in the group's first warp.
+  const int jstep = NR_TC_WARPS / wpt;
+  float d[NR_MAX_TPW][4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) red[(warp * 32 + lane) * 4 + q] = d[q];
-    }
-    if (wpt == 1) {
-      // d: rows g / g + 8, expert columns j*8 + 2t, + 1
+  for (int i = 0; i < NR_MAX_TPW; ++i)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int64_t row = row0 + g + (q >> 1) * 8;
-        const int ec = j * 8 + 2 * t + (q & 1);
-        if (row < rows && ec < E) logits[row * E + ec] = from_f<T>(d[q]);
+    for (int q = 0; q < 4; ++q) d[i][q] = 0.f;
+  const uint32_t* tw = reinterpret_cast<const uint32_t*>(tile);
+  constexpr int LDW = NR_LD / 2;
+  __syncthreads();
+
+  for (int c0 = 0; c0 < H; c0 += NR_KC) {
+    const int cw = min(NR_KC, H - c0);          // multiple of 8
+    const int cwp = (cw + 15) & ~15;            // multiple of the MMA depth
+    const int pieces_per_row = cw / 8;
+    // Normalise the chunk of the 16 rows: 16-byte pieces spread over the CTA.
+    for (int pc = tid; pc < NR_TC_ROWS * pieces_per_row; pc += NR_TC_WARPS * 32) {
+      const int rr = pc / pieces_per_row, cc = (pc % pieces_per_row) * 8;
+      const int64_t row = row0 + rr;
+      float n[8];
+      if (row < rows) {
+        float h[8];
+        load_h<T>(x + row * H, skip != nullptr ? skip + row * H : nullptr, c0 + cc, h);
+        if (residual_out != nullptr) store8<T>(residual_out + row * H + c0 + cc, h);
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + c0 + cc));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + c0 + cc + 4));
+        const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float inv = s_inv[rr];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) n[j] = h[j] * inv * gm[j];
+        if (normed != nullptr) store8<T>(normed + row * H + c0 + cc, n);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) n[j] = 0.f;
+      }
+      store8<T>(tile + rr * NR_LD + cc, n);
+    }
+    if (cwp != cw)  // zero the k tail of the last chunk (H % 16 == 8)
+      for (int i = tid; i < NR_TC_ROWS * 8; i += NR_TC_WARPS * 32)
+        tile[(i >> 3) * NR_LD + cw + (i & 7)] = from_f<T>(0.f);
+    __syncthreads();
+
+    const int ks = cwp / 16;
+    const int kper = (ks + wpt - 1) / wpt;
+    const int kb = kslice * kper, ke = min(ks, kb + kper);
+#pragma unroll
+    for (int i = 0; i < NR_MAX_TPW; ++i) {
+      const int j = warp / wpt + i * jstep;
+      if (j >= ntile) break;
+      const T* wrow = wr + static_cast<int64_t>(min(j * 8 + g, E - 1)) * H + c0;
+      for (int k = kb; k < ke; ++k) {
+        uint32_t a[4];
+        a[0] = tw[g * LDW + k * 8 + t];
+        a[1] = tw[(g + 8) * LDW + k * 8 + t];
+        a[2] = tw[g * LDW + k * 8 + 4 + t];
+        a[3] = tw[(g + 8) * LDW + k * 8 + 4 + t];
+        const int ka = 16 * k + 2 * t, kb2 = ka + 8;
+        const uint32_t b0 = ka < cw ? __ldg(reinterpret_cast<const uint32_t*>(wrow + ka)) : 0u;
+        const uint32_t b1 = kb2 < cw ? __ldg(reinterpret_cast<const uint32_t*>(wrow + kb2)) : 0u;
+        nr_mma(d[i], a, b0, b1, kBf16);
       }
     }
+    __syncthreads();  // the next chunk overwrites the tile
   }
-  if (wpt == 1) return;
-  __syncthreads();
-  const int j = warp / wpt;
-  if (kslice != 0 || j >= ntile) return;
-  float d[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int w2 = warp; w2 < warp + wpt; ++w2)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) d[q] += red[(w2 * 32 + lane) * 4 + q];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int64_t row = row0 + g + (q >> 1) * 8;
-    const int ec = j * 8 + 2 * t + (q & 1);
-    if (row < rows && ec < E) logits[row * E + ec] = from_f<T>(d[q]);
-  }
-}
 
-size_t tc_smem_bytes(int64_t H) {
-  return tc_tile_bytes(H) + NR_TC_WARPS * 32 * 4 * sizeof(float);
+  if (wpt > 1) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) red[(warp * 32 + lane) * 4 + q] = d[0][q];
+    __syncthreads();
+    const int j = warp / wpt;
+    if (kslice != 0 || j >= ntile) return;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d[0][q] = 0.f;
+    for (int w2 = warp; w2 < warp + wpt; ++w2)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) d[0][q] += red[(w2 * 32 + lane) * 4 + q];
+  }
+  // d: rows g / g + 8, expert columns 8j + 2t, + 1
+#pragma unroll
+  for (int i = 0; i < NR_MAX_TPW; ++i) {
+    const int j = warp / wpt + i * jstep;
+    if (j >= ntile || (wpt > 1 && i > 0)) break;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int64_t row = row0 + g + (q >> 1) * 8;
+      const int ec = j * 8 + 2 * t + (q & 1);
+      if (row < rows && ec < E) logits[row * E + ec] = from_f<T>(d[i][q]);
+    }
+  }
 }
 
 template <typename T>
@@ -291,21 +307,12 @@ cudaError_t launch_t(const void* x, const void* skip, const float* gamma, float 
                      const void* wr, int64_t rows, int H, int E, void* residual_out,
                      void* normed, void* logits, cudaStream_t s) {
   if constexpr (sizeof(T) == 2) {
-    const size_t smem = tc_smem_bytes(H);
-    if (smem <= 227 * 1024) {
-      if (smem > 48 * 1024) {
-        cudaError_t st = cudaFuncSetAttribute(norm_router_tc_kernel<T>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(smem));
-        if (st != cudaSuccess) return st;
-      }
-      const int64_t blocks = (rows + NR_TC_ROWS - 1) / NR_TC_ROWS;
-      norm_router_tc_kernel<T><<<static_cast<unsigned>(blocks), NR_TC_WARPS * 32, smem, s>>>(
-          static_cast<const T*>(x), static_cast<const T*>(skip), gamma, eps,
-          static_cast<const T*>(wr), rows, H, E, static_cast<T*>(residual_out),
-          static_cast<T*>(normed), static_cast<T*>(logits));
-      return cudaGetLastError();
-    }
+    const int64_t blocks = (rows + NR_TC_ROWS - 1) / NR_TC_ROWS;
+    norm_router_tc_kernel<T><<<static_cast<unsigned>(blocks), NR_TC_WARPS * 32, 0, s>>>(
+        static_cast<const T*>(x), static_cast<const T*>(skip), gamma, eps,
+        static_cast<const T*>(wr), rows, H, E, static_cast<T*>(residual_out),
+        static_cast<T*>(normed), static_cast<T*>(logits));
+    return cudaGetLastError();
   }
   const size_t smem = static_cast<size_t>(NR_WARPS) * H * sizeof(T);
   if (smem > 48 * 1024) {
@@ -325,7 +332,9 @@ cudaError_t launch_t(const void* x, const void* skip, const float* gamma, float 
 }  // namespace
 
 size_t norm_router_smem_bytes(int dtype, int64_t H) {
-  return static_cast<size_t>(NR_WARPS) * H * dtype_bytes(dtype);
+  // fp32 rows go through the per-warp kernel (a shared-memory copy of each row); 16-bit
+  // rows through the chunked tensor-core kernel (fixed ~13 KB).
+  return dtype == kDtF32 ? static_cast<size_t>(NR_WARPS) * H * 4 : 0;
 }
 
 cudaError_t launch_norm_router(int dtype, const void* x, const void* skip, const float* gamma,

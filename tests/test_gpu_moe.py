@@ -268,12 +268,22 @@ def test_qmoe_decode_path(pkg, orc, dev, case):
     np.testing.assert_allclose(as_np(out2), ref, **TOL["float16"])
 
 
+@pytest.mark.parametrize("shape", [(6, 4, 64), (300, 4, 0), (300, 8, 0), (300, 4, 64)],
+                         ids=["decode_int4_bs64", "prefill_int4_rowscale", "prefill_int8_rowscale",
+                              "prefill_int4_bs64"])
 @pytest.mark.parametrize("variant", ["plain_gelu_bias", "swiglu_interleaved", "swiglu_halves"])
-def test_qmoe_decode_variants(pkg, orc, dev, variant):
-    T, H, I, E, k, bits, bs = 6, 256, 256, 8, 2, 4, 64
+def test_qmoe_decode_variants(pkg, orc, dev, variant, shape):
+    """Activation / fc1 layouts through the decode kernels (T=6) and the packed tensor-core
+    GEMM (T=300), including per-row scales, whose scaling and biased-code correction run in
+    the epilogue with the gate and linear halves' own scale addressing."""
+    T, bits, bs = shape
+    H, I, E, k = 256, 256, 8, 2
     rng = np.random.default_rng(77)
+    # Scales keep the outputs near unit scale, where the fp16 tolerances are meaningful
+    # (the dequantised fp16 weights carry ~5e-4 relative rounding; larger outputs put
+    # near-zero elements past atol).
     q = orc.make_qmoe_inputs(T=T, H=H, I=I, E=E, k=k, bits=bits, block_size=bs,
-                             scale_mu=-4.0, scale_sigma=0.3, seed=78)
+                             scale_mu=-5.0 if bits == 4 else -8.5, scale_sigma=0.3, seed=78)
     attrs = dict(q["attrs"], k=k)
     fc3 = True
     if variant == "plain_gelu_bias":
@@ -286,7 +296,8 @@ def test_qmoe_decode_variants(pkg, orc, dev, variant):
         attrs.update(activation_type="swiglu", swiglu_fusion=fusion, activation_alpha=1.702,
                      activation_beta=1.0, swiglu_limit=7.0)
         if fusion == 1:
-            W = np.empty((E, 2 * I, H // 2), np.uint8); W[:, 0::2] = q["fc1_q"]; W[:, 1::2] = q["fc3_q"]
+            W = np.empty((E, 2 * I, q["fc1_q"].shape[2]), np.uint8)
+            W[:, 0::2] = q["fc1_q"]; W[:, 1::2] = q["fc3_q"]
             S = np.empty((E, 2 * I) + q["fc1_scales"].shape[2:], np.float16)
             S[:, 0::2] = q["fc1_scales"]; S[:, 1::2] = q["fc3_scales"]
         else:
