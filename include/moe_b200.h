@@ -302,6 +302,9 @@ int moe_b200_ep_comm_handle_size(size_t* bytes);
 int moe_b200_ep_comm_get_handle(moe_b200_ep_comm* comm, void* handle);
 /* handles: world handles in rank order (this rank's own entry is ignored). */
 int moe_b200_ep_comm_connect(moe_b200_ep_comm* comm, const void* handles);
+/* Frees this rank's region: every rank must have finished its last moe_b200_ep_forward
+ * (e.g. a barrier after a stream synchronisation) before any rank destroys its
+ * communicator, since peers store into this region. */
 int moe_b200_ep_comm_destroy(moe_b200_ep_comm* comm);
 /* Workspace of one call (problem: this rank's num_rows, local num_experts = E / W). */
 int moe_b200_ep_workspace_size(const moe_b200_ep_comm* comm,

@@ -112,3 +112,36 @@ def test_provider_options(pkg):
     with pytest.raises(ValueError):
         pkg.make_provider_options(ep_world_size=2, ep_rank=2)
     assert pkg.get_ep_names() == [pkg.get_ep_name()] == ["B200MoEExecutionProvider"]
+
+
+def test_new_entries_validate_before_touching_the_device(pkg):
+    """Argument checks of the pipeline, device-side EP, pre-MoE rows and routing-mode
+    entries run on the host before any CUDA call (so they are testable without a GPU)."""
+    import ctypes
+    L = pkg.lib()
+    h = ctypes.c_void_p()
+    # EP communicator: world beyond 8 ranks, rank outside the world, fp32, uneven experts.
+    assert L.moe_b200_ep_comm_create(0, 9, 16, 2, 64, 16, pkg.FLOAT16, ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_ep_comm_create(2, 2, 16, 2, 64, 16, pkg.FLOAT16, ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_ep_comm_create(0, 2, 16, 2, 64, 16, pkg.FLOAT, ctypes.byref(h)) == pkg.NOT_IMPLEMENTED
+    assert L.moe_b200_ep_comm_create(0, 3, 16, 2, 64, 16, pkg.FLOAT16, ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_ep_comm_create(0, 2, 16, 2, 60, 16, pkg.FLOAT16, ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    # Pipeline: depth outside [1, 8], no problem.
+    p = pkg.make_problem(16, 64, 64, 8, pkg.FLOAT16, k=2, activation_type="silu")
+    t = pkg.Tensors()
+    assert L.moe_b200_pipeline_create(ctypes.byref(p), ctypes.byref(t), 0, ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_pipeline_create(None, ctypes.byref(t), 2, ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    # Pre-MoE rows: hidden size not a multiple of 8; nothing to do for zero rows.
+    assert L.moe_b200_norm_router(pkg.FLOAT16, 4, 100, 8, None, None, None, ctypes.c_float(1e-6),
+                                  None, None, None, None, None) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_norm_router(pkg.FLOAT16, 0, 128, 8, None, None, None, ctypes.c_float(1e-6),
+                                  None, None, None, None, None) == pkg.OK
+    assert L.moe_b200_norm_router(99, 4, 128, 8, None, None, None, ctypes.c_float(1e-6),
+                                  None, None, None, None, None) == pkg.NOT_IMPLEMENTED
+    # Routing modes: 2 (sparse mixer) needs k = 2; 3 is not a mode.
+    assert L.moe_b200_route(None, pkg.FLOAT16, 4, 8, 3, 2, None, None, None) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_route(None, pkg.FLOAT16, 4, 8, 2, 3, None, None, None) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_route_noalloc(None, pkg.FLOAT16, 4, 8, 3, 2, None, None, None) == pkg.INVALID_ARGUMENT
+    # Stage events: fewer than stages + 1.
+    evs = (ctypes.c_void_p * 3)()
+    assert L.moe_b200_forward_staged(ctypes.byref(p), ctypes.byref(t), None, 0, None, evs, 3) == pkg.INVALID_ARGUMENT
