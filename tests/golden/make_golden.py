@@ -24,16 +24,20 @@ def save(name, arrays, meta):
     np.savez_compressed(HERE / f"{name}.npz", meta=np.array(json.dumps(meta)), **arrays)
 
 
-def moe_case(name, seed, T, H, I, E, k, act, gated, dtype, bias, normalize, ties=False, **extra):
+def moe_case(name, seed, T, H, I, E, k, act, gated, dtype, bias, normalize, ties=False,
+             logit_scale=1.0, **extra):
     inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act=act, gated=gated, dtype=dtype,
                               bias=bias, normalize=normalize, seed=seed)
+    if logit_scale != 1.0:  # close logits: the sparse mixer's 2% band keeps several experts
+        inp["router_probs"] = (inp["router_probs"].astype(np.float32) * logit_scale).astype(
+            inp["router_probs"].dtype)
     if ties:  # quantise logits so that equal values (ties) are common
         inp["router_probs"] = (np.round(inp["router_probs"].astype(np.float32) * 2) / 2).astype(
             inp["router_probs"].dtype)
     attrs = dict(inp["attrs"], **extra)
     out = orc.moe(inp["x"], inp["router_probs"], inp["fc1_w"], inp["fc1_b"], inp["fc2_w"],
                   inp["fc2_b"], inp["fc3_w"], inp["fc3_b"], **attrs)
-    idx, w = orc.route(inp["router_probs"], k, normalize)
+    idx, w = orc.route(inp["router_probs"], k, normalize, attrs.get("use_sparse_mixer", 0))
     save(name, dict(x=inp["x"], router_probs=inp["router_probs"], fc1_w=inp["fc1_w"],
                     fc1_b=inp["fc1_b"], fc2_w=inp["fc2_w"], fc2_b=inp["fc2_b"],
                     fc3_w=inp["fc3_w"], fc3_b=inp["fc3_b"], output=out, expert_idx=idx,
@@ -61,6 +65,8 @@ if __name__ == "__main__":
              dtype="float16", bias=True, normalize=0, ties=True)
     moe_case("moe_fp32_relu_k1", 14, T=17, H=32, I=48, E=4, k=1, act="relu", gated=False,
              dtype="float32", bias=True, normalize=0)
+    moe_case("moe_fp16_sparse_mixer", 17, T=48, H=64, I=64, E=8, k=2, act="silu", gated=True,
+             dtype="float16", bias=True, normalize=1, logit_scale=0.02, use_sparse_mixer=1)
     qmoe_case("qmoe_int4_block32", 15, T=12, H=128, I=64, E=4, k=2, bits=4, block=32,
               mu=-5.0, sigma=0.3)
     qmoe_case("qmoe_int8_rowscale", 16, T=10, H=64, I=128, E=4, k=2, bits=8, block=0,

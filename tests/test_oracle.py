@@ -178,7 +178,8 @@ def test_golden_fixture(orc, path):
                        d["fc2_q"], d["fc2_scales"], None, get("fc3_q"), get("fc3_scales"),
                        None, **meta["attrs"])
     idx, w = orc.route(d["router_probs"], meta["attrs"]["k"],
-                       meta["attrs"]["normalize_routing_weights"])
+                       meta["attrs"]["normalize_routing_weights"],
+                       meta["attrs"].get("use_sparse_mixer", 0))
     np.testing.assert_array_equal(idx, d["expert_idx"])
     np.testing.assert_allclose(w, d["route_w"], rtol=0, atol=0)
     np.testing.assert_allclose(out, d["output"], rtol=1e-12, atol=1e-12)
