@@ -72,9 +72,13 @@ CONFIGS = {
                     "k=2 SwiGLU(fc3)"),
 }
 
-# DRAM bytes (read + write) of one fc1(+fc3) launch of the default workload from the ncu
-# capture summarised in profiles/tc_pair_grouped_gemm_c2.md.
-FC1_TRAFFIC_BYTES = 2_177_550_848
+# DRAM bytes (read + write) of one fc1(+fc3) launch, keyed by (config, tokens), from the
+# ncu captures summarised in profiles/tc_pair_grouped_gemm_c2.md and
+# profiles/tc_pair_qgemm_kernel_c5_t4096.md.
+FC1_TRAFFIC_BYTES = {("c2", 4096): 2_177_550_848, ("c5", 4096): 1_006_231_808}
+# Routed rows (tokens x k) up to which QMoE prefill converts codes inside the GEMM
+# (kQmoeFusedMaxRows in the library).
+QMOE_FUSED_MAX_ROWS = 16384
 
 
 def peaks():
@@ -457,21 +461,35 @@ def bench_ours(args, cfg, rank, world, dev):
                 "experts_touched": alg["touched"],
                 "layer_frac": round((alg["bytes"] / pk["hbm"] / 1e9) / (ms / 1e3), 4)}
     else:
-        k_name = ("simt_gemm_kernel (FFMA)" if cfg["kind"] == "moe" and cfg["dtype"] == "float32"
-                  else "tc_pair_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)")
+        fused_q = cfg["kind"] == "qmoe" and T * cfg["k"] <= QMOE_FUSED_MAX_ROWS
+        if cfg["kind"] == "moe" and cfg["dtype"] == "float32":
+            k_name = "simt_gemm_kernel (FFMA)"
+        elif fused_q:
+            k_name = "tc_pair_qgemm_kernel (codes converted in shared memory; fc1+fc3, SwiGLU epilogue)"
+        else:
+            k_name = "tc_pair_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)"
         achieved = alg["flops_fc1"] / (gemm_ms["fc1"] / 1e3) / 1e12
         roof_t = max(alg["flops"] / (pk["tflops"] * 1e12), alg["bytes"] / (pk["hbm"] * 1e9))
         roof = {"bound": "tensor", "kernel": k_name, "achieved": round(achieved, 1),
                 "peak": pk["tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["tflops"], 4),
                 "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)",
                 "frac_of_sustained": round(achieved / pk["tflops_sus"], 4) if pk["tflops_sus"] else None,
-                "traffic": FC1_TRAFFIC_BYTES if (args.config == "c2" and T == 4096) else None,
+                "traffic": FC1_TRAFFIC_BYTES.get((args.config, T)),
                 "alg_flops_per_launch": alg["flops_fc1"],
                 "fc2": {"achieved": round(alg["flops_fc2"] / (gemm_ms["fc2"] / 1e3) / 1e12, 1)},
                 "layer_frac": round(roof_t / (ms / 1e3), 4)}
-    # Launches per layer call: route, scan, permute, gather, fc1, fc2, combine; QMoE
-    # prefill adds three dequantisation launches.
-    launches = 10 if (cfg["kind"] == "qmoe" and not decode) else (5 if decode else 7)
+    # Launches per layer call: route, scan, permute, gather, fc1, fc2, combine.  QMoE
+    # prefill with codes converted inside the GEMM adds two row-sum launches for int8
+    # per-row scales (biased codes); beyond the fused limit it adds one dequantisation
+    # launch per weight tensor.
+    if decode:
+        launches = 5
+    elif cfg["kind"] != "qmoe":
+        launches = 7
+    elif not fused_q:
+        launches = 10
+    else:
+        launches = 9 if (cfg["bits"] == 8 and cfg["block"] == 0) else 7
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
