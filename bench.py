@@ -79,6 +79,9 @@ FC1_TRAFFIC_BYTES = {("c2", 4096): 2_177_550_848, ("c5", 4096): 1_006_231_808}
 # Routed rows (tokens x k) up to which QMoE prefill converts codes inside the GEMM
 # (kQmoeFusedMaxRows in the library).
 QMOE_FUSED_MAX_ROWS = 16384
+# Routed rows from which a QMoE call with a prepack runs on the prepacked weights
+# (kPrepackMinRows in the library; MOE_B200_PREPACK_MIN_ROWS overrides both).
+PREPACK_MIN_ROWS = 0
 
 
 def peaks():
@@ -329,8 +332,16 @@ def bench_ours(args, cfg, rank, world, dev):
     T = cfg["T"]
     out = torch.empty_like(L["x"])
     prob, tens, inputs, op_attrs, op_type = problem_and_tensors(pkg, cfg, L, out)
-    ws = torch.empty(pkg.workspace_size(prob), dtype=torch.uint8, device=dev)
+    # --prepack (QMoE): weights dequantised once before timing (moe_b200_prepack_create);
+    # prefill-sized calls then run the fp16 GEMMs on them.
+    pk = pkg.Prepacked(prob, tens) if (args.prepack and cfg["kind"] == "qmoe") else None
+    ws = torch.empty(pkg.workspace_size(prob, pk), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+
+    def fwd(events=None):
+        if pk is None and events is None:
+            return pkg.forward(prob, tens, ws, stream)
+        return pkg.forward(prob, tens, ws, stream, prepacked=pk, events=events)
 
     def barrier():
         if world > 1:
@@ -374,14 +385,14 @@ def bench_ours(args, cfg, rank, world, dev):
         row = next(it_ev)
         evs = [None] * (len(pkg.STAGES) + 1)
         evs[i_fc1], evs[i_fc2], evs[i_fc2 + 1] = row
-        return pkg.forward_staged(prob, tens, ws, evs, stream)
+        return fwd(evs)
 
     warm_left = [args.warmup]  # timed() runs the warm-up calls first
 
     def step():
         if warm_left[0] > 0:
             warm_left[0] -= 1
-            return pkg.forward(prob, tens, ws, stream)
+            return fwd()
         return timed_call()
 
     with ClockSampler(dev.index) as clk:
@@ -401,7 +412,7 @@ def bench_ours(args, cfg, rank, world, dev):
             ev.record(stream)  # creates the event handle
     torch.cuda.synchronize(dev)
     for row in evs:
-        pkg.forward_staged(prob, tens, ws, row, stream)
+        fwd(row)
     torch.cuda.synchronize(dev)
     stage = {s: [row[i].elapsed_time(row[i + 1]) for row in evs]
              for i, s in enumerate(pkg.STAGES)}
@@ -413,6 +424,8 @@ def bench_ours(args, cfg, rank, world, dev):
     hout = torch.empty_like(hx).pin_memory()
     dx, dl = torch.empty_like(L["x"]), torch.empty_like(L["router_probs"])
     e2e_inputs = [dx, dl] + inputs[2:]
+    if pk is not None:
+        op.prepack(e2e_inputs)
 
     def e2e_step():
         dx.copy_(hx, non_blocking=True)
@@ -428,6 +441,8 @@ def bench_ours(args, cfg, rank, world, dev):
     # neighbouring steps overlap this step's compute.  Wall clock from the first submit
     # to the completion of the last D2H, max over ranks.
     with pkg.Pipeline(prob, tens, depth=2) as pl:
+        if pk is not None:
+            pl.set_prepacked(pk)
         for _ in range(args.warmup):
             pl.submit(hx, hl, hout)
         pl.synchronize()
@@ -461,7 +476,10 @@ def bench_ours(args, cfg, rank, world, dev):
                 "experts_touched": alg["touched"],
                 "layer_frac": round((alg["bytes"] / pk["hbm"] / 1e9) / (ms / 1e3), 4)}
     else:
-        fused_q = cfg["kind"] == "qmoe" and T * cfg["k"] <= QMOE_FUSED_MAX_ROWS
+        prepacked = pk is not None and not decode and T * cfg["k"] >= int(
+            os.environ.get("MOE_B200_PREPACK_MIN_ROWS", PREPACK_MIN_ROWS))
+        fused_q = (cfg["kind"] == "qmoe" and not prepacked
+                   and T * cfg["k"] <= QMOE_FUSED_MAX_ROWS)
         if cfg["kind"] == "moe" and cfg["dtype"] == "float32":
             k_name = "simt_gemm_kernel (FFMA)"
         elif fused_q:
@@ -474,7 +492,7 @@ def bench_ours(args, cfg, rank, world, dev):
                 "peak": pk["tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["tflops"], 4),
                 "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)",
                 "frac_of_sustained": round(achieved / pk["tflops_sus"], 4) if pk["tflops_sus"] else None,
-                "traffic": FC1_TRAFFIC_BYTES.get((args.config, T)),
+                "traffic": None if prepacked else FC1_TRAFFIC_BYTES.get((args.config, T)),
                 "alg_flops_per_launch": alg["flops_fc1"],
                 "fc2": {"achieved": round(alg["flops_fc2"] / (gemm_ms["fc2"] / 1e3) / 1e12, 1)},
                 "layer_frac": round(roof_t / (ms / 1e3), 4)}
@@ -485,6 +503,8 @@ def bench_ours(args, cfg, rank, world, dev):
     if decode:
         launches = 5
     elif cfg["kind"] != "qmoe":
+        launches = 7
+    elif prepacked:
         launches = 7
     elif not fused_q:
         launches = 10
@@ -500,7 +520,9 @@ def bench_ours(args, cfg, rank, world, dev):
                    "tokens_per_gpu": T,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (weights streamed every step)"
-                         if alg["bytes"] > 126e6 else "inputs smaller than L2 (not flushed)"},
+                         if alg["bytes"] > 126e6 else "inputs smaller than L2 (not flushed)",
+                   **({"weights": "prepacked: dequantised once before timing "
+                                  "(moe_b200_prepack_create)"} if pk is not None else {})},
         "e2e": e2e, "roofline": roof,
         "stage_ms": {s: round(v, 4) for s, v in stage_ms.items()},
         "adjacent_ops": adjacent,
@@ -643,6 +665,8 @@ def main():
     ap.add_argument("--tokens", default=None,
                     help="tokens per GPU (comma list for a sweep); default: the config's")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--prepack", action="store_true",
+                    help="QMoE: dequantise the weights once before timing (weight prepack)")
     ap.add_argument("--ep-chunks", type=int, default=None,
                     help="token chunks pipelined through the expert-parallel exchange "
                          "(default 1)")

@@ -108,6 +108,7 @@ typedef struct moe_b200_tensor_ref {
 } moe_b200_tensor_ref;
 
 typedef struct moe_b200_kernel moe_b200_kernel;
+typedef struct moe_b200_prepacked moe_b200_prepacked;  /* QMoE weight prepack (below) */
 
 /* ---------------------------------------------------------------- library */
 
@@ -339,9 +340,51 @@ int moe_b200_pipeline_create(const moe_b200_problem* problem,
 int moe_b200_pipeline_submit(moe_b200_pipeline* pipeline, const void* host_input,
                              const void* host_router_probs, void* host_output,
                              int64_t num_rows);
+/* Calls submitted from now on may take `prepacked` (moe_b200_prepack_create; NULL
+ * detaches it); the pipeline holds its own reference. */
+int moe_b200_pipeline_set_prepacked(moe_b200_pipeline* pipeline, moe_b200_prepacked* prepacked);
 /* Waits for every submitted call (host outputs complete). */
 int moe_b200_pipeline_synchronize(moe_b200_pipeline* pipeline);
 int moe_b200_pipeline_destroy(moe_b200_pipeline* pipeline);
+
+/* ------------------------------------------------------- QMoE weight prepack */
+
+/* Dequantised copies of a QMoE node's expert weights, made once when the session is
+ * initialised (the role of OpKernel::PrePack) and used by prefill-sized calls, which then
+ * run the fp16/bf16 tensor-core GEMMs with no per-call dequantisation.  Decode-sized calls
+ * keep streaming the packed codes, so the initializers stay needed (a plugin reports
+ * is_packed = false).  share != 0 is the session option
+ * "ep.musa.enable_prepack_weight_sharing" (parsed at musa/ep/src/ep_factory.cc:472-478):
+ * nodes whose codes and scales have identical content, in any session of the process on
+ * the same device, hold one reference-counted copy (matched by shape and a 64-bit content
+ * hash). */
+/* problem gives the weight shapes and attributes (num_rows is ignored); weights holds
+ * the fc1/fc2(/fc3) codes and scales (other pointers are ignored).  Synchronises
+ * `stream` before returning; the prepack may then be used from any stream. */
+int moe_b200_prepack_create(const moe_b200_problem* problem, const moe_b200_tensors* weights,
+                            int32_t share, void* stream, moe_b200_prepacked** prepacked);
+/* Device bytes held and the current reference count (either pointer may be NULL). */
+int moe_b200_prepack_info(const moe_b200_prepacked* prepacked, size_t* bytes, int32_t* refs);
+/* Drops one reference; the memory is freed with the last one. */
+int moe_b200_prepack_release(moe_b200_prepacked* prepacked);
+/* moe_b200_workspace_size / moe_b200_forward for a call that may use `prepacked` (NULL
+ * behaves as the plain entry points).  The call takes the prepacked weights when the
+ * prepack matches the problem's shapes and the call is not decode-sized (and routes at
+ * least MOE_B200_PREPACK_MIN_ROWS rows, num_rows * k, when that variable is set);
+ * `t` must still hold the packed weights and scales, which other calls read. */
+int moe_b200_workspace_size_prepacked(const moe_b200_problem* problem,
+                                      const moe_b200_prepacked* prepacked, size_t* bytes);
+/* `events`: NULL, or num_events >= 8 stage events recorded as by moe_b200_forward_staged. */
+int moe_b200_forward_prepacked(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                               const moe_b200_prepacked* prepacked, void* workspace,
+                               size_t workspace_bytes, void* stream, void* const* events,
+                               int32_t num_events);
+/* Kernel-object pre-pack: inputs[] in the QMoE schema order (input and router_probs may
+ * be absent); the kernel keeps a reference and later computes whose weight inputs are the
+ * same device pointers use it.  *is_packed is set to 0 (see above). */
+int moe_b200_kernel_prepack(moe_b200_kernel* kernel, int32_t num_inputs,
+                            const moe_b200_tensor_ref* inputs, int32_t share, void* stream,
+                            int32_t* is_packed);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -129,6 +129,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "moe_b200_pipeline_create": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                                 _I32, ctypes.POINTER(_VP)]),
     "moe_b200_pipeline_submit": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I64]),
+    "moe_b200_pipeline_set_prepacked": (ctypes.c_int, [_VP, _VP]),
     "moe_b200_pipeline_synchronize": (ctypes.c_int, [_VP]),
     "moe_b200_pipeline_destroy": (ctypes.c_int, [_VP]),
     "moe_b200_ep_dispatch": (ctypes.c_int, [ctypes.POINTER(Problem), _VP, _VP, _VP, _VP, _VP,
@@ -140,6 +141,16 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "moe_b200_route_noalloc": (ctypes.c_int, [_VP, _I32, _I64, _I64, _I32, _I32, _VP, _VP, _VP]),
     "moe_b200_permute_workspace_size": (_SZ, [_I64, _I32, _I64]),
     "moe_b200_permute": (ctypes.c_int, [_VP, _I64, _I32, _I64, _VP, _VP, _VP, _VP, _SZ, _VP]),
+    "moe_b200_prepack_create": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
+                                               _I32, _VP, ctypes.POINTER(_VP)]),
+    "moe_b200_prepack_info": (ctypes.c_int, [_VP, ctypes.POINTER(_SZ), _PI32]),
+    "moe_b200_prepack_release": (ctypes.c_int, [_VP]),
+    "moe_b200_workspace_size_prepacked": (ctypes.c_int, [ctypes.POINTER(Problem), _VP,
+                                                         ctypes.POINTER(_SZ)]),
+    "moe_b200_forward_prepacked": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
+                                                  _VP, _VP, _SZ, _VP, ctypes.POINTER(_VP), _I32]),
+    "moe_b200_kernel_prepack": (ctypes.c_int, [_VP, _I32, ctypes.POINTER(TensorRef), _I32, _VP,
+                                               _PI32]),
     "moe_b200_device_count": (ctypes.c_int, [_PI32]),
     "moe_b200_device_props_get": (ctypes.c_int, [_I32, ctypes.POINTER(DeviceProps)]),
     "moe_b200_set_device": (ctypes.c_int, [_I32]),
@@ -337,6 +348,17 @@ class MoE:
 
     __call__ = compute
 
+    def prepack(self, inputs: Sequence[Any], share: bool = False, stream=None) -> bool:
+        """Pre-pack the node's constant weights (QMoE: dequantised copies used by
+        prefill-sized calls; ``share`` is the session option
+        ``ep.musa.enable_prepack_weight_sharing``).  Returns ORT's ``is_packed`` (always
+        False: decode-sized calls still read the packed initializers)."""
+        refs = (TensorRef * len(inputs))(*[tensor_ref(t) for t in inputs])
+        packed = ctypes.c_int32(0)
+        check(lib().moe_b200_kernel_prepack(self._h, len(inputs), refs, int(bool(share)),
+                                            _stream_handle(stream), ctypes.byref(packed)))
+        return bool(packed.value)
+
     def release(self) -> None:
         if getattr(self, "_h", None) is not None and self._h.value:
             check(lib().moe_b200_kernel_release(self._h))
@@ -371,21 +393,77 @@ def make_problem(num_rows, hidden_size, inter_size, num_experts, dtype, has_fc3=
     return Problem(num_rows, hidden_size, inter_size, num_experts, dtype, int(has_fc3), a)
 
 
-def workspace_size(problem: Problem) -> int:
+def workspace_size(problem: Problem, prepacked: "Prepacked | None" = None) -> int:
     n = ctypes.c_size_t(0)
-    check(lib().moe_b200_workspace_size(ctypes.byref(problem), ctypes.byref(n)))
+    if prepacked is None:
+        check(lib().moe_b200_workspace_size(ctypes.byref(problem), ctypes.byref(n)))
+    else:
+        check(lib().moe_b200_workspace_size_prepacked(ctypes.byref(problem), prepacked.handle,
+                                                      ctypes.byref(n)))
     return n.value
 
 
-def forward(problem: Problem, tensors: Mapping[str, Any], workspace, stream=None) -> None:
-    """One layer call with a caller-owned workspace (a CUDA uint8 tensor)."""
-    t = Tensors()
-    for name, _ in Tensors._fields_:
-        v = tensors.get(name)
-        setattr(t, name, None if v is None else (v if isinstance(v, int) else v.data_ptr()))
-    check(lib().moe_b200_forward(ctypes.byref(problem), ctypes.byref(t),
-                                 workspace.data_ptr(), workspace.numel(),
-                                 _stream_handle(stream)))
+def forward(problem: Problem, tensors: Mapping[str, Any], workspace, stream=None,
+            prepacked: "Prepacked | None" = None, events=None) -> None:
+    """One layer call with a caller-owned workspace (a CUDA uint8 tensor); with
+    ``prepacked``, prefill-sized QMoE calls run on the prepacked weights; ``events``
+    (8 CUDA events) records the stage boundaries as :func:`forward_staged` does."""
+    t = _tensors_struct(tensors)
+    if prepacked is None and events is None:
+        check(lib().moe_b200_forward(ctypes.byref(problem), ctypes.byref(t),
+                                     workspace.data_ptr(), workspace.numel(),
+                                     _stream_handle(stream)))
+        return
+    ev = None
+    if events is not None:
+        ev = (ctypes.c_void_p * len(events))(*[None if e is None else e.cuda_event
+                                               for e in events])
+    check(lib().moe_b200_forward_prepacked(
+        ctypes.byref(problem), ctypes.byref(t),
+        None if prepacked is None else prepacked.handle, workspace.data_ptr(),
+        workspace.numel(), _stream_handle(stream), ev, 0 if events is None else len(events)))
+
+
+class Prepacked:
+    """Dequantised copies of a QMoE node's expert weights (``moe_b200_prepack_create``).
+    ``weights`` maps fc1/fc2/fc3 ``*_weights`` and ``*_scales`` to CUDA tensors;
+    ``share=True`` reuses an existing prepack of identical content."""
+
+    def __init__(self, problem: Problem, weights: Mapping[str, Any], share: bool = False,
+                 stream=None):
+        t = _tensors_struct(weights)
+        h = ctypes.c_void_p()
+        check(lib().moe_b200_prepack_create(ctypes.byref(problem), ctypes.byref(t),
+                                            int(bool(share)), _stream_handle(stream),
+                                            ctypes.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def info(self) -> tuple[int, int]:
+        """(device bytes, reference count)."""
+        n, r = ctypes.c_size_t(0), ctypes.c_int32(0)
+        check(lib().moe_b200_prepack_info(self._h, ctypes.byref(n), ctypes.byref(r)))
+        return n.value, r.value
+
+    def release(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            check(lib().moe_b200_prepack_release(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.release()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
 
 
 def _tensors_struct(tensors: Mapping[str, Any]) -> Tensors:
@@ -547,6 +625,11 @@ class Pipeline:
         check(lib().moe_b200_pipeline_submit(self._h, host_input.data_ptr(),
                                              host_router_probs.data_ptr(),
                                              host_output.data_ptr(), rows))
+
+    def set_prepacked(self, prepacked: "Prepacked | None") -> None:
+        """Later calls may take the prepacked QMoE weights (the pipeline holds a reference)."""
+        check(lib().moe_b200_pipeline_set_prepacked(
+            self._h, None if prepacked is None else prepacked.handle))
 
     def synchronize(self) -> None:
         check(lib().moe_b200_pipeline_synchronize(self._h))

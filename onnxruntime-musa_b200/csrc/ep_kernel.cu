@@ -19,6 +19,7 @@
 
 #include "../../include/moe_b200.h"
 #include "moe_kernels.h"
+#include "prepack.h"
 
 namespace {
 
@@ -65,6 +66,11 @@ struct moe_b200_kernel {
     size_t bytes = 0;
   };
   std::unordered_map<cudaStream_t, Ws> ws;  // guarded by mu
+  // Pre-pack (QMoE): the prepack and the device pointers of the weight and scale
+  // inputs it was made from (fc1 w/s, fc2 w/s, fc3 w/s); computes whose inputs are
+  // these pointers use it.
+  moe_b200_prepacked* pk = nullptr;
+  const void* pk_src[6] = {};
 };
 
 namespace {
@@ -271,8 +277,14 @@ int moe_b200_kernel_compute(moe_b200_kernel* kern, int32_t num_inputs,
   p.has_fc3 = w3 != nullptr;
   p.attrs = kern->attrs;
   if (!q) p.attrs.expert_weight_bits = 0;
+  const moe_b200_prepacked* pk = nullptr;
+  if (q && kern->pk != nullptr) {
+    const void* src[6] = {w1->data, in[kFc1S].data, w2->data, in[kFc2S].data,
+                          w3 ? w3->data : nullptr, w3 ? in[kFc3S].data : nullptr};
+    if (std::memcmp(src, kern->pk_src, sizeof(src)) == 0) pk = kern->pk;
+  }
   size_t need = 0;
-  st = moe_b200_workspace_size(&p, &need);
+  st = moe_b200_workspace_size_prepacked(&p, pk, &need);
   if (st != MOE_B200_OK) return st;
 
   moe_b200_tensors t{};
@@ -310,7 +322,65 @@ int moe_b200_kernel_compute(moe_b200_kernel* kern, int32_t num_inputs,
     // The call below only enqueues work on `s`; a concurrent caller on another
     // stream has its own workspace, and callers sharing a stream are ordered by it.
   }
-  return moe_b200_forward(&p, &t, wsp, need, stream);
+  return moe_b200_forward_prepacked(&p, &t, pk, wsp, need, stream, nullptr, 0);
+}
+
+int moe_b200_kernel_prepack(moe_b200_kernel* kern, int32_t num_inputs,
+                            const moe_b200_tensor_ref* in, int32_t share, void* stream,
+                            int32_t* is_packed) {
+  if (kern == nullptr || in == nullptr)
+    return (efail(MOE_B200_INVALID_ARGUMENT, "kernel and inputs must be non-NULL"));
+  if (is_packed != nullptr) *is_packed = 0;
+  if (!kern->quantized)
+    return MOE_B200_OK;  // MoE weights are used as given: nothing to pack
+  // QMoE schema slots: fc1 w/s/b 2..4, fc2 w/s/b 5..7, fc3 w/s/b 8..10.
+  if (num_inputs < 7)
+    return (efail(MOE_B200_INVALID_ARGUMENT, "QMoE pre-pack needs inputs up to fc2_experts_bias"));
+  const moe_b200_tensor_ref& w1 = in[2];
+  const moe_b200_tensor_ref& s1 = in[3];
+  const moe_b200_tensor_ref& w2 = in[5];
+  const moe_b200_tensor_ref& s2 = in[6];
+  const bool has3 = num_inputs > 8 && in[8].data != nullptr;
+  if (w1.data == nullptr || w2.data == nullptr || s1.data == nullptr || s2.data == nullptr ||
+      w1.rank != 3 || w2.rank != 3 || s1.rank < 2)
+    return (efail(MOE_B200_INVALID_ARGUMENT, "QMoE pre-pack: fc1/fc2 weights and scales are required"));
+  if (has3 && (num_inputs < 10 || in[9].data == nullptr))
+    return (efail(MOE_B200_INVALID_ARGUMENT, "QMoE pre-pack: fc3_scales is required with fc3 weights"));
+  const int bits = kern->attrs.expert_weight_bits;
+  moe_b200_problem p{};
+  p.num_rows = 0;
+  p.num_experts = w1.dims[0];
+  p.hidden_size = w2.dims[1];
+  p.inter_size = w2.dims[2] * 8 / bits;
+  p.dtype = s1.elem_type;
+  p.has_fc3 = has3 ? 1 : 0;
+  p.attrs = kern->attrs;
+  if (w1.dims[2] * 8 / bits != p.hidden_size || w1.elem_type != MOE_B200_UINT8 ||
+      w2.elem_type != MOE_B200_UINT8)
+    return (efail(MOE_B200_INVALID_ARGUMENT, "QMoE pre-pack: fc1 %s and fc2 %s weights disagree",
+                  shape_str(w1).c_str(), shape_str(w2).c_str()));
+  const int64_t n1 = (p.attrs.activation_type == MOE_B200_ACT_SWIGLU && p.attrs.swiglu_fusion != 0)
+                         ? 2 * p.inter_size : p.inter_size;
+  if (w1.dims[1] != n1)
+    return (efail(MOE_B200_INVALID_ARGUMENT, "QMoE pre-pack: fc1 has %lld rows, expected %lld",
+                  (long long)w1.dims[1], (long long)n1));
+  moe_b200_tensors t{};
+  t.fc1_weights = w1.data;
+  t.fc1_scales = s1.data;
+  t.fc2_weights = w2.data;
+  t.fc2_scales = s2.data;
+  t.fc3_weights = has3 ? in[8].data : nullptr;
+  t.fc3_scales = has3 ? in[9].data : nullptr;
+  moe_b200_prepacked* pk = nullptr;
+  int st = moe_b200_prepack_create(&p, &t, share, stream, &pk);
+  if (st != MOE_B200_OK) return st;
+  std::lock_guard<std::mutex> lock(kern->mu);
+  if (kern->pk != nullptr) moe_b200_prepack_release(kern->pk);
+  kern->pk = pk;
+  const void* src[6] = {t.fc1_weights, t.fc1_scales, t.fc2_weights, t.fc2_scales,
+                        t.fc3_weights, t.fc3_scales};
+  std::memcpy(kern->pk_src, src, sizeof(src));
+  return MOE_B200_OK;
 }
 
 int moe_b200_kernel_release(moe_b200_kernel* kern) {
@@ -323,6 +393,8 @@ int moe_b200_kernel_release(moe_b200_kernel* kern) {
         cudaFree(kv.second.ptr);
       }
     kern->ws.clear();
+    if (kern->pk != nullptr) moe_b200_prepack_release(kern->pk);
+    kern->pk = nullptr;
   }
   delete kern;
   return MOE_B200_OK;

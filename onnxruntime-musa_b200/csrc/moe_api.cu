@@ -23,6 +23,7 @@
 #include "../../include/moe_b200.h"
 #include "ep_p2p.h"
 #include "moe_kernels.h"
+#include "prepack.h"
 #include "qmoe.h"
 
 using namespace moe;
@@ -95,7 +96,8 @@ bool swiglu_fused(const moe_b200_problem& p) {
   return p.attrs.activation_type == MOE_B200_ACT_SWIGLU && p.attrs.swiglu_fusion != 0;
 }
 
-WsLayout plan_workspace(const moe_b200_problem& p) {
+// `prepacked`: the call runs on prepacked weights (no dequantised copies in the workspace).
+WsLayout plan_workspace(const moe_b200_problem& p, bool prepacked = false) {
   WsLayout L{};
   const int64_t T = p.num_rows, E = p.num_experts, k = p.attrs.k;
   const int64_t R = T * k;
@@ -117,7 +119,7 @@ WsLayout plan_workspace(const moe_b200_problem& p) {
   L.rowsum = take(R * 4);                // A row sums of the packed (QMoE) GEMMs
   L.xp = take(R * p.hidden_size * es);   // gathered input, later fc2 output
   L.act = take(R * p.inter_size * es);
-  L.qmoe = take(qmoe_workspace_bytes(p));
+  L.qmoe = take(prepacked ? 0 : qmoe_workspace_bytes(p));
   L.total = o;
   return L;
 }
@@ -281,9 +283,10 @@ enum Stage { kStRoute = 0, kStPlan, kStGather, kStDequant, kStFc1, kStFc2, kStCo
 // output; router_probs is not read.
 int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
                  size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev = nullptr,
-                 const int32_t* given_idx = nullptr) {
+                 const int32_t* given_idx = nullptr, const moe_b200_prepacked* pk = nullptr) {
   auto mark = [&](int i) { if (ev && ev[i]) cudaEventRecord(ev[i], s); };
-  const WsLayout L = plan_workspace(p);
+  const bool use_pk = prepack_applies(pk, p);
+  const WsLayout L = plan_workspace(p, use_pk);
   if (ws_bytes < L.total)
     return fail(MOE_B200_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than %zu",
                 ws_bytes, L.total);
@@ -390,8 +393,13 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   const void* w2 = t.fc2_weights;
   const void* w3 = t.fc3_weights;
   mark(kStDequant);
-  const bool fused_q = qmoe_use_fused(p);
-  if (p.attrs.expert_weight_bits != 0 && !fused_q) {
+  const bool fused_q = !use_pk && qmoe_use_fused(p);
+  if (use_pk) {
+    // Weights dequantised once at session initialisation (moe_b200_prepack_create).
+    w1 = pk->w1;
+    w2 = pk->w2;
+    w3 = pk->w3;
+  } else if (p.attrs.expert_weight_bits != 0 && !fused_q) {
     // QMoE prefill: dequantise the weights of every expert into the workspace, then run
     // the same grouped GEMMs.
     QmoeDequantOut dq;
@@ -704,6 +712,39 @@ int moe_b200_forward_staged(const moe_b200_problem* problem, const moe_b200_tens
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = forward_impl(*problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes, s, ev);
   if (st == MOE_B200_OK && problem->num_rows == 0)
+    for (int i = 0; i <= kNumStages; ++i)
+      if (ev[i]) MOE_CUDA_CHECK(cudaEventRecord(ev[i], s), "event");
+  return st;
+}
+
+int moe_b200_workspace_size_prepacked(const moe_b200_problem* problem,
+                                      const moe_b200_prepacked* prepacked, size_t* bytes) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  if (bytes == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "bytes is NULL");
+  *bytes = plan_workspace(*problem, prepack_applies(prepacked, *problem)).total;
+  return MOE_B200_OK;
+}
+
+int moe_b200_forward_prepacked(const moe_b200_problem* problem, const moe_b200_tensors* t,
+                               const moe_b200_prepacked* prepacked, void* workspace,
+                               size_t workspace_bytes, void* stream, void* const* events,
+                               int32_t num_events) {
+  int st = validate_problem(problem);
+  if (st != MOE_B200_OK) return st;
+  if (t == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "tensors is NULL");
+  if (events != nullptr && num_events < kNumStages + 1)
+    return fail(MOE_B200_INVALID_ARGUMENT, "num_events=%d < %d", num_events, kNumStages + 1);
+  if (prepacked != nullptr && problem->attrs.expert_weight_bits != 0 &&
+      !prepack_matches(*prepacked, *problem))
+    return fail(MOE_B200_INVALID_ARGUMENT, "the prepack was made for other weight shapes");
+  cudaEvent_t ev[kNumStages + 1];
+  for (int i = 0; i <= kNumStages; ++i)
+    ev[i] = events != nullptr ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = forward_impl(*problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes, s,
+                    events != nullptr ? ev : nullptr, nullptr, prepacked);
+  if (st == MOE_B200_OK && events != nullptr && problem->num_rows == 0)
     for (int i = 0; i <= kNumStages; ++i)
       if (ev[i]) MOE_CUDA_CHECK(cudaEventRecord(ev[i], s), "event");
   return st;

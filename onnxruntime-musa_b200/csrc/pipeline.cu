@@ -17,10 +17,12 @@
 // Every dependency is a CUDA event waited on by a stream: submit never blocks the host.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "../../include/moe_b200.h"
 #include "moe_kernels.h"
+#include "prepack.h"
 
 struct moe_b200_pipeline {
   moe_b200_problem problem{};   // num_rows = the largest call
@@ -32,6 +34,7 @@ struct moe_b200_pipeline {
   cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
   void* workspace = nullptr;
   size_t ws_bytes = 0;
+  moe_b200_prepacked* prepacked = nullptr;  // one reference held
   struct Slot {
     void* x = nullptr;
     void* lg = nullptr;
@@ -65,6 +68,7 @@ void destroy(moe_b200_pipeline* pl) {
     if (s.out_done) cudaEventDestroy(s.out_done);
   }
   cudaFree(pl->workspace);
+  if (pl->prepacked != nullptr) moe_b200_prepack_release(pl->prepacked);
   if (pl->s_in) cudaStreamDestroy(pl->s_in);
   if (pl->s_comp) cudaStreamDestroy(pl->s_comp);
   if (pl->s_out) cudaStreamDestroy(pl->s_out);
@@ -87,9 +91,18 @@ int moe_b200_pipeline_create(const moe_b200_problem* problem, const moe_b200_ten
     return moe::set_error(MOE_B200_INVALID_ARGUMENT, "depth=%d must be in [1, 8]", depth);
   if (problem->num_rows < 1)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT, "num_rows (the largest call) must be >= 1");
+  // Workspace for every call size up to num_rows: the largest call's, and (QMoE) a
+  // decode-sized call's, whose fp32 partial sums the prefill paths do not need.
   size_t ws = 0;
   int st = moe_b200_workspace_size(problem, &ws);
   if (st != MOE_B200_OK) return st;
+  if (problem->attrs.expert_weight_bits != 0) {
+    moe_b200_problem small = *problem;
+    small.num_rows = std::min<int64_t>(problem->num_rows, 512 / problem->attrs.k);
+    size_t ws_small = 0;
+    if (small.num_rows > 0 && moe_b200_workspace_size(&small, &ws_small) == MOE_B200_OK)
+      ws = std::max(ws, ws_small);
+  }
   auto* pl = new moe_b200_pipeline();
   pl->problem = *problem;
   pl->weights = *weights;
@@ -130,6 +143,22 @@ int moe_b200_pipeline_create(const moe_b200_problem* problem, const moe_b200_ten
   return MOE_B200_OK;
 }
 
+int moe_b200_pipeline_set_prepacked(moe_b200_pipeline* pl, moe_b200_prepacked* prepacked) {
+  if (pl == nullptr) return moe::set_error(MOE_B200_INVALID_ARGUMENT, "pipeline is NULL");
+  if (prepacked != nullptr && !moe::prepack_matches(*prepacked, pl->problem))
+    return moe::set_error(MOE_B200_INVALID_ARGUMENT, "the prepack was made for other weight shapes");
+  // Calls already submitted keep the weights they were enqueued with; the reference
+  // dropped here is released only after them.
+  if (pl->prepacked != nullptr) {
+    cudaError_t e = cudaStreamSynchronize(pl->s_comp);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    moe_b200_prepack_release(pl->prepacked);
+  }
+  if (prepacked != nullptr) prepacked->refs.fetch_add(1);
+  pl->prepacked = prepacked;
+  return MOE_B200_OK;
+}
+
 int moe_b200_pipeline_submit(moe_b200_pipeline* pl, const void* host_input,
                              const void* host_router_probs, void* host_output,
                              int64_t num_rows) {
@@ -160,7 +189,8 @@ int moe_b200_pipeline_submit(moe_b200_pipeline* pl, const void* host_input,
   t.input = s.x;
   t.router_probs = s.lg;
   t.output = s.out;
-  const int st = moe_b200_forward(&p, &t, pl->workspace, pl->ws_bytes, pl->s_comp);
+  const int st = moe_b200_forward_prepacked(&p, &t, pl->prepacked, pl->workspace, pl->ws_bytes,
+                                            pl->s_comp, nullptr, 0);
   if (st != MOE_B200_OK) return st;
   PL_CHECK(cudaEventRecord(s.comp_done, pl->s_comp), "record");
 

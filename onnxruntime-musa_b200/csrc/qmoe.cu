@@ -319,6 +319,10 @@ bool qmoe_use_fused(const moe_b200_problem& p) {
 size_t qmoe_workspace_bytes(const moe_b200_problem& p) {
   if (p.attrs.expert_weight_bits == 0 || qmoe_use_fused(p)) return 0;
   if (qmoe_use_decode(p)) return fc1_partial_bytes(p) + fc2_partial_bytes(p) + raw4_ws(p).total;
+  return qmoe_dequantized_bytes(p);
+}
+
+size_t qmoe_dequantized_bytes(const moe_b200_problem& p) {
   const size_t es = dtype_bytes(p.dtype);
   const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
   size_t b = align256(E * fc1_rows(p) * H * es) + align256(E * H * I * es);
@@ -326,15 +330,14 @@ size_t qmoe_workspace_bytes(const moe_b200_problem& p) {
   return b;
 }
 
-int qmoe_dequantize(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
-                    const int32_t* expert_offsets, QmoeDequantOut* out, cudaStream_t s) {
-  (void)expert_offsets;
+int qmoe_dequantize_into(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* dst,
+                         QmoeDequantOut* out, cudaStream_t s) {
   if (t.fc1_scales == nullptr || t.fc2_scales == nullptr || (p.has_fc3 && t.fc3_scales == nullptr))
     return MOE_B200_INVALID_ARGUMENT;
   const size_t es = dtype_bytes(p.dtype);
   const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
   const int bits = p.attrs.expert_weight_bits, bs = p.attrs.block_size;
-  uint8_t* w1 = ws;
+  uint8_t* w1 = dst;
   uint8_t* w2 = w1 + align256(E * fc1_rows(p) * H * es);
   uint8_t* w3 = w2 + align256(E * H * I * es);
   cudaError_t st = dequant(p.dtype, t.fc1_weights, t.fc1_scales, E * fc1_rows(p),
@@ -348,6 +351,12 @@ int qmoe_dequantize(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_
   out->w2 = w2;
   out->w3 = p.has_fc3 ? w3 : nullptr;
   return MOE_B200_OK;
+}
+
+int qmoe_dequantize(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
+                    const int32_t* expert_offsets, QmoeDequantOut* out, cudaStream_t s) {
+  (void)expert_offsets;
+  return qmoe_dequantize_into(p, t, ws, out, s);
 }
 
 }  // namespace moe

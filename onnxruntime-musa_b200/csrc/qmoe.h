@@ -39,6 +39,14 @@ int qmoe_decode_combine(const moe_b200_problem& p, const moe_b200_tensors& t, co
                         const int32_t* offsets, const int32_t* pos, const float* w,
                         cudaStream_t s);
 
+// Bytes of the dequantised fc1/fc2(/fc3) copies of every expert (element type p.dtype,
+// each matrix 256-byte aligned).
+size_t qmoe_dequantized_bytes(const moe_b200_problem& p);
+
+// Dequantises fc1/fc2(/fc3) of every expert into `dst` (qmoe_dequantized_bytes(p) bytes).
+int qmoe_dequantize_into(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* dst,
+                         QmoeDequantOut* out, cudaStream_t s);
+
 // Dequantises fc1/fc2(/fc3) of every expert into `ws` in element type p.dtype.
 int qmoe_dequantize(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
                     const int32_t* expert_offsets, QmoeDequantOut* out, cudaStream_t s);

@@ -145,3 +145,52 @@ def test_new_entries_validate_before_touching_the_device(pkg):
     # Stage events: fewer than stages + 1.
     evs = (ctypes.c_void_p * 3)()
     assert L.moe_b200_forward_staged(ctypes.byref(p), ctypes.byref(t), None, 0, None, evs, 3) == pkg.INVALID_ARGUMENT
+
+
+def test_prepack_entries_validate_before_touching_the_device(pkg):
+    """QMoE weight prepack: argument checks on the host (no CUDA call)."""
+    import ctypes
+    L = pkg.lib()
+    h = ctypes.c_void_p()
+    t = pkg.Tensors()
+    # MoE (bits 0) has nothing to prepack; QMoE with NULL codes or scales is refused.
+    p = pkg.make_problem(0, 128, 128, 8, pkg.FLOAT16, k=2, activation_type="silu")
+    assert L.moe_b200_prepack_create(ctypes.byref(p), ctypes.byref(t), 0, None,
+                                     ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    q = pkg.make_problem(0, 128, 128, 8, pkg.FLOAT16, has_fc3=True, k=2, activation_type="silu",
+                         expert_weight_bits=4, block_size=128)
+    assert L.moe_b200_prepack_create(ctypes.byref(q), ctypes.byref(t), 1, None,
+                                     ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    # Shape checks are the layer call's: a block size that is not a power of two.
+    bad = pkg.make_problem(0, 128, 128, 8, pkg.FLOAT16, k=2, activation_type="silu",
+                           expert_weight_bits=8, block_size=48)
+    assert L.moe_b200_prepack_create(ctypes.byref(bad), ctypes.byref(t), 0, None,
+                                     ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_prepack_create(None, ctypes.byref(t), 0, None, ctypes.byref(h)) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_prepack_info(None, None, None) == pkg.INVALID_ARGUMENT
+    assert L.moe_b200_prepack_release(None) == pkg.OK
+    # Without a prepack the prepacked workspace size is the plain one.
+    n1, n2 = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    q.num_rows = 4096
+    assert L.moe_b200_workspace_size(ctypes.byref(q), ctypes.byref(n1)) == pkg.OK
+    assert L.moe_b200_workspace_size_prepacked(ctypes.byref(q), None, ctypes.byref(n2)) == pkg.OK
+    assert n1.value == n2.value > 0
+    # Stage events of the prepacked forward: fewer than stages + 1.
+    evs = (ctypes.c_void_p * 3)()
+    assert L.moe_b200_forward_prepacked(ctypes.byref(q), ctypes.byref(t), None, None, 0, None,
+                                        evs, 3) == pkg.INVALID_ARGUMENT
+    # Kernel pre-pack of an MoE node: nothing to pack, is_packed = 0.
+    op = pkg.MoE(k=2, activation_type="silu")
+    try:
+        refs = (pkg.TensorRef * 8)()
+        packed = ctypes.c_int32(7)
+        assert L.moe_b200_kernel_prepack(op._h, 8, refs, 0, None, ctypes.byref(packed)) == pkg.OK
+        assert packed.value == 0
+    finally:
+        op.release()
+    op = pkg.QMoE(k=2, activation_type="silu", expert_weight_bits=4, block_size=128)
+    try:
+        refs = (pkg.TensorRef * 11)()
+        assert L.moe_b200_kernel_prepack(op._h, 11, refs, 0, None, None) == pkg.INVALID_ARGUMENT
+    finally:
+        op.release()
