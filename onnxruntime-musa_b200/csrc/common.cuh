@@ -283,6 +283,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
+// Four rows (r0..r3) of a 2-D tensor whose map has a one-row box, written one after the
+// other at dst (4 x the box bytes), completion on the leader CTA's barrier `bar`.
+__device__ __forceinline__ void tma_gather4_pair(void* dst, const CUtensorMap* map, uint32_t bar,
+                                                 int c0, int r0, int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile::gather4"
+      ".mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
                                                  int c0, int c1, int c2, int c3) {
   asm volatile(

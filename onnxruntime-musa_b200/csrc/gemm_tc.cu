@@ -92,6 +92,10 @@ struct TcParams {
   int qepi;
   float qbias;
   const float* rowsum;
+  // CTA-pair kernel: A row p is row a_src[p] / a_k of the map's tensor (TMA gather4,
+  // four rows per lane of the producer warp); nullptr = A rows p of the map's tensor.
+  const int32_t* a_src;
+  int a_k;
 };
 
 // Per-tile phase trace of CTA 0 (diagnostics only).  Entry i: [2i] = %globaltimer ns,
@@ -706,11 +710,15 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int it = 0;; ++it) {
-        int L;
+    // Lane 0 claims tiles, waits for free slots and loads B (and A when it is not
+    // gathered).  With a gathered A (p.a_src) every lane loads four A rows per k-block
+    // with one gather4: lane l rows 4l..4l+3 of this CTA's share of the tile.
+    const bool gather = p.a_src != nullptr;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int it = 0;; ++it) {
+      int L = -1;
+      if (lane == 0) {
         if (leader) {
           const int slot = it % TQ;
           if (!mbar_wait_cluster(&tq_empty[slot], ((it / TQ) & 1) ^ 1)) {
@@ -728,48 +736,70 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
         } else if (*abort_flag || !tq_take(it, s_tq, tq_full, tq_empty, false, L)) {
           atomicExch(p.err, kErrTimeoutProducer);
           *abort_flag = 1;
-          break;
+          L = -1;
         }
-        if (L < 0) break;
-        trace(p, kTrClaim, L);
-        if (p.test_stall) continue;
-        const PairTile t = pair_tile(L, s_tiles, s_offs, p);
-        const int e = t.e, n = t.n;
-        const int row0 = t.nt ? t.r0 + static_cast<int>(rank) * (t.nt / 2)
-                              : t.r0 + static_cast<int>(rank) * BM;
-        const CUtensorMap* bmap = (p.gated && rank == 1) ? &map_b3 : &map_b1;
-        int bg, brow;
-        if (p.gated) {
-          bg = rank == 1 ? p.b3_g : p.b1_g;
-          brow = n * (BN / 2) + (rank == 1 ? p.b3_noff : p.b1_noff);
-        } else {
-          bg = p.b1_g;
-          brow = n * BN + static_cast<int>(rank) * (BN / 2) + p.b1_noff;
+      }
+      L = __shfl_sync(0xffffffffu, L, 0);
+      if (L < 0) break;
+      if (lane == 0) trace(p, kTrClaim, L);
+      if (p.test_stall) continue;
+      const PairTile t = pair_tile(L, s_tiles, s_offs, p);
+      const int e = t.e, n = t.n;
+      const int row0 = t.nt ? t.r0 + static_cast<int>(rank) * (t.nt / 2)
+                            : t.r0 + static_cast<int>(rank) * BM;
+      const CUtensorMap* bmap = (p.gated && rank == 1) ? &map_b3 : &map_b1;
+      int bg, brow;
+      if (p.gated) {
+        bg = rank == 1 ? p.b3_g : p.b1_g;
+        brow = n * (BN / 2) + (rank == 1 ? p.b3_noff : p.b1_noff);
+      } else {
+        bg = p.b1_g;
+        brow = n * BN + static_cast<int>(rank) * (BN / 2) + p.b1_noff;
+      }
+      // Swapped gated tile: this CTA's weight rows are the 64 gate rows, then the 64
+      // linear rows, of output columns n*128 + rank*64 + [0,64).
+      const int sw_col = n * (BN / 2) + static_cast<int>(rank) * SW_HALF;
+      const int tok_boxes = (t.nt / 2 + SW_TOK_ROWS - 1) / SW_TOK_ROWS;  // 1 or 2
+      // A rows of this CTA: 128 (normal tile) or nt / 2 (swapped; a multiple of 8).
+      const int a_rows = t.nt ? t.nt / 2 : BM;
+      const uint32_t a_bytes =
+          gather ? a_rows * BK * 2 : (t.nt ? tok_boxes * SW_TOK_ROWS * BK * 2 : A_BYTES);
+      const uint32_t tx = 2 * (B_HALF + a_bytes);
+      // Gathered rows of this lane: source rows of the tile's rows past the expert's end
+      // are replaced by a valid row (their outputs are never stored).
+      int g0 = 0, g1 = 0, g2 = 0, g3 = 0;
+      const bool g_issue = gather && 4 * lane < a_rows;
+      if (g_issue) {
+        const int end = t.r0 + t.rows;
+        const int rb = row0 + 4 * lane;
+        g0 = rb + 0 < end ? __ldg(p.a_src + rb + 0) / p.a_k : 0;
+        g1 = rb + 1 < end ? __ldg(p.a_src + rb + 1) / p.a_k : 0;
+        g2 = rb + 2 < end ? __ldg(p.a_src + rb + 2) / p.a_k : 0;
+        g3 = rb + 3 < end ? __ldg(p.a_src + rb + 3) / p.a_k : 0;
+      }
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        if (lane == 0 && !mbar_wait(&empty[stage], phase ^ 1)) {
+          atomicExch(p.err, kErrTimeoutProducer);
+          *abort_flag = 1;
+          ok = false;
         }
-        // Swapped gated tile: this CTA's weight rows are the 64 gate rows, then the 64
-        // linear rows, of output columns n*128 + rank*64 + [0,64).
-        const int sw_col = n * (BN / 2) + static_cast<int>(rank) * SW_HALF;
-        const int tok_boxes = (t.nt / 2 + SW_TOK_ROWS - 1) / SW_TOK_ROWS;  // 1 or 2
-        const uint32_t tx =
-            t.nt ? 2 * (B_HALF + tok_boxes * SW_TOK_ROWS * BK * 2) : 2 * P_STAGE_BYTES;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1)) {
-            atomicExch(p.err, kErrTimeoutProducer);
-            *abort_flag = 1;
-            break;
-          }
-          const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
+        const int kc = kb * BK;
+        uint8_t* a_dst = sA + stage * A_BYTES;
+        uint8_t* b_dst = sB + stage * B_HALF;
+        if (lane == 0) {
           if (leader) mbar_arrive_expect_tx(&full[stage], tx);
-          const int kc = kb * BK;
-          uint8_t* a_dst = sA + stage * A_BYTES;
-          uint8_t* b_dst = sB + stage * B_HALF;
           if (!t.nt) {
-            tma_load_2d_pair(a_dst, &map_a, full_leader, kc, row0);
+            if (!gather) tma_load_2d_pair(a_dst, &map_a, full_leader, kc, row0);
             tma_load_4d_pair(b_dst, bmap, full_leader, kc, bg, brow, e);
           } else {
-            for (int j = 0; j < tok_boxes; ++j)
-              tma_load_2d_pair(a_dst + j * SW_TOK_ROWS * BK * 2, &map_a_sw, full_leader, kc,
-                               row0 + j * SW_TOK_ROWS);
+            if (!gather)
+              for (int j = 0; j < tok_boxes; ++j)
+                tma_load_2d_pair(a_dst + j * SW_TOK_ROWS * BK * 2, &map_a_sw, full_leader, kc,
+                                 row0 + j * SW_TOK_ROWS);
             if (p.gated) {
               tma_load_4d_pair(b_dst, &map_b1_sw, full_leader, kc, p.b1_g, sw_col + p.b1_noff, e);
               tma_load_4d_pair(b_dst + SW_HALF * BK * 2, &map_b3_sw, full_leader, kc, p.b3_g,
@@ -778,10 +808,13 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
               tma_load_4d_pair(b_dst, bmap, full_leader, kc, bg, brow, e);
             }
           }
-          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
         }
-        trace(p, kTrProdDone, L);
+        if (g_issue)
+          tma_gather4_pair(a_dst + lane * 4 * BK * 2, &map_a, full_leader, kc, g0, g1, g2, g3);
+        if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
       }
+      // After a timeout the next claim publishes -1 (abort_flag), so the consumers stop.
+      if (lane == 0 && ok) trace(p, kTrProdDone, L);
     }
   } else if (warp == 1) {
     // ------------------------------------------------- MMA issuer (leader CTA only)
@@ -1334,7 +1367,13 @@ void dump_trace(const char* path, int K, cudaStream_t s) {
 template <typename T>
 cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) {
   CUtensorMap ma, mb1, mb3;
-  if (!make_map_a(&ma, g.dtype, g.a, g.rows, g.K)) return cudaErrorInvalidValue;
+  // Gathered A (pair kernel only): the map covers the un-permuted rows with a one-row box.
+  const bool gather = pair && g.gather_src != nullptr;
+  if (gather) {
+    if (!make_map_a(&ma, g.dtype, g.gather_x, g.gather_x_rows, g.K, 1)) return cudaErrorInvalidValue;
+  } else if (!make_map_a(&ma, g.dtype, g.a, g.rows, g.K)) {
+    return cudaErrorInvalidValue;
+  }
   if (!make_map_b(&mb1, g.dtype, g.b1, g.K, g.E)) return cudaErrorInvalidValue;
   if (g.gated) {
     if (!make_map_b(&mb3, g.dtype, g.b3, g.K, g.E)) return cudaErrorInvalidValue;
@@ -1369,6 +1408,8 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   p.nseg = g.nseg;
   p.remap_world = g.remap_world;
   for (int i = 0; i < kMaxEpRanks; ++i) p.out_peers[i] = g.out_peers[i];
+  p.a_src = gather ? g.gather_src : nullptr;
+  p.a_k = gather ? g.gather_k : 1;
   const char* trace_path = pair ? std::getenv("MOE_B200_GEMM_TRACE") : nullptr;
   p.trace = trace_path != nullptr ? 1 : 0;
 
@@ -1380,7 +1421,8 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   }
   CUtensorMap ma_sw = ma, mb1_sw = mb1, mb3_sw = mb3;
   if (p.swap_max > 0) {
-    if (!make_map_a(&ma_sw, g.dtype, g.a, g.rows, g.K, SW_TOK_ROWS)) return cudaErrorInvalidValue;
+    if (!gather && !make_map_a(&ma_sw, g.dtype, g.a, g.rows, g.K, SW_TOK_ROWS))
+      return cudaErrorInvalidValue;
     if (g.gated) {
       if (!make_map_b(&mb1_sw, g.dtype, g.b1, g.K, g.E, SW_HALF) ||
           !make_map_b(&mb3_sw, g.dtype, g.b3, g.K, g.E, SW_HALF))
@@ -1533,10 +1575,25 @@ bool tc_supported(const GemmArgs& g) {
   return get_encode_fn() != nullptr;
 }
 
+namespace {
+// mode 0: choose (CTA pairs when experts average >= 256 rows), 1: single CTA, 2: pairs.
+bool use_pair(const GemmArgs& g, int mode) {
+  return mode == 2 || (mode == 0 && g.rows >= 256 * static_cast<int64_t>(g.E));
+}
+}  // namespace
+
+bool tc_pair_gathers(const GemmArgs& g, int mode) {
+  if (g.gather_src == nullptr || g.gather_x == nullptr || g.gather_x_rows < 1 || g.gather_k < 1)
+    return false;
+  if ((reinterpret_cast<uintptr_t>(g.gather_x) & 15) != 0) return false;
+  return tc_supported(g) && use_pair(g, mode);
+}
+
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, int mode, cudaStream_t s) {
   if (g.rows == 0 || g.N == 0) return cudaSuccess;
-  // mode 0: choose (CTA pairs when experts average >= 256 rows), 1: single CTA, 2: pairs.
-  const bool pair = mode == 2 || (mode == 0 && g.rows >= 256 * static_cast<int64_t>(g.E));
+  // A gathered A needs the pair kernel (callers gather into g.a otherwise).
+  if (g.gather_src != nullptr && !tc_pair_gathers(g, mode)) return cudaErrorInvalidValue;
+  const bool pair = use_pair(g, mode);
   if (g.dtype == kDtF16) return launch_t<__half>(g, num_sms, pair, s);
   if (g.dtype == kDtBF16) return launch_t<__nv_bfloat16>(g, num_sms, pair, s);
   return cudaErrorInvalidValue;

@@ -252,9 +252,25 @@ GemmArgs fc2_args(const moe_b200_problem& p, const void* w2, const void* b2) {
 // single-CTA or CTA-pair tensor-core kernel (used by tests to cover both);
 // MOE_B200_PAIR_SWAP_MAX overrides the swapped-tail-tile limit.
 cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
-  if (!env_flag("MOE_B200_FORCE_SIMT") && tc_supported(g)) {
-    const char* m = std::getenv("MOE_B200_TC_MODE");
-    const int mode = m ? std::atoi(m) : 0;
+  const bool tc = !env_flag("MOE_B200_FORCE_SIMT") && tc_supported(g);
+  const char* m = std::getenv("MOE_B200_TC_MODE");
+  const int mode = m ? std::atoi(m) : 0;
+  // A gathered A (set only with MOE_B200_GATHER_FUSION=1): the CTA-pair kernel loads the
+  // rows itself with TMA gather4 (four 128-byte rows per instruction); other kernels get
+  // a gather pass into g.a first.  The fused loads are exact but slower on B200 (C2 fc1
+  // 4.39 ms against 1.62 ms with the separate gather): at about 90 cycles per gather4, the
+  // 32 instructions a 128-row A tile needs per k-block take ~4x the k-block's MMA time.
+  if (g.gather_src != nullptr) {
+    const bool fuse = tc && tc_pair_gathers(g, mode);
+    if (!fuse) {
+      cudaError_t st = launch_gather(g.gather_x, static_cast<int64_t>(g.K) * dtype_bytes(g.dtype),
+                                     g.gather_k, g.gather_src, g.rows, const_cast<void*>(g.a), s);
+      if (st != cudaSuccess) return st;
+      g.gather_src = nullptr;
+      g.gather_x = nullptr;
+    }
+  }
+  if (tc) {
     // MOE_B200_PAIR_SWAP_MAX: row limit of the pair kernel's swapped tail tiles (0 = off).
     if (const char* sw = std::getenv("MOE_B200_PAIR_SWAP_MAX")) g.swap_max = std::atoi(sw);
     // MOE_B200_PAIR_STATIC=1: static round-robin tile schedule (comparison runs).
@@ -385,15 +401,20 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
     MOE_CUDA_CHECK(launch_plan(idx, T, k, E, cc, cb, offs, t128, t64, t256, pos, src, s, chunk),
                    "plan");
   }
+  // Routed rows gathered into xp (expert order).  With MOE_B200_GATHER_FUSION=1 the fc1
+  // GEMM gets the un-permuted input instead (run_gemm: TMA gather4 in the CTA-pair kernel,
+  // else a gather pass just before the GEMM).
+  const bool fused_q = !use_pk && qmoe_use_fused(p);
+  const bool gather_in_gemm = !fused_q && env_flag("MOE_B200_GATHER_FUSION");
   mark(kStGather);
-  MOE_CUDA_CHECK(launch_gather(t.input, static_cast<int64_t>(H) * es, k, src, R, xp, s),
-                 "gather");
+  if (!gather_in_gemm)
+    MOE_CUDA_CHECK(launch_gather(t.input, static_cast<int64_t>(H) * es, k, src, R, xp, s),
+                   "gather");
 
   const void* w1 = t.fc1_weights;
   const void* w2 = t.fc2_weights;
   const void* w3 = t.fc3_weights;
   mark(kStDequant);
-  const bool fused_q = !use_pk && qmoe_use_fused(p);
   if (use_pk) {
     // Weights dequantised once at session initialisation (moe_b200_prepack_create).
     w1 = pk->w1;
@@ -413,6 +434,12 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   GemmArgs g1 = fc1_args(p, w1, t.fc1_bias, w3, t.fc3_bias);
   g1.a = xp;
   g1.rows = R;
+  if (gather_in_gemm) {
+    g1.gather_x = t.input;
+    g1.gather_src = src;
+    g1.gather_k = k;
+    g1.gather_x_rows = T;
+  }
   g1.offsets = offs;
   g1.tiles128 = t128;
   g1.tiles64 = t64;

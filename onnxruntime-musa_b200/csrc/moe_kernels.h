@@ -135,6 +135,14 @@ struct GemmArgs {
   int nseg = 0;
   int remap_world = 1;
   void* out_peers[kMaxEpRanks] = {};
+  // Gathered A (fc1): row p of A is row gather_src[p] / gather_k of gather_x
+  // ([gather_x_rows, K]).  The CTA-pair tensor-core kernel reads those rows straight
+  // from gather_x with TMA gather4 loads; every other kernel gets them from a gather
+  // pass into `a` first (launch_gemm_tc_gathered).
+  const void* gather_x = nullptr;
+  const int32_t* gather_src = nullptr;
+  int gather_k = 1;
+  int64_t gather_x_rows = 0;
 };
 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);
@@ -142,6 +150,9 @@ cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);
 bool tc_supported(const GemmArgs& g);
 // mode: 0 = choose, 1 = single-CTA kernel, 2 = CTA-pair (cta_group::2) kernel.
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, int mode, cudaStream_t s);
+// True when launch_gemm_tc(g, mode) runs the CTA-pair kernel with A rows gathered by TMA
+// (g.gather_src set, operands aligned for the gather map).
+bool tc_pair_gathers(const GemmArgs& g, int mode);
 // CTA-pair kernel with int4/int8 B operands dequantised in shared memory (fp16 only).
 bool tc_q_supported(const GemmArgs& g);
 cudaError_t launch_gemm_tc_q(const GemmArgs& g, int num_sms, cudaStream_t s);

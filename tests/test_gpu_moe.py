@@ -459,3 +459,39 @@ def test_qmoe_sparse_mixer(pkg, orc, dev, T):
     ref = orc.qmoe(q["x"], q["router_probs"], q["fc1_q"], q["fc1_scales"], None, q["fc2_q"],
                    q["fc2_scales"], None, q["fc3_q"], q["fc3_scales"], None, **attrs)
     np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+
+
+@pytest.mark.parametrize("dtype_name", ["float16", "bfloat16"])
+@pytest.mark.parametrize("case", [(700, 256, 320, 4, 2, "silu", True),
+                                  (530, 192, 256, 8, 1, "gelu", False),
+                                  (300, 128, 136, 3, 2, "swiglu", True)],
+                         ids=["gated_k2", "plain_k1", "swiglu_halves"])
+def test_gather_fused_into_pair_gemm(pkg, orc, dev, dtype_name, case):
+    """MOE_B200_GATHER_FUSION=1: the CTA-pair kernel loads fc1's rows from the
+    un-permuted input with TMA gather4 (normal and swapped tail tiles).  Identical values
+    to the separate gather, and within tolerance of the oracle."""
+    T, H, I, E, k, act, gated = case
+    inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act=act, gated=gated, dtype="float32",
+                              bias=True, normalize=1, seed=T + E)
+    attrs = dict(inp["attrs"])
+    if act == "swiglu":
+        inp.update(fc1_w=np.concatenate([inp["fc1_w"], inp["fc3_w"]], 1),
+                   fc1_b=np.concatenate([inp["fc1_b"], inp["fc3_b"]], 1), fc3_w=None, fc3_b=None)
+        attrs.update(swiglu_fusion=2, activation_alpha=1.702, activation_beta=1.0,
+                     swiglu_limit=7.0)
+    d, h = moe_inputs_on(dev, inp, dtype_name)
+    env = {"MOE_B200_TC_MODE": "2", "MOE_B200_PAIR_SWAP_MAX": "240"}
+    old = {n: os.environ.get(n) for n in list(env) + ["MOE_B200_GATHER_FUSION"]}
+    try:
+        os.environ.update(env)
+        plain = run_moe(pkg, d, attrs)
+        os.environ["MOE_B200_GATHER_FUSION"] = "1"
+        fused = run_moe(pkg, d, attrs)
+    finally:
+        for n, v in old.items():
+            if v is None:
+                os.environ.pop(n, None)
+            else:
+                os.environ[n] = v
+    np.testing.assert_array_equal(as_np(fused), as_np(plain))
+    np.testing.assert_allclose(as_np(fused), oracle_out(orc, h, attrs), **TOL[dtype_name])
