@@ -36,6 +36,7 @@
 // fc2 (long K = inter_size) is split over K across CTAs; each split writes fp32 partial
 // sums [split][row][col] and the combine kernel adds splits in a fixed order, so the
 // result is deterministic.
+#include <algorithm>
 #include "qmoe_decode.h"
 
 namespace moe {
@@ -413,7 +414,35 @@ template <int BITS, bool GATED, int kScale, bool RAW4>
 __global__ void __launch_bounds__(QD_WARPS * 32, 4) qmoe_decode_kernel(const QDecodeArgs a) {
   extern __shared__ __align__(128) uint8_t s_ring[];  // one ring per warp
   uint8_t* ring = s_ring + (threadIdx.x >> 5) * ring_bytes<BITS, GATED>();
-  const int e = blockIdx.y;
+  // Grid rows cover the experts that can hold rows (min(E, routed rows)): row j takes the
+  // j-th expert with rows, found from the offsets.
+  int e = blockIdx.y;
+  if (gridDim.y < static_cast<unsigned>(a.E)) {
+    __shared__ int s_cnt[QD_WARPS];
+    __shared__ int s_e;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_e = -1;
+    int before = 0;  // experts with rows ahead of this 128-wide chunk
+    for (int c0 = 0; c0 < a.E; c0 += QD_WARPS * 32) {
+      const int ex = c0 + static_cast<int>(threadIdx.x);
+      const bool has = ex < a.E && a.offsets[ex + 1] > a.offsets[ex];
+      const unsigned m = __ballot_sync(0xffffffffu, has);
+      if (lane == 0) s_cnt[w] = __popc(m);
+      __syncthreads();
+      int rank = before + __popc(m & ((1u << lane) - 1u));
+      int total = 0;
+#pragma unroll
+      for (int i = 0; i < QD_WARPS; ++i) {
+        if (i < w) rank += s_cnt[i];
+        total += s_cnt[i];
+      }
+      if (has && rank == static_cast<int>(blockIdx.y)) s_e = ex;
+      before += total;
+      __syncthreads();
+    }
+    e = s_e;
+    if (e < 0) return;
+  }
   const int row_begin = a.offsets[e];
   const int cnt = a.offsets[e + 1] - row_begin;
   if (cnt == 0) return;
@@ -473,11 +502,21 @@ finalize_fc1_kernel(const QDecodeArgs a, __half* __restrict__ act) {
   if (n >= a.N) return;
   const int e = expert_of(a.offsets, a.E, r);
   const int64_t bi = e * a.bias_e_stride + static_cast<int64_t>(n) * a.bias_stride;
-  float g = 0.f, u = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
+  // All splits' loads in flight at once; the sums keep the split order.
+  float pg[kQmoeMaxSplits], pu[kQmoeMaxSplits];
+#pragma unroll
+  for (int s = 0; s < kQmoeMaxSplits; ++s) {
     const float* prow = a.out_partial + (static_cast<int64_t>(s) * a.rows + r) * a.ldo;
-    g += prow[n];
-    if (a.gated) u += prow[a.N + n];
+    pg[s] = s < a.splits ? prow[n] : 0.f;
+    pu[s] = s < a.splits && a.gated ? prow[a.N + n] : 0.f;
+  }
+  float g = 0.f, u = 0.f;
+#pragma unroll
+  for (int s = 0; s < kQmoeMaxSplits; ++s) {
+    if (s < a.splits) {
+      g += pg[s];
+      u += pu[s];
+    }
   }
   const __half* b1p = static_cast<const __half*>(a.bias1);
   const __half* b3p = static_cast<const __half*>(a.bias3);
@@ -504,9 +543,19 @@ combine_partials_kernel(const float* __restrict__ part, int splits, int64_t rows
   float acc = 0.f;
   for (int j = 0; j < k; ++j) {
     const int64_t r = pos[static_cast<int64_t>(t) * k + j];
+    // All splits' loads (and the bias) in flight at once; the sums keep the split order.
+    float pv[kQmoeMaxSplits];
+#pragma unroll
+    for (int s = 0; s < kQmoeMaxSplits; ++s)
+      pv[s] = s < splits ? part[(static_cast<int64_t>(s) * rows + r) * H + c] : 0.f;
+    const float b =
+        bias != nullptr ? __half2float(bias[static_cast<int64_t>(expert_of(offsets, E, r)) * H + c])
+                        : 0.f;
     float y = 0.f;
-    for (int s = 0; s < splits; ++s) y += part[(static_cast<int64_t>(s) * rows + r) * H + c];
-    if (bias != nullptr) y += __half2float(bias[static_cast<int64_t>(expert_of(offsets, E, r)) * H + c]);
+#pragma unroll
+    for (int s = 0; s < kQmoeMaxSplits; ++s)
+      if (s < splits) y += pv[s];
+    if (bias != nullptr) y += b;
     acc += w[static_cast<int64_t>(t) * k + j] * y;
   }
   out[static_cast<int64_t>(t) * H + c] = __float2half_rn(acc);
@@ -522,7 +571,9 @@ cudaError_t launch_decode_t(const QDecodeArgs& a, cudaStream_t s) {
     if (st != cudaSuccess) return st;
     attr_set = true;
   }
-  const dim3 grid((a.N + QD_WARPS * 16 - 1) / (QD_WARPS * 16), a.E, a.splits);
+  // At most min(E, routed rows) experts hold rows: CTAs for the others would exit at once.
+  const int ey = static_cast<int>(std::min<int64_t>(a.E, std::max<int64_t>(a.rows, 1)));
+  const dim3 grid((a.N + QD_WARPS * 16 - 1) / (QD_WARPS * 16), ey, a.splits);
   qmoe_decode_kernel<BITS, GATED, kScale, RAW4><<<grid, QD_WARPS * 32, kSmem, s>>>(a);
   return cudaGetLastError();
 }
