@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 import pathlib
 from typing import Any, Mapping, Sequence
 
@@ -173,7 +174,13 @@ _lib: ctypes.CDLL | None = None
 
 
 def get_library_path() -> str:
-    """Path of the plugin's shared library (raises if it has not been built)."""
+    """Path of the plugin's shared library (raises if it has not been built);
+    ``MOE_B200_LIBRARY`` names another build of it."""
+    alt = os.environ.get("MOE_B200_LIBRARY")
+    if alt:
+        if not pathlib.Path(alt).is_file():
+            raise RuntimeError(f"MOE_B200_LIBRARY={alt} is not a file")
+        return alt
     if not _LIB_PATH.is_file():
         raise RuntimeError(f"{_LIB_PATH} is missing: run __graft_entry__.build() "
                            "(the MoE path has no CPU fallback)")
