@@ -15,6 +15,39 @@
 
 namespace moe {
 
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched with launch_dependent() may start while the previous kernel on its
+// stream is still running.  Before it reads anything that kernel wrote (or writes what
+// that kernel reads) it calls pdl_wait(), which returns once the previous grid has
+// completed and its memory is visible; it calls pdl_wait() before exiting in any case,
+// so that its own completion implies its predecessor's.  pdl_launch_dependents() lets
+// the next such kernel launch.  Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// True unless MOE_B200_PDL=0 (host side; read once).
+bool pdl_enabled();
+
+// Launches kernel<<<grid, block, smem, s>>>(args...) with programmatic stream
+// serialisation when pdl_enabled(): the kernel must follow the pdl_wait() rule above.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ------------------------------------------------------------------ error codes
 // Written to the workspace error word by device code.
 enum DeviceError : int {

@@ -35,6 +35,14 @@ thread_local std::string g_last_error;
 
 }  // namespace
 
+bool moe::pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_B200_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
+
 int moe::set_error(int code, const char* fmt, ...) {
   char buf[1024];
   va_list ap;

@@ -387,6 +387,8 @@ qdec_prep_kernel(const __half* __restrict__ x, int64_t rows, int K, __half* __re
                  float* __restrict__ corr) {
   const int64_t groups = rows * (K / 8);
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  pdl_wait();  // launched dependent: x may be the previous kernel's output
+  pdl_launch_dependents();
   float part = 0.f;
   if (gid < groups) {
     const uint4 v = reinterpret_cast<const uint4*>(x)[gid];
@@ -423,6 +425,9 @@ __global__ void __launch_bounds__(QD_WARPS * 32, (qd_min_blocks<BITS, GATED, NGM
 qmoe_decode_kernel(const QDecodeArgs a) {
   extern __shared__ __align__(128) uint8_t s_ring[];  // one ring per warp
   uint8_t* ring = s_ring + (threadIdx.x >> 5) * ring_bytes<BITS, GATED>();
+  // Launched dependent: every input (offsets, activations) comes from earlier kernels.
+  pdl_wait();
+  pdl_launch_dependents();
   // Grid rows cover the experts that can hold rows (min(E, routed rows)): row j takes the
   // j-th expert with rows, found from the offsets.
   int e = blockIdx.y;
@@ -506,6 +511,8 @@ __global__ void __launch_bounds__(256)
 finalize_fc1_kernel(const QDecodeArgs a, __half* __restrict__ act) {
   const int64_t r = blockIdx.y;
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();  // launched dependent: the partial sums come from the previous kernel
+  pdl_launch_dependents();
   if (n >= a.N) return;
   const int e = expert_of(a.offsets, a.E, r);
   const int64_t bi = e * a.bias_e_stride + static_cast<int64_t>(n) * a.bias_stride;
@@ -546,6 +553,8 @@ combine_partials_kernel(const float* __restrict__ part, int splits, int64_t rows
                         const __half* __restrict__ bias, __half* __restrict__ out) {
   const int t = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();  // launched dependent: the partial sums come from the previous kernel
+  pdl_launch_dependents();
   if (c >= H) return;
   float acc = 0.f;
   for (int j = 0; j < k; ++j) {
@@ -581,8 +590,8 @@ cudaError_t launch_decode_n(const QDecodeArgs& a, cudaStream_t s) {
   // At most min(E, routed rows) experts hold rows: CTAs for the others would exit at once.
   const int ey = static_cast<int>(std::min<int64_t>(a.E, std::max<int64_t>(a.rows, 1)));
   const dim3 grid((a.N + QD_WARPS * 16 - 1) / (QD_WARPS * 16), ey, a.splits);
-  qmoe_decode_kernel<BITS, GATED, kScale, RAW4, NGMAX><<<grid, QD_WARPS * 32, kSmem, s>>>(a);
-  return cudaGetLastError();
+  return launch_dependent(qmoe_decode_kernel<BITS, GATED, kScale, RAW4, NGMAX>, grid,
+                          dim3(QD_WARPS * 32), kSmem, s, a);
 }
 
 // An expert holds at most all routed rows: groups of 8 per pass up to min(4, ceil(rows / 8)).
@@ -628,16 +637,14 @@ cudaError_t launch_qdec_prep(const __half* x, int64_t rows, int K, __half* xp, f
                              cudaStream_t s) {
   const int64_t groups = rows * (K / 8);
   if (groups == 0) return cudaSuccess;
-  qdec_prep_kernel<<<static_cast<unsigned>((groups + 255) / 256), 256, 0, s>>>(x, rows, K, xp,
-                                                                                 corr);
-  return cudaGetLastError();
+  return launch_dependent(qdec_prep_kernel, dim3(static_cast<unsigned>((groups + 255) / 256)),
+                          dim3(256), 0, s, x, rows, K, xp, corr);
 }
 
 cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s) {
   if (a.rows == 0) return cudaSuccess;
   const dim3 grid((a.N + 255) / 256, static_cast<unsigned>(a.rows));
-  finalize_fc1_kernel<<<grid, 256, 0, s>>>(a, act);
-  return cudaGetLastError();
+  return launch_dependent(finalize_fc1_kernel, grid, dim3(256), 0, s, a, act);
 }
 
 cudaError_t launch_combine_partials(const float* part, int splits, int64_t rows, const int32_t* pos,
@@ -645,10 +652,9 @@ cudaError_t launch_combine_partials(const float* part, int splits, int64_t rows,
                                     int E, const void* bias, void* out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   const dim3 grid((H + 255) / 256, T);
-  combine_partials_kernel<<<grid, 256, 0, s>>>(part, splits, rows, pos, w, k, H, offsets, E,
-                                               static_cast<const __half*>(bias),
-                                               static_cast<__half*>(out));
-  return cudaGetLastError();
+  return launch_dependent(combine_partials_kernel, grid, dim3(256), 0, s, part, splits, rows, pos,
+                          w, k, H, offsets, E, static_cast<const __half*>(bias),
+                          static_cast<__half*>(out));
 }
 
 }  // namespace moe
