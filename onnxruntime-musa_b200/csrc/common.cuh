@@ -27,14 +27,19 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// True unless MOE_B200_PDL=0 (host side; read once).
+// Host side, read once.  Decode chain (QMoE weight streaming): on unless MOE_B200_PDL=0.
+// Layer chain (planning, gather, GEMMs, combine): off unless MOE_B200_PDL_LAYER=1.  On
+// B200 the layer chain gained 6% of device time at C1 (0.114 -> 0.107 ms) but lost 21% of
+// end-to-end throughput through the host-buffer pipeline (2.39 -> 1.89 M tokens/s), whose
+// submission rate bounds calls that small; C2 and C4 did not move.
 bool pdl_enabled();
+bool pdl_layer_enabled();
 
-// Launches kernel<<<grid, block, smem, s>>>(args...) with programmatic stream
-// serialisation when pdl_enabled(): the kernel must follow the pdl_wait() rule above.
+// Launches kernel<<<grid, block, smem, s>>>(args...), with programmatic stream
+// serialisation when `pdl`: the kernel must follow the pdl_wait() rule above.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                             cudaStream_t s, Args&&... args) {
+cudaError_t launch_dependent(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                             size_t smem, cudaStream_t s, Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -42,7 +47,7 @@ cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);

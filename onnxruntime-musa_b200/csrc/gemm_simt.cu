@@ -28,6 +28,8 @@ __device__ __forceinline__ float bias_at(const void* bias, int e, int n, const G
 
 template <typename T, bool kGated>
 __global__ void __launch_bounds__(SB_THREADS) simt_gemm_kernel(const GemmArgs g) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   constexpr int NB = kGated ? 2 : 1;
   __shared__ __align__(16) float As[SB_K][SB_M + 4];
   __shared__ __align__(16) float Bs[NB][SB_K][SB_N + 4];
@@ -148,6 +150,8 @@ __device__ __forceinline__ float4 lds4(const T* p) {
 
 template <typename T, bool kGated>
 __global__ void __launch_bounds__(SB_THREADS) simt_gemm_pipe_kernel(const GemmArgs g) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   constexpr int NB = kGated ? 2 : 1;
   constexpr int P = pitch<T>();
   constexpr int VEC = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte piece
@@ -280,17 +284,11 @@ cudaError_t launch_t(const GemmArgs& g, cudaStream_t s) {
       if (st != cudaSuccess) return st;
       attr_set[g.gated] = true;
     }
-    if (g.gated)
-      simt_gemm_pipe_kernel<T, true><<<grid, SB_THREADS, smem, s>>>(g);
-    else
-      simt_gemm_pipe_kernel<T, false><<<grid, SB_THREADS, smem, s>>>(g);
-    return cudaGetLastError();
+    return g.gated ? launch_dependent(pdl_layer_enabled(), simt_gemm_pipe_kernel<T, true>, grid, dim3(SB_THREADS), smem, s, g)
+                   : launch_dependent(pdl_layer_enabled(), simt_gemm_pipe_kernel<T, false>, grid, dim3(SB_THREADS), smem, s, g);
   }
-  if (g.gated)
-    simt_gemm_kernel<T, true><<<grid, SB_THREADS, 0, s>>>(g);
-  else
-    simt_gemm_kernel<T, false><<<grid, SB_THREADS, 0, s>>>(g);
-  return cudaGetLastError();
+  return g.gated ? launch_dependent(pdl_layer_enabled(), simt_gemm_kernel<T, true>, grid, dim3(SB_THREADS), 0, s, g)
+                 : launch_dependent(pdl_layer_enabled(), simt_gemm_kernel<T, false>, grid, dim3(SB_THREADS), 0, s, g);
 }
 
 }  // namespace

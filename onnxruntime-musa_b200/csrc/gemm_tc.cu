@@ -308,6 +308,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b1,
                        const __grid_constant__ CUtensorMap map_b3, const TcParams p) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -633,6 +635,8 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                             const __grid_constant__ CUtensorMap map_a_sw,
                             const __grid_constant__ CUtensorMap map_b1_sw,
                             const __grid_constant__ CUtensorMap map_b3_sw, const TcParams p) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1003,6 +1007,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Q_THREADS, 1)
 tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_q1,
                      const __grid_constant__ CUtensorMap map_q3, const TcParams p) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   constexpr int PB = q_packed_bytes<BITS>();
   constexpr int ROW_BYTES = BK * BITS / 8;  // packed bytes of one B row per k-block
   extern __shared__ uint8_t smem_raw[];
@@ -1446,12 +1452,16 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   const int64_t ub = ((g.rows + rows_per_tile - 1) / rows_per_tile + g.E) * p.n_tiles;
   if (pair) {
     const int64_t pairs = std::min<int64_t>(ub, num_sms / 2);
-    tc_pair_grouped_gemm_kernel<T><<<static_cast<int>(2 * pairs), THREADS, P_SMEM_BYTES, s>>>(
-        ma, mb1, mb3, ma_sw, mb1_sw, mb3_sw, p);
+    cudaError_t st = launch_dependent(pdl_layer_enabled(), tc_pair_grouped_gemm_kernel<T>,
+                                      dim3(static_cast<unsigned>(2 * pairs)), dim3(THREADS),
+                                      P_SMEM_BYTES, s, ma, mb1, mb3, ma_sw, mb1_sw, mb3_sw, p);
+    if (st != cudaSuccess) return st;
     if (p.trace) dump_trace(trace_path, g.K, s);
   } else {
     const int grid = static_cast<int>(std::min<int64_t>(ub, num_sms));
-    tc_grouped_gemm_kernel<T><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb1, mb3, p);
+    cudaError_t st = launch_dependent(pdl_layer_enabled(), tc_grouped_gemm_kernel<T>, dim3(grid), dim3(THREADS),
+                                      SMEM_BYTES, s, ma, mb1, mb3, p);
+    if (st != cudaSuccess) return st;
   }
   return cudaGetLastError();
 }
@@ -1527,9 +1537,8 @@ cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   }
   const int64_t ub = ((g.rows + P_BM - 1) / P_BM + g.E) * p.n_tiles;
   const int64_t pairs = std::min<int64_t>(ub, num_sms / 2);
-  tc_pair_qgemm_kernel<BITS, QEPI><<<static_cast<int>(2 * pairs), Q_THREADS, q_smem_bytes<BITS>(), s>>>(
-      ma, mq1, mq3, p);
-  return cudaGetLastError();
+  return launch_dependent(pdl_layer_enabled(), tc_pair_qgemm_kernel<BITS, QEPI>, dim3(static_cast<unsigned>(2 * pairs)),
+                          dim3(Q_THREADS), q_smem_bytes<BITS>(), s, ma, mq1, mq3, p);
 }
 
 }  // namespace

@@ -43,6 +43,14 @@ bool moe::pdl_enabled() {
   return on;
 }
 
+bool moe::pdl_layer_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_B200_PDL_LAYER");
+    return v != nullptr && std::strcmp(v, "0") != 0 && v[0] != '\0';
+  }();
+  return on;
+}
+
 int moe::set_error(int code, const char* fmt, ...) {
   char buf[1024];
   va_list ap;

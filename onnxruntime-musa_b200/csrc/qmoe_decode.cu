@@ -590,7 +590,7 @@ cudaError_t launch_decode_n(const QDecodeArgs& a, cudaStream_t s) {
   // At most min(E, routed rows) experts hold rows: CTAs for the others would exit at once.
   const int ey = static_cast<int>(std::min<int64_t>(a.E, std::max<int64_t>(a.rows, 1)));
   const dim3 grid((a.N + QD_WARPS * 16 - 1) / (QD_WARPS * 16), ey, a.splits);
-  return launch_dependent(qmoe_decode_kernel<BITS, GATED, kScale, RAW4, NGMAX>, grid,
+  return launch_dependent(pdl_enabled(), qmoe_decode_kernel<BITS, GATED, kScale, RAW4, NGMAX>, grid,
                           dim3(QD_WARPS * 32), kSmem, s, a);
 }
 
@@ -637,14 +637,14 @@ cudaError_t launch_qdec_prep(const __half* x, int64_t rows, int K, __half* xp, f
                              cudaStream_t s) {
   const int64_t groups = rows * (K / 8);
   if (groups == 0) return cudaSuccess;
-  return launch_dependent(qdec_prep_kernel, dim3(static_cast<unsigned>((groups + 255) / 256)),
+  return launch_dependent(pdl_enabled(), qdec_prep_kernel, dim3(static_cast<unsigned>((groups + 255) / 256)),
                           dim3(256), 0, s, x, rows, K, xp, corr);
 }
 
 cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s) {
   if (a.rows == 0) return cudaSuccess;
   const dim3 grid((a.N + 255) / 256, static_cast<unsigned>(a.rows));
-  return launch_dependent(finalize_fc1_kernel, grid, dim3(256), 0, s, a, act);
+  return launch_dependent(pdl_enabled(), finalize_fc1_kernel, grid, dim3(256), 0, s, a, act);
 }
 
 cudaError_t launch_combine_partials(const float* part, int splits, int64_t rows, const int32_t* pos,
@@ -652,7 +652,7 @@ cudaError_t launch_combine_partials(const float* part, int splits, int64_t rows,
                                     int E, const void* bias, void* out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   const dim3 grid((H + 255) / 256, T);
-  return launch_dependent(combine_partials_kernel, grid, dim3(256), 0, s, part, splits, rows, pos,
+  return launch_dependent(pdl_enabled(), combine_partials_kernel, grid, dim3(256), 0, s, part, splits, rows, pos,
                           w, k, H, offsets, E, static_cast<const __half*>(bias),
                           static_cast<__half*>(out));
 }

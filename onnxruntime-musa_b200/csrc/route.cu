@@ -236,6 +236,8 @@ scan_kernel(const int32_t* __restrict__ chunk_counts, int num_chunks, int E,
             int32_t* __restrict__ chunk_base, int32_t* __restrict__ expert_offsets,
             int32_t* __restrict__ tiles128, int32_t* __restrict__ tiles64,
             int32_t* __restrict__ tiles256) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   extern __shared__ int32_t s_cnt[];  // [E]
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int32_t run = 0;
@@ -277,6 +279,8 @@ permute_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, int 
                const int32_t* __restrict__ expert_offsets,
                const int32_t* __restrict__ chunk_base, int32_t* __restrict__ permuted_pos,
                int32_t* __restrict__ permuted_src, int chunk) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   extern __shared__ int32_t smem[];
   constexpr int kWarps = kRouteThreads / 32;
   int32_t* s_warp = smem;               // [kWarps][E]
@@ -329,6 +333,8 @@ __global__ void __launch_bounds__(256)
 gather_rows_kernel(const uint8_t* __restrict__ x, int64_t row_bytes, int k,
                    const int32_t* __restrict__ permuted_src, int64_t num_perm_rows,
                    uint8_t* __restrict__ xp) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t p = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (p >= num_perm_rows) return;
@@ -351,6 +357,8 @@ __global__ void __launch_bounds__(256)
 combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ permuted_pos,
                const float* __restrict__ route_w, int num_rows, int k, int H,
                T* __restrict__ out) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   const int t = blockIdx.x;
   if (t >= num_rows) return;
   const int32_t* pos = permuted_pos + static_cast<int64_t>(t) * k;
@@ -393,6 +401,8 @@ __global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n,
 // One warp per row: fp32 sum of an fp16 row, lanes over 16-byte pieces, fixed butterfly.
 __global__ void __launch_bounds__(256)
 row_sums_kernel(const __half* __restrict__ a, int64_t rows, int K, float* __restrict__ out) {
+  pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
+  pdl_launch_dependents();
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -415,9 +425,8 @@ row_sums_kernel(const __half* __restrict__ a, int64_t rows, int K, float* __rest
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_row_sums(const void* a, int64_t rows, int K, float* out, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
-  row_sums_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(
+  return launch_dependent(pdl_layer_enabled(), row_sums_kernel, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0, s,
       static_cast<const __half*>(a), rows, K, out);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t s, int* clear) {
@@ -500,23 +509,22 @@ cudaError_t launch_plan(const int32_t* idx, int T_, int k, int E, const int32_t*
                         int32_t* tiles64, int32_t* tiles256, int32_t* pos, int32_t* src,
                         cudaStream_t s, int chunk) {
   const int chunks = num_route_chunks(T_, chunk);
-  scan_kernel<<<1, 1024, E * sizeof(int32_t), s>>>(chunk_counts, chunks, E, chunk_base,
-                                                   offsets, tiles128, tiles64, tiles256);
-  cudaError_t st = cudaGetLastError();
+  cudaError_t st = launch_dependent(pdl_layer_enabled(), scan_kernel, dim3(1), dim3(1024), E * sizeof(int32_t), s,
+                                    chunk_counts, chunks, E, chunk_base, offsets, tiles128,
+                                    tiles64, tiles256);
   if (st != cudaSuccess || T_ == 0) return st;
   const size_t sm = (static_cast<size_t>(kRouteThreads / 32) + 2) * E * sizeof(int32_t);
-  permute_kernel<<<chunks, kRouteThreads, sm, s>>>(idx, T_, k, E, offsets, chunk_base, pos, src,
-                                                   chunk);
-  return cudaGetLastError();
+  return launch_dependent(pdl_layer_enabled(), permute_kernel, dim3(chunks), dim3(kRouteThreads), sm, s, idx, T_, k, E,
+                          offsets, chunk_base, pos, src, chunk);
 }
 
 cudaError_t launch_gather(const void* x, int64_t row_bytes, int k, const int32_t* src,
                           int64_t rows, void* xp, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   const int64_t blocks = (rows + 7) / 8;
-  gather_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-      static_cast<const uint8_t*>(x), row_bytes, k, src, rows, static_cast<uint8_t*>(xp));
-  return cudaGetLastError();
+  return launch_dependent(pdl_layer_enabled(), gather_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
+                          static_cast<const uint8_t*>(x), row_bytes, k, src, rows,
+                          static_cast<uint8_t*>(xp));
 }
 
 cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const float* w,
@@ -524,21 +532,19 @@ cudaError_t launch_combine(int dtype, const void* y, const int32_t* pos, const f
   if (T_ == 0) return cudaSuccess;
   switch (dtype) {
     case kDtF32:
-      combine_kernel<float><<<T_, 256, 0, s>>>(static_cast<const float*>(y), pos, w, T_, k, H,
-                                               static_cast<float*>(out));
-      break;
+      return launch_dependent(pdl_layer_enabled(), combine_kernel<float>, dim3(T_), dim3(256), 0, s,
+                              static_cast<const float*>(y), pos, w, T_, k, H,
+                              static_cast<float*>(out));
     case kDtF16:
-      combine_kernel<__half><<<T_, 256, 0, s>>>(static_cast<const __half*>(y), pos, w, T_, k, H,
-                                                static_cast<__half*>(out));
-      break;
+      return launch_dependent(pdl_layer_enabled(), combine_kernel<__half>, dim3(T_), dim3(256), 0, s,
+                              static_cast<const __half*>(y), pos, w, T_, k, H,
+                              static_cast<__half*>(out));
     case kDtBF16:
-      combine_kernel<__nv_bfloat16><<<T_, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(y), pos,
-                                                       w, T_, k, H,
-                                                       static_cast<__nv_bfloat16*>(out));
-      break;
+      return launch_dependent(pdl_layer_enabled(), combine_kernel<__nv_bfloat16>, dim3(T_), dim3(256), 0, s,
+                              static_cast<const __nv_bfloat16*>(y), pos, w, T_, k, H,
+                              static_cast<__nv_bfloat16*>(out));
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace moe
