@@ -334,14 +334,14 @@ def bench_ours(args, cfg, rank, world, dev):
     prob, tens, inputs, op_attrs, op_type = problem_and_tensors(pkg, cfg, L, out)
     # --prepack (QMoE): weights dequantised once before timing (moe_b200_prepack_create);
     # prefill-sized calls then run the fp16 GEMMs on them.
-    pk = pkg.Prepacked(prob, tens) if (args.prepack and cfg["kind"] == "qmoe") else None
-    ws = torch.empty(pkg.workspace_size(prob, pk), dtype=torch.uint8, device=dev)
+    wpk = pkg.Prepacked(prob, tens) if (args.prepack and cfg["kind"] == "qmoe") else None
+    ws = torch.empty(pkg.workspace_size(prob, wpk), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def fwd(events=None):
-        if pk is None and events is None:
+        if wpk is None and events is None:
             return pkg.forward(prob, tens, ws, stream)
-        return pkg.forward(prob, tens, ws, stream, prepacked=pk, events=events)
+        return pkg.forward(prob, tens, ws, stream, prepacked=wpk, events=events)
 
     def barrier():
         if world > 1:
@@ -424,7 +424,7 @@ def bench_ours(args, cfg, rank, world, dev):
     hout = torch.empty_like(hx).pin_memory()
     dx, dl = torch.empty_like(L["x"]), torch.empty_like(L["router_probs"])
     e2e_inputs = [dx, dl] + inputs[2:]
-    if pk is not None:
+    if wpk is not None:
         op.prepack(e2e_inputs)
 
     def e2e_step():
@@ -441,8 +441,8 @@ def bench_ours(args, cfg, rank, world, dev):
     # neighbouring steps overlap this step's compute.  Wall clock from the first submit
     # to the completion of the last D2H, max over ranks.
     with pkg.Pipeline(prob, tens, depth=2) as pl:
-        if pk is not None:
-            pl.set_prepacked(pk)
+        if wpk is not None:
+            pl.set_prepacked(wpk)
         for _ in range(args.warmup):
             pl.submit(hx, hl, hout)
         pl.synchronize()
@@ -476,7 +476,7 @@ def bench_ours(args, cfg, rank, world, dev):
                 "experts_touched": alg["touched"],
                 "layer_frac": round((alg["bytes"] / pk["hbm"] / 1e9) / (ms / 1e3), 4)}
     else:
-        prepacked = pk is not None and not decode and T * cfg["k"] >= int(
+        prepacked = wpk is not None and not decode and T * cfg["k"] >= int(
             os.environ.get("MOE_B200_PREPACK_MIN_ROWS", PREPACK_MIN_ROWS))
         fused_q = (cfg["kind"] == "qmoe" and not prepacked
                    and T * cfg["k"] <= QMOE_FUSED_MAX_ROWS)
@@ -522,7 +522,7 @@ def bench_ours(args, cfg, rank, world, dev):
                    "l2": "inputs larger than L2 (weights streamed every step)"
                          if alg["bytes"] > 126e6 else "inputs smaller than L2 (not flushed)",
                    **({"weights": "prepacked: dequantised once before timing "
-                                  "(moe_b200_prepack_create)"} if pk is not None else {})},
+                                  "(moe_b200_prepack_create)"} if wpk is not None else {})},
         "e2e": e2e, "roofline": roof,
         "stage_ms": {s: round(v, 4) for s, v in stage_ms.items()},
         "adjacent_ops": adjacent,
