@@ -94,18 +94,57 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clocks and throttle reasons during the timed region: NVML queries from a thread
+    every 2 ms (read-only), else nvidia-smi sampling.  The NVML handle is found by the CUDA
+    device's PCI address, so it is the GPU being timed whatever the index order."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h): SwPowerCap, HwSlowdown, SwThermal, HwThermal.
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.rows = []
+        self.rows = []      # nvidia-smi rows
+        self.samples = []   # NVML: (sm_mhz, max_mhz, reasons bitmask)
+        self._stop = None
+        self._thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.index)
+        try:
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx,
+                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.002)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+            return self
+        except Exception:
+            self._thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
@@ -116,6 +155,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -127,6 +169,10 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
+        for clk, m, bits in self.samples:
+            sm.append(float(clk))
+            mx = max(mx, float(m))
+            reasons.update(n for n, b in self.BITS.items() if bits & b)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in self.rows:
             try:
@@ -138,7 +184,8 @@ class ClockSampler:
             except (ValueError, IndexError):
                 continue
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.samples else ("nvidia-smi" if self.rows else None)}
 
 
 # ----------------------------------------------------------------- synthetic layer
