@@ -71,4 +71,10 @@ if __name__ == "__main__":
               mu=-5.0, sigma=0.3)
     qmoe_case("qmoe_int8_rowscale", 16, T=10, H=64, I=128, E=4, k=2, bits=8, block=0,
               mu=-6.0, sigma=0.25)
+    # Decode-sized QMoE (T*k <= 512, H and I multiples of 128): the weight-streaming
+    # kernels, int4 with 128-wide blocks (biased codes) and int8 with per-row scales.
+    qmoe_case("qmoe_int4_block128_decode", 18, T=3, H=256, I=128, E=8, k=2, bits=4, block=128,
+              mu=-5.0, sigma=0.3)
+    qmoe_case("qmoe_int8_rowscale_decode", 19, T=5, H=128, I=256, E=4, k=2, bits=8, block=0,
+              mu=-6.0, sigma=0.25)
     print("fixtures:", sorted(p.name for p in HERE.glob("*.npz")))
