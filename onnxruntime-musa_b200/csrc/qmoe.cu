@@ -234,7 +234,7 @@ int qmoe_decode_fc1(const moe_b200_problem& p, const moe_b200_tensors& t, const 
     const Raw4Ws w = raw4_ws(p);
     auto* xp = reinterpret_cast<__half*>(ws + w.xp1);
     auto* corr = reinterpret_cast<float*>(ws + w.c1);
-    cudaError_t st = launch_qdec_prep(a.x, p.num_rows, a.K, xp, corr, s);
+    cudaError_t st = launch_qdec_prep(a.x, p.num_rows, a.K, xp, corr, false, s);
     if (st != cudaSuccess)
       return set_error(MOE_B200_EP_FAIL, "QMoE fc1 activation prep: %s", cudaGetErrorString(st));
     a.x = xp;
@@ -281,7 +281,7 @@ int qmoe_decode_fc2(const moe_b200_problem& p, const moe_b200_tensors& t, const 
     const Raw4Ws w = raw4_ws(p);
     auto* xp = reinterpret_cast<__half*>(ws + w.xp2);
     auto* corr = reinterpret_cast<float*>(ws + w.c2);
-    cudaError_t st = launch_qdec_prep(b.x, R, b.K, xp, corr, s);
+    cudaError_t st = launch_qdec_prep(b.x, R, b.K, xp, corr, true, s);
     if (st != cudaSuccess)
       return set_error(MOE_B200_EP_FAIL, "QMoE fc2 activation prep: %s", cudaGetErrorString(st));
     b.x = xp;

@@ -384,11 +384,16 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
 // chunk's offset term with a fixed butterfly (deterministic).
 __global__ void __launch_bounds__(256)
 qdec_prep_kernel(const __half* __restrict__ x, int64_t rows, int K, __half* __restrict__ xp,
-                 float* __restrict__ corr) {
+                 float* __restrict__ corr, int x_from_previous) {
   const int64_t groups = rows * (K / 8);
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  pdl_wait();  // launched dependent: x may be the previous kernel's output
-  pdl_launch_dependents();
+  // Launched dependent.  x_from_previous: x is the previous kernel's output, so wait first;
+  // else x predates the layer call (its routing kernel started after every earlier kernel
+  // finished) and only the exit has to wait.
+  if (x_from_previous) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
   float part = 0.f;
   if (gid < groups) {
     const uint4 v = reinterpret_cast<const uint4*>(x)[gid];
@@ -407,6 +412,10 @@ qdec_prep_kernel(const __half* __restrict__ x, int64_t rows, int K, __half* __re
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   if (gid < groups && (gid & 15) == 0) corr[gid >> 4] = part;
+  if (!x_from_previous) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
 }
 
 template <int BITS, bool GATED>
@@ -634,11 +643,11 @@ cudaError_t launch_qmoe_decode(const QDecodeArgs& a, int max_experts_touched, cu
 }
 
 cudaError_t launch_qdec_prep(const __half* x, int64_t rows, int K, __half* xp, float* corr,
-                             cudaStream_t s) {
+                             bool x_from_previous, cudaStream_t s) {
   const int64_t groups = rows * (K / 8);
   if (groups == 0) return cudaSuccess;
   return launch_dependent(pdl_enabled(), qdec_prep_kernel, dim3(static_cast<unsigned>((groups + 255) / 256)),
-                          dim3(256), 0, s, x, rows, K, xp, corr);
+                          dim3(256), 0, s, x, rows, K, xp, corr, x_from_previous ? 1 : 0);
 }
 
 cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s) {

@@ -54,8 +54,10 @@ bool qmoe_decode_supported(int dtype, int bits, int block_size, int64_t H, int64
 // x0..x7, stored as (x0,x4)(x1/16,x5/16)(x2,x6)(x3/16,x7/16): the mma.sync B fragments of
 // the decode kernel's k order, odd slots scaled to match the in-place high nibbles) and
 // corr [rows, K/128] = per 128-wide chunk, 1032 * sum(even slots) + 1152 * sum(odd, scaled).
+// x_from_previous: x is written by the kernel launched just before (the fc1 activations);
+// false when x is the layer input, so the prep overlaps the routing kernel.
 cudaError_t launch_qdec_prep(const __half* x, int64_t rows, int K, __half* xp, float* corr,
-                             cudaStream_t s);
+                             bool x_from_previous, cudaStream_t s);
 cudaError_t launch_qmoe_decode(const QDecodeArgs& a, int max_experts_touched, cudaStream_t s);
 // act = activation(sum of fc1 partials + bias), fp16 [rows, N].
 cudaError_t launch_finalize_fc1(const QDecodeArgs& a, __half* act, cudaStream_t s);

@@ -165,6 +165,9 @@ small_dispatch_kernel(const T* __restrict__ logits, int num_rows, int E, int k, 
                       int32_t* __restrict__ expert_idx, float* __restrict__ route_w,
                       int32_t* __restrict__ expert_offsets, int32_t* __restrict__ permuted_pos,
                       int32_t* __restrict__ permuted_src, int* __restrict__ clear) {
+  // The decode chain's next kernel (the activation prep) reads only the layer input, so it
+  // may start now (it waits for this kernel before it exits).
+  pdl_launch_dependents();
   __shared__ int32_t s_idx[kSmallDispatchRows];
   if (clear != nullptr && threadIdx.x < kClearWords) clear[threadIdx.x] = 0;
   __shared__ int32_t s_cnt[kMaxExperts + 1];
