@@ -381,7 +381,9 @@ int moe_b200_forward_prepacked(const moe_b200_problem* problem, const moe_b200_t
                                int32_t num_events);
 /* Kernel-object pre-pack: inputs[] in the QMoE schema order (input and router_probs may
  * be absent); the kernel keeps a reference and later computes whose weight inputs are the
- * same device pointers use it.  *is_packed is set to 0 (see above). */
+ * same device pointers use it.  *is_packed is set to 0 (see above).  Call it before the
+ * kernel's first compute, as ORT runs PrePack at session initialisation: it must not run
+ * concurrently with a compute of the same kernel.  For an MoE kernel it packs nothing. */
 int moe_b200_kernel_prepack(moe_b200_kernel* kernel, int32_t num_inputs,
                             const moe_b200_tensor_ref* inputs, int32_t share, void* stream,
                             int32_t* is_packed);
