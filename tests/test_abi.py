@@ -194,3 +194,50 @@ def test_prepack_entries_validate_before_touching_the_device(pkg):
         assert L.moe_b200_kernel_prepack(op._h, 11, refs, 0, None, None) == pkg.INVALID_ARGUMENT
     finally:
         op.release()
+
+
+C_CONSUMER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "moe_b200.h"
+
+int main(void) {
+  if (moe_b200_abi_version() != MOE_B200_ABI_VERSION) return 10;
+  moe_b200_problem p;
+  memset(&p, 0, sizeof(p));
+  p.num_rows = 16; p.hidden_size = 64; p.inter_size = 64; p.num_experts = 8;
+  p.dtype = MOE_B200_FLOAT16; p.attrs.k = 2; p.attrs.activation_type = MOE_B200_ACT_SILU;
+  p.attrs.swiglu_limit = 1e30f; p.attrs.activation_alpha = 1.0f;
+  size_t ws = 0;
+  if (moe_b200_workspace_size(&p, &ws) != MOE_B200_OK || ws == 0) return 11;
+  p.attrs.k = 9;  /* more experts per token than experts */
+  if (moe_b200_workspace_size(&p, &ws) != MOE_B200_INVALID_ARGUMENT) return 12;
+  if (strlen(moe_b200_last_error()) == 0) return 13;
+  moe_b200_prepacked* pk = NULL;
+  moe_b200_tensors t;
+  memset(&t, 0, sizeof(t));
+  p.attrs.k = 2;
+  if (moe_b200_prepack_create(&p, &t, 0, NULL, &pk) != MOE_B200_INVALID_ARGUMENT) return 14;
+  printf("ok %zu\n", ws);
+  return 0;
+}
+"""
+
+
+def test_header_is_plain_c_and_links(pkg, tmp_path):
+    """A C99 program includes the header, links the library and calls host-only entries
+    (the binding a cgo / FFI consumer would make)."""
+    import shutil
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "consumer.c"
+    src.write_text(C_CONSUMER)
+    lib = pathlib.Path(pkg.get_library_path())
+    exe = tmp_path / "consumer"
+    inc = pathlib.Path(__file__).resolve().parents[1] / "include"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-pedantic", f"-I{inc}", str(src),
+                    "-o", str(exe), str(lib), f"-Wl,-rpath,{lib.parent}"], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    assert r.stdout.startswith("ok ")
