@@ -974,8 +974,9 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__
 
 // 8 codes (one 16-byte output chunk, natural order) -> fp16: (q - zp) * s (QEPI 0),
 // q - zp (QEPI 1, scale applied in the epilogue) or the biased code 1024 + q (QEPI 2).
+// w: the 8 codes (int8: both words; int4: w.x only).
 template <int BITS, int QEPI>
-__device__ __forceinline__ uint4 convert8(const uint8_t* codes, __half2 s2) {
+__device__ __forceinline__ uint4 convert8(uint2 w, __half2 s2) {
   uint4 o;
   uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
   auto fin = [&](uint32_t biased, __half2 zp) -> uint32_t {
@@ -984,18 +985,16 @@ __device__ __forceinline__ uint4 convert8(const uint8_t* codes, __half2 s2) {
     return h2u(QEPI == 1 ? d : __hmul2(d, s2));
   };
   if (BITS == 8) {
-    const uint2 w = *reinterpret_cast<const uint2*>(codes);
     const __half2 zp = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
     ow[0] = fin(__byte_perm(w.x, 0x64646464u, 0x4140u), zp);
     ow[1] = fin(__byte_perm(w.x, 0x64646464u, 0x4342u), zp);
     ow[2] = fin(__byte_perm(w.y, 0x64646464u, 0x4140u), zp);
     ow[3] = fin(__byte_perm(w.y, 0x64646464u, 0x4342u), zp);
   } else {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(codes);
     const __half2 zp = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t b = (w >> (8 * i)) & 0xFFu;
+      const uint32_t b = (w.x >> (8 * i)) & 0xFFu;
       ow[i] = fin((b & 0xFu) | ((b & 0xF0u) << 12) | 0x64006400u, zp);
     }
   }
@@ -1228,17 +1227,26 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
           const int r = r0 + j * kThreadsPerGroup;
           const uint8_t* prow = sP + sp * PB + r * ROW_BYTES;
           uint8_t* brow_s = sB + sb * B_HALF + r * 128;
+          // One 16-byte load per swizzled chunk of the packed row (16 int8 or 32 int4
+          // codes; the eight rows of a load phase hit eight distinct 16-byte bank groups),
+          // then 8 codes per 16-byte store of the B tile.
+          constexpr int kPerLoad = 16 / BITS;  // chunks of 8 codes per 16-byte load
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {  // chunks of 8 codes
-            const int byte_off = c * BITS;     // byte offset of code 8c in the packed row
-            const int chunk = byte_off >> 4;
-            const int phys = BITS == 8 ? (chunk ^ ((r >> 1) & 3)) : (chunk ^ ((r >> 2) & 1));
-            const uint8_t* codes = prow + phys * 16 + (byte_off & 15);
-            const __half2 s2 =
-                p.qblock ? __half2half2(srs[j][min(kb * BK + 8 * c, p.K - 1) / p.qblock])
-                         : row_scale[j];
-            const uint4 o = convert8<BITS, QEPI>(codes, s2);
-            *reinterpret_cast<uint4*>(brow_s + ((c ^ (r & 7)) * 16)) = o;
+          for (int m = 0; m < 8 / kPerLoad; ++m) {
+            const int phys = BITS == 8 ? (m ^ ((r >> 1) & 3)) : (m ^ ((r >> 2) & 1));
+            const uint4 w16 = *reinterpret_cast<const uint4*>(prow + phys * 16);
+            const uint32_t ww[4] = {w16.x, w16.y, w16.z, w16.w};
+#pragma unroll
+            for (int u = 0; u < kPerLoad; ++u) {
+              const int c = m * kPerLoad + u;  // chunk of 8 codes
+              const uint2 w = BITS == 8 ? make_uint2(ww[2 * u], ww[2 * u + 1])
+                                        : make_uint2(ww[u], 0u);
+              const __half2 s2 =
+                  p.qblock ? __half2half2(srs[j][min(kb * BK + 8 * c, p.K - 1) / p.qblock])
+                           : row_scale[j];
+              const uint4 o = convert8<BITS, QEPI>(w, s2);
+              *reinterpret_cast<uint4*>(brow_s + ((c ^ (r & 7)) * 16)) = o;
+            }
           }
         }
         fence_proxy_async_smem();
