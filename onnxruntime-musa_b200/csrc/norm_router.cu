@@ -144,20 +144,25 @@ norm_router_kernel(const T* __restrict__ x, const T* __restrict__ skip,
   }
 }
 
-// 16-bit types: a CTA of 8 warps takes 16 rows.  A first pass gives each row its
-// 1/rms (warp per two rows); then K is walked in chunks of NR_KC columns: the CTA
-// normalises the chunk of its 16 rows (writing normed and residual), stages it in shared
-// memory ([16][NR_KC + 8]: 8 elements of padding make the fragment loads conflict-free)
-// and the warps run the router MatMul on it with mma.sync m16n8k16 (fp32 accumulation),
-// keeping their expert tiles' accumulators in registers across chunks.  Warp w owns
-// expert columns [8j, 8j + 8) for j = w / wpt, ...; with fewer than 8 tiles `wpt` warps
-// share a tile by splitting each chunk's k-steps and sum their partials at the end in warp
-// order (deterministic).  ~13 KB of shared memory per CTA: several CTAs per SM.
-constexpr int NR_TC_ROWS = 16;
+// 16-bit types: a CTA of 8 warps takes NR_TC_LIVE = 8 rows (more CTAs per SM than 16-row
+// CTAs; the MMA's rows 8-15 are zero).  A first pass gives each row its 1/rms (a warp per
+// row); then K is walked in chunks of NR_KC columns: every thread normalises one 16-byte
+// piece of the chunk (writing normed and residual), stages it in shared memory
+// ([16][NR_KC + 8]: 8 elements of padding make the fragment loads conflict-free), loads its
+// piece of the next chunk into registers, and the warps run the router MatMul on the staged
+// chunk with mma.sync m16n8k16 (fp32 accumulation), keeping their expert tiles'
+// accumulators in registers across chunks, so the next chunk's global loads overlap this
+// chunk's MMAs.  Warp w owns expert columns [8j, 8j + 8) for j = w / wpt, ...; with fewer
+// than 8 tiles `wpt` warps share a tile by splitting each chunk's k-steps and sum their
+// partials at the end in warp order (deterministic).  ~13 KB of shared memory per CTA.
+constexpr int NR_TC_ROWS = 16;             // MMA rows
+constexpr int NR_TC_LIVE = 8;              // rows a CTA normalises
 constexpr int NR_TC_WARPS = 8;
-constexpr int NR_KC = 256;                 // K columns per chunk
+constexpr int NR_KC = 256;                 // K columns per chunk: one 16-byte piece of one
+                                           // live row per thread
 constexpr int NR_LD = NR_KC + 8;           // padded tile row (elements)
 constexpr int NR_MAX_TPW = 4;              // expert tiles per warp (E <= 256)
+static_assert(NR_TC_LIVE * NR_KC / 8 == NR_TC_WARPS * 32, "one piece per thread per chunk");
 
 __device__ __forceinline__ void nr_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                        uint32_t b1, bool bf16) {
@@ -182,14 +187,18 @@ norm_router_tc_kernel(const T* __restrict__ x, const T* __restrict__ skip,
                       int64_t rows, int H, int E, T* __restrict__ residual_out,
                       T* __restrict__ normed, T* __restrict__ logits) {
   __shared__ __align__(16) T tile[NR_TC_ROWS * NR_LD];
-  __shared__ float s_inv[NR_TC_ROWS];
+  __shared__ float s_inv[NR_TC_LIVE];
   __shared__ float red[NR_TC_WARPS * 32 * 4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * NR_TC_ROWS;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * NR_TC_LIVE;
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
 
+  // The MMA's rows NR_TC_LIVE..15 stay zero.
+  for (int i = tid; i < (NR_TC_ROWS - NR_TC_LIVE) * NR_LD; i += NR_TC_WARPS * 32)
+    tile[NR_TC_LIVE * NR_LD + i] = from_f<T>(0.f);
+
   // 1/rms of each row.
-  for (int rr = warp; rr < NR_TC_ROWS; rr += NR_TC_WARPS) {
+  for (int rr = warp; rr < NR_TC_LIVE; rr += NR_TC_WARPS) {
     const int64_t row = row0 + rr;
     float ss = 0.f;
     if (row < rows) {
@@ -220,28 +229,39 @@ norm_router_tc_kernel(const T* __restrict__ x, const T* __restrict__ skip,
     for (int q = 0; q < 4; ++q) d[i][q] = 0.f;
   const uint32_t* tw = reinterpret_cast<const uint32_t*>(tile);
   constexpr int LDW = NR_LD / 2;
-  __syncthreads();
+
+  // This thread's piece of every chunk: live row rr, columns c0 + cc .. + 7.
+  const int rr = tid / (NR_KC / 8), cc = (tid % (NR_KC / 8)) * 8;
+  const int64_t prow = row0 + rr;
+  const bool row_ok = prow < rows;
+  const T* px = x + (row_ok ? prow : 0) * H;
+  const T* ps = skip != nullptr ? skip + (row_ok ? prow : 0) * H : nullptr;
+  float h[8];
+  auto fetch = [&](int c0) {
+    if (row_ok && c0 + cc < H) {
+      load_h<T>(px, ps, c0 + cc, h);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = 0.f;
+    }
+  };
+  fetch(0);
+  __syncthreads();  // s_inv and the zero rows
 
   for (int c0 = 0; c0 < H; c0 += NR_KC) {
     const int cw = min(NR_KC, H - c0);          // multiple of 8
     const int cwp = (cw + 15) & ~15;            // multiple of the MMA depth
-    const int pieces_per_row = cw / 8;
-    // Normalise the chunk of the 16 rows: 16-byte pieces spread over the CTA.
-    for (int pc = tid; pc < NR_TC_ROWS * pieces_per_row; pc += NR_TC_WARPS * 32) {
-      const int rr = pc / pieces_per_row, cc = (pc % pieces_per_row) * 8;
-      const int64_t row = row0 + rr;
+    if (cc < cw) {
       float n[8];
-      if (row < rows) {
-        float h[8];
-        load_h<T>(x + row * H, skip != nullptr ? skip + row * H : nullptr, c0 + cc, h);
-        if (residual_out != nullptr) store8<T>(residual_out + row * H + c0 + cc, h);
+      if (row_ok) {
+        if (residual_out != nullptr) store8<T>(residual_out + prow * H + c0 + cc, h);
         const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + c0 + cc));
         const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + c0 + cc + 4));
         const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         const float inv = s_inv[rr];
 #pragma unroll
         for (int j = 0; j < 8; ++j) n[j] = h[j] * inv * gm[j];
-        if (normed != nullptr) store8<T>(normed + row * H + c0 + cc, n);
+        if (normed != nullptr) store8<T>(normed + prow * H + c0 + cc, n);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) n[j] = 0.f;
@@ -249,9 +269,10 @@ norm_router_tc_kernel(const T* __restrict__ x, const T* __restrict__ skip,
       store8<T>(tile + rr * NR_LD + cc, n);
     }
     if (cwp != cw)  // zero the k tail of the last chunk (H % 16 == 8)
-      for (int i = tid; i < NR_TC_ROWS * 8; i += NR_TC_WARPS * 32)
+      for (int i = tid; i < NR_TC_LIVE * 8; i += NR_TC_WARPS * 32)
         tile[(i >> 3) * NR_LD + cw + (i & 7)] = from_f<T>(0.f);
     __syncthreads();
+    if (c0 + NR_KC < H) fetch(c0 + NR_KC);  // in flight during the MMAs below
 
     const int ks = cwp / 16;
     const int kper = (ks + wpt - 1) / wpt;
@@ -288,16 +309,16 @@ norm_router_tc_kernel(const T* __restrict__ x, const T* __restrict__ skip,
 #pragma unroll
       for (int q = 0; q < 4; ++q) d[0][q] += red[(w2 * 32 + lane) * 4 + q];
   }
-  // d: rows g / g + 8, expert columns 8j + 2t, + 1
+  // d: rows g / g + 8 (live rows are g < NR_TC_LIVE), expert columns 8j + 2t, + 1
 #pragma unroll
   for (int i = 0; i < NR_MAX_TPW; ++i) {
     const int j = warp / wpt + i * jstep;
     if (j >= ntile || (wpt > 1 && i > 0)) break;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int64_t row = row0 + g + (q >> 1) * 8;
-      const int ec = j * 8 + 2 * t + (q & 1);
-      if (row < rows && ec < E) logits[row * E + ec] = from_f<T>(d[i][q]);
+    for (int q = 0; q < 2; ++q) {
+      const int64_t row = row0 + g;
+      const int ec = j * 8 + 2 * t + q;
+      if (g < NR_TC_LIVE && row < rows && ec < E) logits[row * E + ec] = from_f<T>(d[i][q]);
     }
   }
 }
@@ -307,7 +328,7 @@ cudaError_t launch_t(const void* x, const void* skip, const float* gamma, float 
                      const void* wr, int64_t rows, int H, int E, void* residual_out,
                      void* normed, void* logits, cudaStream_t s) {
   if constexpr (sizeof(T) == 2) {
-    const int64_t blocks = (rows + NR_TC_ROWS - 1) / NR_TC_ROWS;
+    const int64_t blocks = (rows + NR_TC_LIVE - 1) / NR_TC_LIVE;
     norm_router_tc_kernel<T><<<static_cast<unsigned>(blocks), NR_TC_WARPS * 32, 0, s>>>(
         static_cast<const T*>(x), static_cast<const T*>(skip), gamma, eps,
         static_cast<const T*>(wr), rows, H, E, static_cast<T*>(residual_out),
