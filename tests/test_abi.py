@@ -241,3 +241,82 @@ def test_header_is_plain_c_and_links(pkg, tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
     assert r.stdout.startswith("ok ")
+
+
+def _ref(pkg, dims, et, addr=0x10000):
+    r = pkg.TensorRef()
+    r.data = addr if dims is not None else None
+    r.elem_type = et
+    if dims is not None:
+        r.rank = len(dims)
+        for i, d in enumerate(dims):
+            r.dims[i] = d
+    return r
+
+
+def _compute(pkg, op, specs, out_dims, out_et):
+    """kernel_compute with placeholder device pointers: only the host-side checks run."""
+    import ctypes
+    refs = (pkg.TensorRef * len(specs))(*[_ref(pkg, d, e) for d, e in specs])
+    o = _ref(pkg, out_dims, out_et)
+    return pkg.lib().moe_b200_kernel_compute(op._h, len(specs), refs, ctypes.byref(o), None)
+
+
+def test_kernel_compute_rejects_bad_inputs_on_the_host(pkg):
+    """Shape, type and arity checks of the kernel object, in the order the schema gives its
+    inputs, return before any CUDA call."""
+    F16, U8, I32 = pkg.FLOAT16, pkg.UINT8, pkg.INT32
+    T, H, I, E = 16, 64, 32, 8
+    moe = pkg.MoE(k=2, activation_type="silu")
+    try:
+        good = [((T, H), F16), ((T, E), F16), ((E, I, H), F16), (None, F16), ((E, H, I), F16),
+                (None, F16), ((E, I, H), F16), (None, F16)]
+
+        def bad(i, spec, out=(T, H), out_et=F16, n=None):
+            specs = list(good)
+            if i is not None:
+                specs[i] = spec
+            return _compute(pkg, moe, specs[:n] if n else specs, out, out_et)
+
+        IA, NI = pkg.INVALID_ARGUMENT, pkg.NOT_IMPLEMENTED
+        assert bad(None, None, n=4) == IA                       # fewer than 5 inputs
+        assert bad(0, ((T, H), I32)) == NI                      # input element type
+        assert bad(0, ((H,), F16)) == IA                        # input rank
+        assert bad(1, ((T + 1, E), F16)) == IA                  # router rows
+        assert bad(1, ((T, E), pkg.BFLOAT16)) == IA             # router type
+        assert bad(2, ((E, I, H + 8), F16)) == IA               # fc1 K
+        assert bad(2, ((E + 1, I, H), F16)) == IA               # fc1 experts
+        assert bad(4, ((E, H + 8, I), F16)) == IA               # fc2 rows
+        assert bad(6, ((E, I + 8, H), F16)) == IA               # fc3 rows
+        assert bad(3, ((E, I + 1), F16)) == IA                  # fc1 bias
+        assert bad(5, ((E, H), pkg.FLOAT)) == IA                # fc2 bias type
+        assert bad(None, None, out=(T, H + 8)) == IA            # output shape
+        assert bad(None, None, out_et=pkg.FLOAT) == IA          # output type
+        assert "output" in pkg.lib().moe_b200_last_error().decode()
+    finally:
+        moe.release()
+
+    q = pkg.QMoE(k=2, activation_type="silu", expert_weight_bits=4, block_size=32)
+    try:
+        goodq = [((T, H), F16), ((T, E), F16), ((E, I, H // 2), U8), ((E, I, H // 32), F16),
+                 (None, F16), ((E, H, I // 2), U8), ((E, H, I // 32), F16), (None, F16),
+                 ((E, I, H // 2), U8), ((E, I, H // 32), F16), (None, F16)]
+
+        def badq(i, spec, n=None):
+            specs = list(goodq)
+            if i is not None:
+                specs[i] = spec
+            return _compute(pkg, q, specs[:n] if n else specs, (T, H), F16)
+
+        IA, NI = pkg.INVALID_ARGUMENT, pkg.NOT_IMPLEMENTED
+        assert badq(None, None, n=6) == IA                      # fewer than 7 inputs
+        assert badq(2, ((E, I, H), U8)) == IA                   # codes not packed 2 per byte
+        assert badq(2, ((E, I, H // 2), F16)) == IA             # codes not uint8
+        assert badq(3, ((E, I, H // 32 + 1), F16)) == IA        # block count of fc1 scales
+        assert badq(3, ((E, I), F16)) == IA                     # per-row scales, block_size 32
+        assert badq(6, (None, F16)) == IA                       # fc2 scales missing
+        assert badq(9, (None, F16)) == IA                       # fc3 scales missing
+        specs = goodq + [((E, I), U8)]                          # fc1 zero points (asymmetric)
+        assert _compute(pkg, q, specs, (T, H), F16) == NI
+    finally:
+        q.release()
