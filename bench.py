@@ -534,11 +534,24 @@ def bench_ours(args, cfg, rank, world, dev):
         else:
             k_name = "tc_pair_grouped_gemm_kernel (fc1+fc3, SwiGLU epilogue)"
         achieved = alg["flops_fc1"] / (gemm_ms["fc1"] / 1e3) / 1e12
-        roof_t = max(alg["flops"] / (pk["tflops"] * 1e12), alg["bytes"] / (pk["hbm"] * 1e9))
-        roof = {"bound": "tensor", "kernel": k_name, "achieved": round(achieved, 1),
-                "peak": pk["tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["tflops"], 4),
-                "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)",
-                "frac_of_sustained": round(achieved / pk["tflops_sus"], 4) if pk["tflops_sus"] else None,
+        if cfg["kind"] == "moe" and cfg["dtype"] == "float32":
+            # FFMA-bound: no tensor-core peak applies.  Derived peak = SMs x 128 fp32
+            # lanes x 2 FLOP x the maximum SM clock (no measured FFMA figure exists).
+            props = torch.cuda.get_device_properties(dev)
+            mhz = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get(
+                "sm_max_mhz", 1965.0)) if (ROOT / "MEASURED_PEAKS.json").exists() else 1965.0
+            c_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+            bound, c_src, c_sus = "fp32 FFMA", (f"derived: {props.multi_processor_count} SMs x "
+                                                f"128 lanes x 2 x {mhz:.0f} MHz"), None
+        else:
+            c_peak, bound = pk["tflops"], "tensor"
+            c_src = f"{pk['src']} bf16 burst (MEASURED_PEAKS.json)"
+            c_sus = round(achieved / pk["tflops_sus"], 4) if pk["tflops_sus"] else None
+        roof_t = max(alg["flops"] / (c_peak * 1e12), alg["bytes"] / (pk["hbm"] * 1e9))
+        roof = {"bound": bound, "kernel": k_name, "achieved": round(achieved, 1),
+                "peak": round(c_peak, 1), "unit": "TFLOP/s", "frac": round(achieved / c_peak, 4),
+                "peak_source": c_src,
+                "frac_of_sustained": c_sus,
                 "traffic": None if prepacked else FC1_TRAFFIC_BYTES.get((args.config, T)),
                 "alg_flops_per_launch": alg["flops_fc1"],
                 "fc2": {"achieved": round(alg["flops_fc2"] / (gemm_ms["fc2"] / 1e3) / 1e12, 1)},

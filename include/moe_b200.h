@@ -264,8 +264,11 @@ int moe_b200_notification_wait(void* event, void* stream);       /* stream wait 
 int moe_b200_notification_synchronize(void* event);              /* host wait */
 int moe_b200_notification_destroy(void* event);
 
-/* Data transfer (musa/ep/src/ep_data_transfer.cc:108-227).  kind: 1 = H2D,
- * 2 = D2H, 3 = D2D.  D2H synchronises `stream` before returning. */
+/* Data transfer (musa/ep/src/ep_data_transfer.cc:108-227).  kind: 0 = host to host,
+ * 1 = H2D, 2 = D2H, 3 = D2D.  H2D and D2D are ordered on `stream` and return at once.
+ * D2H returns with the data in place: it waits for `stream` only, or, when `stream` is
+ * NULL, for the whole device before copying.  Host to host waits for `stream` (the
+ * source's producer, if any) and copies on the host.  bytes == 0 or dst == src: no-op. */
 int moe_b200_copy(void* dst, const void* src, size_t bytes, int32_t kind,
                   void* stream);
 
@@ -298,10 +301,14 @@ typedef struct moe_b200_ep_comm moe_b200_ep_comm;
 int moe_b200_ep_comm_create(int32_t rank, int32_t world, int64_t max_rows, int32_t k_max,
                             int64_t hidden_size, int64_t num_experts, int32_t dtype,
                             moe_b200_ep_comm** comm);
-/* Bytes of one rank's IPC handle (cudaIpcMemHandle_t). */
+/* Bytes of one rank's handle: its cudaIpcMemHandle_t followed by the arguments its
+ * region was created with (rank, world, max_rows, k_max, hidden_size, num_experts, dtype). */
 int moe_b200_ep_comm_handle_size(size_t* bytes);
 int moe_b200_ep_comm_get_handle(moe_b200_ep_comm* comm, void* handle);
-/* handles: world handles in rank order (this rank's own entry is ignored). */
+/* handles: world handles in rank order (this rank's own entry is ignored).  Every rank
+ * must have created its communicator with the same world, max_rows, k_max, hidden_size,
+ * num_experts and dtype, since peers write at offsets computed from their own layout:
+ * any difference returns INVALID_ARGUMENT before a peer region is opened. */
 int moe_b200_ep_comm_connect(moe_b200_ep_comm* comm, const void* handles);
 /* Frees this rank's region: every rank must have finished its last moe_b200_ep_forward
  * (e.g. a barrier after a stream synchronisation) before any rank destroys its

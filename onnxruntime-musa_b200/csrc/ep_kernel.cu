@@ -162,6 +162,7 @@ int moe_b200_kernel_create(const char* op_type, int32_t num_attrs, const char* c
 int moe_b200_kernel_compute(moe_b200_kernel* kern, int32_t num_inputs,
                             const moe_b200_tensor_ref* in, moe_b200_tensor_ref* output,
                             void* stream) {
+  moe::clear_stale_cuda_error();
   if (kern == nullptr || in == nullptr || output == nullptr)
     return (efail(MOE_B200_INVALID_ARGUMENT, "kernel, inputs and output must be non-NULL"));
   const bool q = kern->quantized;
@@ -328,6 +329,7 @@ int moe_b200_kernel_compute(moe_b200_kernel* kern, int32_t num_inputs,
 int moe_b200_kernel_prepack(moe_b200_kernel* kern, int32_t num_inputs,
                             const moe_b200_tensor_ref* in, int32_t share, void* stream,
                             int32_t* is_packed) {
+  moe::clear_stale_cuda_error();
   if (kern == nullptr || in == nullptr)
     return (efail(MOE_B200_INVALID_ARGUMENT, "kernel and inputs must be non-NULL"));
   if (is_packed != nullptr) *is_packed = 0;
@@ -404,8 +406,10 @@ int moe_b200_kernel_release(moe_b200_kernel* kern) {
 #define RT_CHECK(expr, what)                                                            \
   do {                                                                                  \
     cudaError_t _st = (expr);                                                           \
-    if (_st != cudaSuccess)                                                             \
-      return (efail(MOE_B200_EP_FAIL, "%s: %s", what, cudaGetErrorString(_st)));  \
+    if (_st != cudaSuccess) {                                                           \
+      (void)cudaGetLastError(); /* the failure is returned here, not left behind */      \
+      return (efail(MOE_B200_EP_FAIL, "%s: %s", what, cudaGetErrorString(_st)));         \
+    }                                                                                   \
   } while (0)
 
 int moe_b200_device_count(int32_t* count) {
@@ -514,20 +518,35 @@ int moe_b200_notification_destroy(void* event) {
   return MOE_B200_OK;
 }
 
+// Ordering follows MusaDataTransfer::CopyImpl (musa/ep/src/ep_data_transfer.cc:108-161):
+// device-bound copies are stream-ordered and return at once; a device-to-host copy with a
+// stream waits for that stream only (other workers' streams keep running), and without
+// one waits for the whole device first, since a synchronous copy on the legacy stream does
+// not order work on non-blocking streams; host-to-host copies wait for the given stream
+// (the producer of the source) and then copy on the host.
 int moe_b200_copy(void* dst, const void* src, size_t bytes, int32_t kind, void* stream) {
-  if (bytes == 0) return MOE_B200_OK;
+  if (bytes == 0 || dst == src) return MOE_B200_OK;
   if (!dst || !src) return (efail(MOE_B200_INVALID_ARGUMENT, "copy with NULL pointer"));
-  cudaMemcpyKind k;
-  switch (kind) {
-    case 1: k = cudaMemcpyHostToDevice; break;
-    case 2: k = cudaMemcpyDeviceToHost; break;
-    case 3: k = cudaMemcpyDeviceToDevice; break;
-    default: return (efail(MOE_B200_INVALID_ARGUMENT, "copy kind %d", kind));
-  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  RT_CHECK(cudaMemcpyAsync(dst, src, bytes, k, s), "cudaMemcpyAsync");
-  if (kind == 2) RT_CHECK(cudaStreamSynchronize(s), "cudaStreamSynchronize");
-  return MOE_B200_OK;
+  switch (kind) {
+    case 0:
+      if (s) RT_CHECK(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+      std::memcpy(dst, src, bytes);
+      return MOE_B200_OK;
+    case 1:
+      RT_CHECK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+      return MOE_B200_OK;
+    case 2:
+      if (!s) RT_CHECK(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+      RT_CHECK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
+      RT_CHECK(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+      return MOE_B200_OK;
+    case 3:
+      RT_CHECK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s), "cudaMemcpyAsync");
+      return MOE_B200_OK;
+    default:
+      return (efail(MOE_B200_INVALID_ARGUMENT, "copy kind %d", kind));
+  }
 }
 
 }  // extern "C"

@@ -283,6 +283,33 @@ int cuda_fail(cudaError_t st, const char* what) {
   return moe::set_error(MOE_B200_EP_FAIL, "%s: %s", what, cudaGetErrorString(st));
 }
 
+// Travels after the IPC handle: the parameters that fix a region's layout.  Peers store
+// rows and flags at offsets computed from their own layout, so every rank must hold the
+// same one; connect compares them before it opens any peer region.
+struct EpHandleDesc {
+  uint32_t magic;
+  int32_t rank, world, k_max, num_experts, dtype;
+  int64_t max_rows, hidden;
+  uint64_t total;
+};
+constexpr uint32_t kEpHandleMagic = 0x4d4f4550u;  // "MOEP"
+
+EpHandleDesc describe(const moe_b200_ep_comm* c) {
+  EpHandleDesc d{};
+  d.magic = kEpHandleMagic;
+  d.rank = c->rank;
+  d.world = c->world;
+  d.k_max = c->k_max;
+  d.num_experts = c->num_experts;
+  d.dtype = c->dtype;
+  d.max_rows = c->max_rows;
+  d.hidden = c->hidden;
+  d.total = c->lay.total;
+  return d;
+}
+
+constexpr size_t kEpHandleBytes = sizeof(cudaIpcMemHandle_t) + sizeof(EpHandleDesc);
+
 }  // namespace
 
 extern "C" {
@@ -290,6 +317,7 @@ extern "C" {
 int moe_b200_ep_comm_create(int32_t rank, int32_t world, int64_t max_rows, int32_t k_max,
                             int64_t hidden_size, int64_t num_experts, int32_t dtype,
                             moe_b200_ep_comm** comm) {
+  moe::clear_stale_cuda_error();
   if (comm == nullptr) return moe::set_error(MOE_B200_INVALID_ARGUMENT, "comm is NULL");
   if (world < 1 || world > moe::kMaxEpRanks || rank < 0 || rank >= world)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT, "rank %d / world %d (world <= %d)", rank,
@@ -331,7 +359,7 @@ int moe_b200_ep_comm_create(int32_t rank, int32_t world, int64_t max_rows, int32
 
 int moe_b200_ep_comm_handle_size(size_t* bytes) {
   if (bytes == nullptr) return moe::set_error(MOE_B200_INVALID_ARGUMENT, "bytes is NULL");
-  *bytes = sizeof(cudaIpcMemHandle_t);
+  *bytes = kEpHandleBytes;
   return MOE_B200_OK;
 }
 
@@ -341,7 +369,9 @@ int moe_b200_ep_comm_get_handle(moe_b200_ep_comm* c, void* handle) {
   cudaIpcMemHandle_t h;
   const cudaError_t e = cudaIpcGetMemHandle(&h, c->sym);
   if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  const EpHandleDesc d = describe(c);
   std::memcpy(handle, &h, sizeof(h));
+  std::memcpy(static_cast<uint8_t*>(handle) + sizeof(h), &d, sizeof(d));
   return MOE_B200_OK;
 }
 
@@ -349,12 +379,33 @@ int moe_b200_ep_comm_connect(moe_b200_ep_comm* c, const void* handles) {
   if (c == nullptr || handles == nullptr)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT, "comm and handles must be non-NULL");
   if (c->connected) return moe::set_error(MOE_B200_INVALID_ARGUMENT, "already connected");
+  const uint8_t* blob = static_cast<const uint8_t*>(handles);
+  const EpHandleDesc mine = describe(c);
+  for (int d = 0; d < c->world; ++d) {
+    if (d == c->rank) continue;
+    EpHandleDesc o;
+    std::memcpy(&o, blob + d * kEpHandleBytes + sizeof(cudaIpcMemHandle_t), sizeof(o));
+    if (o.magic != kEpHandleMagic || o.rank != d)
+      return moe::set_error(MOE_B200_INVALID_ARGUMENT,
+                            "handle %d is not a moe_b200_ep_comm handle of rank %d", d, d);
+    if (o.world != mine.world || o.k_max != mine.k_max || o.num_experts != mine.num_experts ||
+        o.dtype != mine.dtype || o.max_rows != mine.max_rows || o.hidden != mine.hidden ||
+        o.total != mine.total)
+      return moe::set_error(
+          MOE_B200_INVALID_ARGUMENT,
+          "rank %d's region differs from rank %d's (world %d/%d, max_rows %lld/%lld, k_max "
+          "%d/%d, hidden %lld/%lld, experts %d/%d, dtype %d/%d): every rank must create its "
+          "communicator with the same arguments",
+          d, c->rank, o.world, mine.world, (long long)o.max_rows, (long long)mine.max_rows,
+          o.k_max, mine.k_max, (long long)o.hidden, (long long)mine.hidden, o.num_experts,
+          mine.num_experts, o.dtype, mine.dtype);
+  }
   cudaError_t e = cudaSetDevice(c->device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   for (int d = 0; d < c->world; ++d) {
     if (d == c->rank) continue;
     cudaIpcMemHandle_t h;
-    std::memcpy(&h, static_cast<const uint8_t*>(handles) + d * sizeof(h), sizeof(h));
+    std::memcpy(&h, blob + d * kEpHandleBytes, sizeof(h));
     void* ptr = nullptr;
     e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
     if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
@@ -387,6 +438,7 @@ int moe_b200_ep_workspace_size(const moe_b200_ep_comm* c, const moe_b200_problem
 int moe_b200_ep_forward(moe_b200_ep_comm* c, const moe_b200_problem* problem,
                         const moe_b200_tensors* t, void* workspace, size_t workspace_bytes,
                         void* stream) {
+  moe::clear_stale_cuda_error();
   if (c == nullptr || problem == nullptr || t == nullptr)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT, "comm, problem and tensors must be non-NULL");
   if (!c->connected) return moe::set_error(MOE_B200_INVALID_ARGUMENT, "comm is not connected");

@@ -712,6 +712,7 @@ int moe_b200_workspace_size(const moe_b200_problem* problem, size_t* bytes) {
 
 int moe_b200_forward(const moe_b200_problem* problem, const moe_b200_tensors* t,
                      void* workspace, size_t workspace_bytes, void* stream) {
+  moe::clear_stale_cuda_error();
   int st = validate_problem(problem);
   if (st != MOE_B200_OK) return st;
   if (t == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "tensors is NULL");
@@ -722,6 +723,7 @@ int moe_b200_forward(const moe_b200_problem* problem, const moe_b200_tensors* t,
 int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tensors* t,
                            void* workspace, size_t workspace_bytes, void* stream,
                            float* stage_ms, int32_t num_stages) {
+  moe::clear_stale_cuda_error();
   int st = validate_problem(problem);
   if (st != MOE_B200_OK) return st;
   if (t == nullptr || stage_ms == nullptr || num_stages < kNumStages)
@@ -745,6 +747,7 @@ int moe_b200_forward_timed(const moe_b200_problem* problem, const moe_b200_tenso
 int moe_b200_forward_staged(const moe_b200_problem* problem, const moe_b200_tensors* t,
                             void* workspace, size_t workspace_bytes, void* stream,
                             void* const* events, int32_t num_events) {
+  moe::clear_stale_cuda_error();
   int st = validate_problem(problem);
   if (st != MOE_B200_OK) return st;
   if (t == nullptr || events == nullptr || num_events < kNumStages + 1)
@@ -773,6 +776,7 @@ int moe_b200_forward_prepacked(const moe_b200_problem* problem, const moe_b200_t
                                const moe_b200_prepacked* prepacked, void* workspace,
                                size_t workspace_bytes, void* stream, void* const* events,
                                int32_t num_events) {
+  moe::clear_stale_cuda_error();
   int st = validate_problem(problem);
   if (st != MOE_B200_OK) return st;
   if (t == nullptr) return fail(MOE_B200_INVALID_ARGUMENT, "tensors is NULL");
@@ -797,6 +801,7 @@ int moe_b200_ep_dispatch(const moe_b200_problem* problem, const void* router_pro
                          const void* input, void* send_rows, int32_t* expert_offsets,
                          int32_t* permuted_pos, float* route_weight, void* workspace,
                          size_t workspace_bytes, void* stream) {
+  moe::clear_stale_cuda_error();
   int st = validate_problem(problem);
   if (st != MOE_B200_OK) return st;
   const moe_b200_problem& p = *problem;
@@ -839,6 +844,7 @@ int moe_b200_ep_dispatch(const moe_b200_problem* problem, const void* router_pro
 int moe_b200_expert_ffn(const moe_b200_problem* problem, const moe_b200_tensors* t,
                         const int32_t* row_expert, void* workspace, size_t workspace_bytes,
                         void* stream) {
+  moe::clear_stale_cuda_error();
   int st = validate_problem(problem);
   if (st != MOE_B200_OK) return st;
   if (t == nullptr || (problem->num_rows > 0 && row_expert == nullptr))
@@ -850,6 +856,7 @@ int moe_b200_expert_ffn(const moe_b200_problem* problem, const moe_b200_tensors*
 int moe_b200_ep_combine(int32_t dtype, int64_t num_rows, int64_t hidden_size, int32_t k,
                         const void* expert_rows, const int32_t* permuted_pos,
                         const float* route_weight, void* output, void* stream) {
+  moe::clear_stale_cuda_error();
   if (!is_float_type(dtype)) return fail(MOE_B200_NOT_IMPLEMENTED, "unsupported dtype %d", dtype);
   if (num_rows < 0 || hidden_size <= 0 || k < 1)
     return fail(MOE_B200_INVALID_ARGUMENT, "ep_combine: invalid shape");
@@ -864,6 +871,7 @@ int moe_b200_ep_combine(int32_t dtype, int64_t num_rows, int64_t hidden_size, in
 int moe_b200_route(const void* router_probs, int32_t dtype, int64_t num_rows,
                    int64_t num_experts, int32_t k, int32_t normalize_routing_weights,
                    int32_t* expert_idx, float* route_weight, void* stream) {
+  moe::clear_stale_cuda_error();
   if (!is_float_type(dtype)) return fail(MOE_B200_NOT_IMPLEMENTED, "unsupported dtype %d", dtype);
   if (num_experts < 1 || num_experts > kMaxExperts || k < 1 || k > num_experts || k > kMaxK ||
       num_rows < 0)
@@ -890,6 +898,7 @@ int moe_b200_norm_router(int32_t dtype, int64_t num_rows, int64_t hidden_size,
                          int64_t num_experts, const void* input, const void* skip,
                          const float* gamma, float epsilon, const void* router_weight,
                          void* residual_out, void* normed, void* router_logits, void* stream) {
+  moe::clear_stale_cuda_error();
   if (!is_float_type(dtype)) return fail(MOE_B200_NOT_IMPLEMENTED, "unsupported dtype %d", dtype);
   if (num_rows < 0 || hidden_size < 8 || hidden_size % 8 != 0 || num_experts < 1)
     return fail(MOE_B200_INVALID_ARGUMENT,
@@ -924,6 +933,7 @@ int moe_b200_permute(const int32_t* expert_idx, int64_t num_rows, int32_t k,
                      int64_t num_experts, int32_t* expert_offsets, int32_t* permuted_pos,
                      int32_t* permuted_src, void* workspace, size_t workspace_bytes,
                      void* stream) {
+  moe::clear_stale_cuda_error();
   if (num_experts < 1 || num_experts > kMaxExperts || k < 1 || num_rows < 0)
     return fail(MOE_B200_INVALID_ARGUMENT, "invalid permutation shape");
   if (workspace_bytes < moe_b200_permute_workspace_size(num_rows, k, num_experts))

@@ -15,6 +15,12 @@ constexpr int kDtBF16 = 16;
 // Records `fmt` as this thread's last error message (read by moe_b200_last_error)
 // and returns `code`.
 int set_error(int code, const char* fmt, ...);
+// Resets the runtime's last-error state at the start of a public entry point.  A failed
+// runtime call elsewhere in the process (an allocation that ran out of memory, say) leaves
+// a non-sticky error that the next cudaGetLastError() would report; without the reset a
+// launch check of this library would blame its own launch for it.  Sticky errors (a
+// faulted context) stay and are still reported.
+inline void clear_stale_cuda_error() { (void)cudaGetLastError(); }
 
 inline int dtype_bytes(int dt) { return dt == kDtF32 ? 4 : (dt == kDtU8 ? 1 : 2); }
 

@@ -85,6 +85,7 @@ extern "C" {
 
 int moe_b200_pipeline_create(const moe_b200_problem* problem, const moe_b200_tensors* weights,
                              int32_t depth, moe_b200_pipeline** pipeline) {
+  moe::clear_stale_cuda_error();
   if (problem == nullptr || weights == nullptr || pipeline == nullptr)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT, "problem, weights and pipeline must be non-NULL");
   if (depth < 1 || depth > 8)
@@ -162,6 +163,7 @@ int moe_b200_pipeline_set_prepacked(moe_b200_pipeline* pl, moe_b200_prepacked* p
 int moe_b200_pipeline_submit(moe_b200_pipeline* pl, const void* host_input,
                              const void* host_router_probs, void* host_output,
                              int64_t num_rows) {
+  moe::clear_stale_cuda_error();
   if (pl == nullptr) return moe::set_error(MOE_B200_INVALID_ARGUMENT, "pipeline is NULL");
   if (num_rows < 0 || num_rows > pl->problem.num_rows)
     return moe::set_error(MOE_B200_INVALID_ARGUMENT,

@@ -129,6 +129,7 @@ extern "C" {
 
 int moe_b200_prepack_create(const moe_b200_problem* problem, const moe_b200_tensors* weights,
                             int32_t share, void* stream, moe_b200_prepacked** out) {
+  moe::clear_stale_cuda_error();
   using moe::set_error;
   if (problem == nullptr || weights == nullptr || out == nullptr)
     return set_error(MOE_B200_INVALID_ARGUMENT, "problem, weights and out must be non-NULL");

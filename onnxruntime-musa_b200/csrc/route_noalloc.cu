@@ -65,6 +65,7 @@ extern "C" int moe_b200_route_noalloc(const void* router_probs, int32_t dtype,
                                       int64_t num_rows, int64_t num_experts, int32_t k,
                                       int32_t normalize_routing_weights, int32_t* expert_idx,
                                       float* route_weight, void* stream) {
+  moe::clear_stale_cuda_error();
   if (dtype != moe::kDtF32 && dtype != moe::kDtF16 && dtype != moe::kDtBF16)
     return moe::set_error(MOE_B200_NOT_IMPLEMENTED, "unsupported dtype %d", dtype);
   if (num_experts < 1 || num_experts > moe::kMaxExperts || k < 1 || k > num_experts ||

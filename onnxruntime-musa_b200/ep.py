@@ -113,15 +113,27 @@ class ExpertParallelMoE:
         return out
 
     # ------------------------------------------------------------- p2p transport
+    def agree_max_rows(self, T: int) -> int:
+        """The exchange region's row capacity, the same on every rank: the max_rows given
+        to the constructor (which must then be equal on all ranks; peers write at offsets
+        computed from it), else the largest first call's T over the ranks."""
+        mine = (int(self.max_rows) if self.max_rows is not None else int(T),
+                self.max_rows is not None)
+        vals = [mine]
+        if self.world > 1:
+            vals = [None] * self.world
+            dist.all_gather_object(vals, mine, group=self.group)
+        given = {v for v, g in vals if g}
+        if given and (len(given) > 1 or not all(g for _, g in vals)):
+            raise ValueError(f"ranks were constructed with different max_rows "
+                             f"{[v if g else None for v, g in vals]}: the exchange "
+                             "regions must have the same layout on every rank")
+        return max(1, max(v for v, _ in vals))
+
     def _connect(self, T: int, device) -> None:
         """Creates this rank's exchange region (same size on every rank: the largest call,
         agreed by an all-reduce) and opens the other ranks' regions (IPC handles)."""
-        max_rows = self.max_rows
-        if max_rows is None:
-            t = torch.tensor([T], dtype=torch.int64, device=device)
-            if self.world > 1:
-                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
-            max_rows = max(1, int(t.item()))
+        max_rows = self.agree_max_rows(T)
         self.max_rows = max_rows
         comm = self.pkg.EpComm(self.rank, self.world, max_rows, self.k, self.H, self.E,
                                self.dtype)

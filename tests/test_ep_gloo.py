@@ -149,3 +149,44 @@ def test_expert_parallel_dead_peer_raises():
     assert res[1] == "left"
     assert isinstance(res[0], tuple) and res[0][0] == "raised", res[0]
     assert res[0][2] < 60
+
+
+def _max_rows_worker(rank, world, port, result_q, given):
+    import __graft_entry__ as ge
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pkg, orc = ge.load_package(), ge.load_oracle()
+        from onnxruntime_musa_b200 import ep
+        attrs = dict(activation_type="silu", k=2, normalize_routing_weights=1)
+        layer = ep.ExpertParallelMoE(pkg, num_experts=4, hidden_size=16, inter_size=8,
+                                     dtype=pkg.FLOAT, has_fc3=False, local_weights={},
+                                     backend=OracleBackend(orc, attrs), max_rows=given[rank],
+                                     **attrs)
+        try:
+            result_q.put((rank, ("ok", layer.agree_max_rows(10 + rank))))
+        except ValueError as exc:
+            result_q.put((rank, ("rejected", str(exc))))
+    except Exception as exc:
+        result_q.put((rank, ("error", repr(exc))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("given,expect", [((None, None), ("ok", 11)), ((64, 64), ("ok", 64)),
+                                          ((64, 128), ("rejected",)), ((64, None), ("rejected",))])
+def test_exchange_region_capacity_agreed_or_rejected(given, expect):
+    """The p2p exchange regions must have the same layout on every rank (peers store at
+    offsets computed from their own max_rows): ranks given different max_rows fail on
+    every rank before any region is opened."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_max_rows_worker, args=(r, 2, port, q, given)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert res[r][:len(expect)] == expect, res[r]

@@ -176,3 +176,30 @@ def test_ep_host_pipeline(pkg, orc, dev):
         ref = layer.forward(hx.to(dev), hl.to(dev)).cpu()
         assert torch.equal(ho, ref)
     layer.close()
+
+
+def test_ep_connect_rejects_mismatched_regions(pkg, dev):
+    """Two communicators of one 2-rank job whose regions differ (max_rows 64 against 128):
+    connect refuses the peer's handle before it opens it (no peer memory is touched)."""
+    import ctypes
+    a = pkg.EpComm(0, 2, 64, 2, 256, 8, pkg.FLOAT16)
+    b = pkg.EpComm(1, 2, 128, 2, 256, 8, pkg.FLOAT16)
+    try:
+        ha, hb = a.handle(), b.handle()
+        n = ctypes.c_size_t()
+        assert pkg.lib().moe_b200_ep_comm_handle_size(ctypes.byref(n)) == 0
+        assert len(ha) == len(hb) == n.value > 64  # IPC handle + region description
+        with pytest.raises(pkg.MoeB200Error, match="same arguments"):
+            a.connect([ha, hb])
+        with pytest.raises(pkg.MoeB200Error, match="same arguments"):
+            b.connect([ha, hb])
+        # a handle in the wrong rank slot is refused too
+        c = pkg.EpComm(1, 2, 64, 2, 256, 8, pkg.FLOAT16)
+        try:
+            with pytest.raises(pkg.MoeB200Error, match="not a moe_b200_ep_comm handle"):
+                a.connect([ha, ha])
+        finally:
+            c.close()
+    finally:
+        a.close()
+        b.close()
