@@ -294,7 +294,8 @@ int moe_b200_norm_router(int32_t dtype, int64_t num_rows, int64_t hidden_size,
  * writes routed rows into the owners' receive buffers, the fc2 epilogue writes the FFN
  * rows back into the senders' return buffers, and flags (bounded waits) order the steps.
  * The reference EP has no multi-device path (musa/ep/src/ep_factory.cc:466-470); these
- * entries are the dispatch / combine exchange of the MoE path.  fp16/bf16 MoE only. */
+ * entries are the dispatch / combine exchange of the MoE path.  fp16/bf16 MoE and fp16
+ * QMoE (int4/int8 codes converted inside the tensor-core GEMM on the received rows). */
 typedef struct moe_b200_ep_comm moe_b200_ep_comm;
 
 /* Allocates this rank's region for calls of up to max_rows tokens with k <= k_max. */

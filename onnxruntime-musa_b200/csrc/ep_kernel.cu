@@ -94,6 +94,10 @@ std::string shape_str(const moe_b200_tensor_ref& t) {
 
 extern "C" {
 
+static const char* op_name(const moe_b200_kernel* kern) {
+  return kern == nullptr ? "?" : (kern->quantized ? "QMoE" : "MoE");
+}
+
 int moe_b200_kernel_create(const char* op_type, int32_t num_attrs, const char* const* names,
                            const char* const* values, moe_b200_kernel** kernel) {
   if (kernel == nullptr || op_type == nullptr)
@@ -156,12 +160,50 @@ int moe_b200_kernel_create(const char* op_type, int32_t num_attrs, const char* c
   kern->quantized = q;
   kern->attrs = a;
   *kernel = kern;
+  if (std::getenv("MOE_B200_TRACE_KERNELS") != nullptr) {
+    std::fprintf(stderr, "MOE_B200_KERNEL_CREATE %s impl=%p k=%d bits=%d block=%d\n",
+                 op_name(kern), static_cast<void*>(kern), a.k, a.expert_weight_bits,
+                 a.block_size);
+    std::fflush(stderr);
+  }
   return MOE_B200_OK;
 }
 
+static int kernel_compute_impl(moe_b200_kernel* kern, int32_t num_inputs,
+                               const moe_b200_tensor_ref* in, moe_b200_tensor_ref* output,
+                               void* stream);
+
+// Kernel trace of the reference EP (OpKernelBase::ComputeImpl,
+// musa/ep/src/kernels/shared_inc/kernel_base.h:45-84): with MOE_B200_TRACE_KERNELS set,
+// one BEGIN and one END line per compute on stderr, flushed; with MOE_B200_TRACE_SYNC as
+// well, a successful compute synchronises its stream so an asynchronous fault is reported
+// (EP_FAIL) at the kernel that caused it.
 int moe_b200_kernel_compute(moe_b200_kernel* kern, int32_t num_inputs,
                             const moe_b200_tensor_ref* in, moe_b200_tensor_ref* output,
                             void* stream) {
+  const bool trace = std::getenv("MOE_B200_TRACE_KERNELS") != nullptr;
+  if (trace) {
+    std::fprintf(stderr, "MOE_B200_KERNEL_BEGIN %s impl=%p\n", op_name(kern),
+                 static_cast<void*>(kern));
+    std::fflush(stderr);
+  }
+  int rc = kernel_compute_impl(kern, num_inputs, in, output, stream);
+  if (trace) {
+    if (rc == MOE_B200_OK && std::getenv("MOE_B200_TRACE_SYNC") != nullptr) {
+      const cudaError_t st = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+      if (st != cudaSuccess)
+        rc = efail(MOE_B200_EP_FAIL, "stream synchronize: %s", cudaGetErrorString(st));
+    }
+    std::fprintf(stderr, "MOE_B200_KERNEL_END %s impl=%p status=%d\n", op_name(kern),
+                 static_cast<void*>(kern), rc);
+    std::fflush(stderr);
+  }
+  return rc;
+}
+
+static int kernel_compute_impl(moe_b200_kernel* kern, int32_t num_inputs,
+                               const moe_b200_tensor_ref* in, moe_b200_tensor_ref* output,
+                               void* stream) {
   moe::clear_stale_cuda_error();
   if (kern == nullptr || in == nullptr || output == nullptr)
     return (efail(MOE_B200_INVALID_ARGUMENT, "kernel, inputs and output must be non-NULL"));
@@ -387,6 +429,11 @@ int moe_b200_kernel_prepack(moe_b200_kernel* kern, int32_t num_inputs,
 
 int moe_b200_kernel_release(moe_b200_kernel* kern) {
   if (kern == nullptr) return MOE_B200_OK;
+  if (std::getenv("MOE_B200_TRACE_KERNELS") != nullptr) {
+    std::fprintf(stderr, "MOE_B200_KERNEL_RELEASE %s impl=%p\n", op_name(kern),
+                 static_cast<void*>(kern));
+    std::fflush(stderr);
+  }
   {
     std::lock_guard<std::mutex> lock(kern->mu);
     for (auto& kv : kern->ws)

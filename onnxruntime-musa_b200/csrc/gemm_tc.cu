@@ -1535,6 +1535,11 @@ cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.qepi = QEPI;
   p.qbias = 1024.0f + static_cast<float>(1 << (BITS - 1));
   p.rowsum = g.rowsum;
+  p.seg_start = g.seg_start;
+  p.seg_dst = g.seg_dst;
+  p.nseg = g.nseg;
+  p.remap_world = g.remap_world;
+  for (int i = 0; i < kMaxEpRanks; ++i) p.out_peers[i] = g.out_peers[i];
   static bool attr_set = false;  // idempotent; a race between first callers is benign
   if (!attr_set) {
     cudaError_t st = cudaFuncSetAttribute(tc_pair_qgemm_kernel<BITS, QEPI>,

@@ -10,6 +10,7 @@
 //   fc1(+fc3)   grouped GEMM, activation fused in the epilogue  -> act [R, I]
 //   fc2         grouped GEMM, bias fused                          -> Y [R, H] (aliases Xp)
 //   combine     out[t] = sum_j w[t, j] * Y[pos[t, j]]
+#include <nvtx3/nvToolsExt.h>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -309,6 +310,23 @@ void set_quantized(const moe_b200_problem& p, GemmArgs& g, const void* scales_a,
 // Stage boundaries recorded when `ev` is non-NULL (kNumStages + 1 events).
 enum Stage { kStRoute = 0, kStPlan, kStGather, kStDequant, kStFc1, kStFc2, kStCombine, kNumStages };
 
+// NVTX ranges, one per stage of a layer call ("moe_b200/route", ...), as the host
+// enqueues it: a profiler filters on them (ncu --nvtx --nvtx-include "moe_b200/fc1/").
+// Without a tool attached an NVTX call is a null-pointer check.
+constexpr const char* kStageNames[kNumStages] = {
+    "moe_b200/route", "moe_b200/plan", "moe_b200/gather", "moe_b200/dequant",
+    "moe_b200/fc1", "moe_b200/fc2", "moe_b200/combine"};
+
+struct StageRanges {
+  bool open = false;
+  void enter(int i) {
+    if (open) nvtxRangePop();
+    open = i >= 0 && i < kNumStages;
+    if (open) nvtxRangePushA(kStageNames[i]);
+  }
+  ~StageRanges() { if (open) nvtxRangePop(); }
+};
+
 // One layer call.  With `given_idx` (k == 1) the routing is supplied by the caller: rows
 // of `input` are already assigned to experts (expert parallelism: the rows a rank
 // received), every routing weight is 1, and the output row i is expert(row i)'s FFN
@@ -316,7 +334,11 @@ enum Stage { kStRoute = 0, kStPlan, kStGather, kStDequant, kStFc1, kStFc2, kStCo
 int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
                  size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev = nullptr,
                  const int32_t* given_idx = nullptr, const moe_b200_prepacked* pk = nullptr) {
-  auto mark = [&](int i) { if (ev && ev[i]) cudaEventRecord(ev[i], s); };
+  StageRanges ranges;
+  auto mark = [&](int i) {
+    if (ev && ev[i]) cudaEventRecord(ev[i], s);
+    ranges.enter(i);
+  };
   const bool use_pk = prepack_applies(pk, p);
   const WsLayout L = plan_workspace(p, use_pk);
   if (ws_bytes < L.total)
@@ -595,8 +617,10 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
                 "(dtype %d, hidden %lld, rows <= %lld, k <= %d)",
                 p.dtype, (long long)p.hidden_size, (long long)p.num_rows, p.attrs.k, c->dtype,
                 (long long)c->hidden, (long long)c->max_rows, c->k_max);
-  if (p.attrs.expert_weight_bits != 0)
-    return fail(MOE_B200_NOT_IMPLEMENTED, "device-side expert parallelism runs MoE (not QMoE)");
+  const bool quant = p.attrs.expert_weight_bits != 0;
+  if (quant && (t.fc1_scales == nullptr || t.fc2_scales == nullptr ||
+                (p.has_fc3 && t.fc3_scales == nullptr)))
+    return fail(MOE_B200_INVALID_ARGUMENT, "QMoE: fc1/fc2(/fc3) scales must be non-NULL");
   if (p.attrs.k > E) return fail(MOE_B200_INVALID_ARGUMENT, "k=%d > %d experts", p.attrs.k, E);
   if (t.fc1_weights == nullptr || t.fc2_weights == nullptr || (p.has_fc3 && !t.fc3_weights))
     return fail(MOE_B200_INVALID_ARGUMENT, "local fc1/fc2(/fc3) weights must be non-NULL");
@@ -655,9 +679,20 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
   g1.ldo = I;
   g1.err = err;
   g1.tile_counter = err + 1;
-  if (!tc_supported(g1))
-    return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc1: tensor-core path unsupported");
-  MOE_CUDA_CHECK(launch_gemm_tc(g1, device_sm_count(), 2, s), "fc1 grouped GEMM");
+  // QMoE: the code-converting pair GEMM on the received rows.  With one scale per row the
+  // codes stay exact and the scale moves to the epilogue (no row sums: the receive buffer
+  // is sized for the capacity, not the rows that arrived).
+  if (quant) {
+    set_quantized(pl, g1, t.fc1_scales, t.fc3_scales);
+    g1.qepi = p.attrs.block_size == 0 ? 1 : 0;
+    if (!tc_q_supported(g1))
+      return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel QMoE fc1: operands unsupported");
+    MOE_CUDA_CHECK(launch_gemm_tc_q(g1, device_sm_count(), s), "fc1 grouped GEMM (packed)");
+  } else {
+    if (!tc_supported(g1))
+      return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc1: tensor-core path unsupported");
+    MOE_CUDA_CHECK(launch_gemm_tc(g1, device_sm_count(), 2, s), "fc1 grouped GEMM");
+  }
   GemmArgs g2 = fc2_args(pl, t.fc2_weights, t.fc2_bias);
   g2.a = act;
   g2.rows = c->cap_rows;
@@ -674,9 +709,17 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
   g2.nseg = El * W;
   g2.remap_world = W;
   for (int d = 0; d < W; ++d) g2.out_peers[d] = c->peers.base[d] + c->lay.ret;
-  if (!tc_supported(g2))
-    return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc2: tensor-core path unsupported");
-  MOE_CUDA_CHECK(launch_gemm_tc(g2, device_sm_count(), 2, s), "fc2 grouped GEMM");
+  if (quant) {
+    set_quantized(pl, g2, t.fc2_scales, nullptr);
+    g2.qepi = g1.qepi;
+    if (!tc_q_supported(g2))
+      return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel QMoE fc2: operands unsupported");
+    MOE_CUDA_CHECK(launch_gemm_tc_q(g2, device_sm_count(), s), "fc2 grouped GEMM (packed)");
+  } else {
+    if (!tc_supported(g2))
+      return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc2: tensor-core path unsupported");
+    MOE_CUDA_CHECK(launch_gemm_tc(g2, device_sm_count(), 2, s), "fc2 grouped GEMM");
+  }
   if (!stall)
     MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpReturn, epoch, s),
                    "signal return");

@@ -22,8 +22,9 @@
 // agree.  Thread t (of the 4 sharing a row) handles the 32 consecutive codes
 // [32t, 32t+32) of a chunk and places 4 of them per MMA step in the fragment slots
 // {2t, 2t+1, 2t+8, 2t+9}; the B fragment is gathered with the same mapping:
-//   * int8, and int4 in kScaleElem: step j takes codes 32t+4j .. 32t+4j+3 in order;
-//   * int4 in the exact modes: word m (codes 8m..8m+7) is split by one mask per half2 into
+//   * int8, and int4 with per-code conversion: step j takes codes 32t+4j .. 32t+4j+3 in
+//     order (int4: (q - 8) exact, times the block scale in kScaleElem);
+//   * int4 biased codes (the default for the exact modes): word m (codes 8m..8m+7) is split by one mask per half2 into
 //     pairs (c_i, c_{i+4}) (steps 2m / 2m+1 take pairs (0,1) / (2,3), after one shift for
 //     the second); the activations come pre-arranged in that order (launch_qdec_prep).
 //     The masked words are used as they are: low nibbles read as 1024 + q and high
@@ -73,16 +74,10 @@ __device__ __forceinline__ uint32_t deq4_scaled(uint32_t byte, __half2 s2) {
   const uint32_t u = (byte & 0xFu) | ((byte & 0xF0u) << 12) | 0x64006400u;
   return h2_bits(__hmul2(__hsub2(bits_h2(u), h2c(0x6408)), s2));
 }
-// Nibbles i and i+4 of a word (after shifting it right by 4i) -> (q - 8) exact.
-__device__ __forceinline__ uint32_t deq4_pair(uint32_t shifted) {
-  const uint32_t u = (shifted & 0x000F000Fu) | 0x64006400u;
+// Codes (lo nibble, hi nibble) of one byte -> (q_lo - 8, q_hi - 8), exact in fp16.
+__device__ __forceinline__ uint32_t deq4_exact(uint32_t byte) {
+  const uint32_t u = (byte & 0xFu) | ((byte & 0xF0u) << 12) | 0x64006400u;
   return h2_bits(__hsub2(bits_h2(u), h2c(0x6408)));
-}
-// Nibbles i+1 and i+5 of the same shifted word, masked in place: 1024 + 16q, and
-// (1024 + 16q) / 16 - 72 = q - 8, exact in one fused multiply-add.
-__device__ __forceinline__ uint32_t deq4_pair_hi(uint32_t shifted) {
-  const uint32_t u = (shifted & 0x00F000F0u) | 0x64006400u;
-  return h2_bits(__hfma2(bits_h2(u), h2c(0x2C00), h2c(0xD480)));
 }
 // Biased codes of the low nibbles i, i+4 (1024 + q) and, masked in place, of the high
 // nibbles i+1, i+5 (1024 + 16 q) of a word shifted right by 4i.
@@ -265,11 +260,15 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
               const uint32_t word = w[m] >> (h * 8);  // pairs (0,4),(1,5) or (2,6),(3,7)
               lo = raw4_lo(word);
               hi = raw4_hi(word);
-            } else if (BITS == 4) {
+            } else if (BITS == 4 && kScale == kScaleElem) {
               const uint32_t word = w[m] >> (h * 16);
               const __half2 s2 = r ? s8[x] : s0[x];
               lo = deq4_scaled(word & 0xFFu, s2);
               hi = deq4_scaled((word >> 8) & 0xFFu, s2);
+            } else if (BITS == 4) {  // exact codes, scale applied to the fp32 sums
+              const uint32_t word = w[m] >> (h * 16);
+              lo = deq4_exact(word & 0xFFu);
+              hi = deq4_exact((word >> 8) & 0xFFu);
             } else if (kScale == kScaleElem) {
               const __half2 s2 = r ? s8[x] : s0[x];
               lo = deq8_scaled(w[j], 0x4140u, s2);

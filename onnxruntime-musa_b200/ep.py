@@ -15,7 +15,7 @@ routing).  One layer call:
 Optionally the tokens go through in chunks whose row all-to-alls run on NCCL's stream while
 another chunk's experts compute (off by default; see :meth:`ExpertParallelMoE.forward`).
 
-Transport "p2p" (the default for fp16/bf16 MoE) replaces steps 2-6 by the device-side
+Transport "p2p" (the default for fp16/bf16 MoE and fp16 QMoE) replaces steps 2-6 by the device-side
 exchange of the library (``moe_b200_ep_forward``): counts, rows and returned rows move by
 peer stores between IPC-shared regions, ordered by flags with bounded waits, so a layer
 call has no host synchronisation; the fc2 epilogue writes straight into the sender's
@@ -85,14 +85,16 @@ class ExpertParallelMoE:
         self.backend = backend if backend is not None else CudaBackend(pkg)
         # "p2p": device-side exchange over peer memory (moe_b200_ep_*: no host sync, no
         # collective on the data path); "collective": NCCL all-to-all around the device
-        # steps.  "auto" takes p2p for fp16/bf16 MoE on CUDA ranks with the CUDA backend.
-        p2p_ok = (backend is None and dtype in (pkg.FLOAT16, pkg.BFLOAT16)
-                  and int(attrs.get("expert_weight_bits", 0)) == 0
-                  and self.world <= 8 and torch.cuda.is_available())
+        # steps.  "auto" takes p2p for fp16/bf16 MoE and fp16 QMoE on CUDA ranks with the
+        # CUDA backend.
+        bits = int(attrs.get("expert_weight_bits", 0))
+        p2p_ok = (backend is None and self.world <= 8 and torch.cuda.is_available()
+                  and (dtype in (pkg.FLOAT16, pkg.BFLOAT16) if bits == 0
+                       else dtype == pkg.FLOAT16))
         if transport == "auto":
             transport = "p2p" if p2p_ok else "collective"
         if transport == "p2p" and not p2p_ok:
-            raise ValueError("the p2p transport needs fp16/bf16 MoE weights on CUDA ranks")
+            raise ValueError("the p2p transport needs fp16/bf16 MoE or fp16 QMoE on CUDA ranks")
         if transport not in ("p2p", "collective"):
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport

@@ -43,21 +43,29 @@ def test_ep_single_rank_matches_layer(pkg, orc, dev, dtype, transport):
     np.testing.assert_allclose(as_np(out), as_np(ref), **TOL[dtype])
 
 
-@pytest.mark.parametrize("T", [4, 400])  # decode kernels and dequantise + GEMM
-def test_ep_single_rank_qmoe(pkg, orc, dev, T):
+@pytest.mark.parametrize("transport", ["p2p", "collective"])
+@pytest.mark.parametrize("T,bits,bs", [(4, 4, 128), (400, 4, 128), (400, 8, 0), (37, 8, 0)],
+                         ids=["T4_int4_bs128", "T400_int4_bs128", "T400_int8_row", "T37_int8_row"])
+def test_ep_single_rank_qmoe(pkg, orc, dev, transport, T, bits, bs):
+    """QMoE through both transports on one rank (p2p: codes converted inside the pair GEMM
+    on the received rows; collective: the single-device QMoE steps) against the oracle."""
     from onnxruntime_musa_b200 import ep
-    q = orc.make_qmoe_inputs(T=T, H=256, I=256, E=8, k=2, bits=4, block_size=128,
-                             scale_mu=-5.0, scale_sigma=0.3, seed=T)
+    q = orc.make_qmoe_inputs(T=T, H=256, I=256, E=8, k=2, bits=bits, block_size=bs,
+                             scale_mu=-5.0 if bits == 4 else -8.5, scale_sigma=0.3, seed=T + bits)
     g = lambda n: to_dev(q[n], dev)
     attrs = q["attrs"]
     weights = dict(fc1_weights=g("fc1_q"), fc1_scales=g("fc1_scales"), fc2_weights=g("fc2_q"),
                    fc2_scales=g("fc2_scales"), fc3_weights=g("fc3_q"), fc3_scales=g("fc3_scales"))
     layer = ep.ExpertParallelMoE(pkg, num_experts=8, hidden_size=256, inter_size=256,
-                                 dtype=pkg.FLOAT16, has_fc3=True, local_weights=weights, **attrs)
+                                 dtype=pkg.FLOAT16, has_fc3=True, local_weights=weights,
+                                 transport=transport, **attrs)
+    assert layer.transport == transport
     out = layer.forward(g("x"), g("router_probs"))
     ref = orc.qmoe(q["x"], q["router_probs"], q["fc1_q"], q["fc1_scales"], None, q["fc2_q"],
                    q["fc2_scales"], None, q["fc3_q"], q["fc3_scales"], None, **attrs)
     np.testing.assert_allclose(as_np(out), ref, **TOL["float16"])
+    if hasattr(layer, "close"):
+        layer.close()
 
 
 def _free_port():
@@ -92,7 +100,10 @@ def test_ep_p2p_single_rank_ragged_calls(pkg, orc, dev):
     layer.close()
 
 
-def _nccl_worker(rank, world, port, q, transport="p2p", E=8):
+def _nccl_worker(rank, world, port, q, transport="p2p", E=8, kind="moe"):
+    """One rank of a `world`-rank expert-parallel layer over NCCL (device-side p2p exchange
+    or NCCL all-to-all).  Each rank routes its own tokens; two calls, the second ragged
+    (rank 1 sends fewer rows).  Both outputs are checked against the oracle."""
     import torch
     import torch.distributed as dist
     import __graft_entry__ as ge
@@ -104,25 +115,44 @@ def _nccl_worker(rank, world, port, q, transport="p2p", E=8):
     try:
         pkg, orc = ge.load_package(), ge.load_oracle()
         from onnxruntime_musa_b200 import ep
-        d, weights, attrs = _moe_case(orc, dev, 512, 512, 256, E, 2, 33 + E, "float16")
         T_r = 256
-        xs, ls = d["x"][rank * T_r:(rank + 1) * T_r], d["router_probs"][rank * T_r:(rank + 1) * T_r]
+        if kind == "moe":
+            d, weights, attrs = _moe_case(orc, dev, T_r * world, 512, 256, E, 2, 33 + E,
+                                          "float16")
+            h = {n: as_np(v) for n, v in d.items()}
+            ref_fn = lambda x, lg: orc.moe(x, lg, h["fc1_w"], h["fc1_b"], h["fc2_w"],
+                                           h["fc2_b"], h["fc3_w"], h["fc3_b"], **attrs)
+        else:
+            bits = 8 if kind.endswith("8") else 4
+            qi = orc.make_qmoe_inputs(T=T_r * world, H=512, I=256, E=E, k=2, bits=bits,
+                                      block_size=0 if bits == 8 else 128,
+                                      scale_mu=-8.5 if bits == 8 else -5.0,
+                                      scale_sigma=0.3, seed=44 + E)
+            g = lambda n: to_dev(qi[n], dev)
+            d = dict(x=g("x"), router_probs=g("router_probs"))
+            weights = dict(fc1_weights=g("fc1_q"), fc1_scales=g("fc1_scales"),
+                           fc2_weights=g("fc2_q"), fc2_scales=g("fc2_scales"),
+                           fc3_weights=g("fc3_q"), fc3_scales=g("fc3_scales"))
+            attrs = qi["attrs"]
+            h = {n: as_np(v) for n, v in d.items()}
+            ref_fn = lambda x, lg: orc.qmoe(x, lg, qi["fc1_q"], qi["fc1_scales"], None,
+                                            qi["fc2_q"], qi["fc2_scales"], None, qi["fc3_q"],
+                                            qi["fc3_scales"], None, **attrs)
+        sl = slice(rank * T_r, (rank + 1) * T_r)
+        xs, ls = d["x"][sl], d["router_probs"][sl]
         layer = ep.ExpertParallelMoE(pkg, num_experts=E, hidden_size=512, inter_size=256,
                                      dtype=pkg.FLOAT16, has_fc3=True,
                                      local_weights=ep.shard_experts(weights, rank, world),
                                      transport=transport, **attrs)
-        # Ragged per-rank calls: rank 1 sends fewer rows on the second call.
+        assert layer.transport == transport
         out = layer.forward(xs.contiguous(), ls.contiguous())
         T2 = T_r if rank == 0 else 100
         out2 = layer.forward(xs[:T2].contiguous(), ls[:T2].contiguous())
-        op = pkg.MoE(**attrs)
-        ref = op([xs.contiguous(), ls.contiguous(), d["fc1_w"], d["fc1_b"], d["fc2_w"],
-                  d["fc2_b"], d["fc3_w"], d["fc3_b"]])
         torch.cuda.synchronize()
-        err = np.abs(as_np(out) - as_np(ref)) - (TOL["float16"]["atol"] +
-                                                 TOL["float16"]["rtol"] * np.abs(as_np(ref)))
-        err2 = np.abs(as_np(out2) - as_np(ref)[:T2]) - (
-            TOL["float16"]["atol"] + TOL["float16"]["rtol"] * np.abs(as_np(ref)[:T2]))
+        ref = ref_fn(h["x"][sl], h["router_probs"][sl])
+        tol = lambda r: TOL["float16"]["atol"] + TOL["float16"]["rtol"] * np.abs(r)
+        err = np.abs(as_np(out) - ref) - tol(ref)
+        err2 = np.abs(as_np(out2) - ref[:T2]) - tol(ref[:T2])
         if hasattr(layer, "close"):
             layer.close()
         q.put((rank, float(max(err.max(), err2.max()))))
@@ -132,24 +162,28 @@ def _nccl_worker(rank, world, port, q, transport="p2p", E=8):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,E", [("p2p", 8), ("collective", 8), ("p2p", 2)],
-                         ids=["p2p", "collective", "p2p_one_expert_per_rank"])
-def test_ep_two_ranks(transport, E):
+@pytest.mark.parametrize("world,transport,E,kind", [
+    (2, "p2p", 8, "moe"), (2, "collective", 8, "moe"), (2, "p2p", 2, "moe"),
+    (2, "p2p", 8, "qmoe4"), (2, "p2p", 16, "qmoe8"), (2, "collective", 8, "qmoe4"),
+    (4, "p2p", 8, "moe"), (4, "p2p", 16, "qmoe8"), (8, "p2p", 64, "moe"), (8, "p2p", 16, "qmoe8")],
+    ids=lambda v: str(v))
+def test_ep_multi_rank(world, transport, E, kind):
+    """W NCCL ranks (one per GPU): outputs of every rank against the oracle."""
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, transport, E))
-             for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q, transport, E, kind))
+             for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(2))
+    res = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
-    for r in range(2):
+    for r in range(world):
         assert not isinstance(res[r], str), res[r]
         assert res[r] <= 0, f"rank {r} exceeds the fp16 tolerance by {res[r]}"
 

@@ -268,6 +268,30 @@ def test_qmoe_decode_path(pkg, orc, dev, case):
     np.testing.assert_allclose(as_np(out2), ref, **TOL["float16"])
 
 
+@pytest.mark.parametrize("case", [(1, 512, 384, 8, 2, 4, 128), (8, 512, 384, 8, 2, 4, 0),
+                                  (64, 512, 256, 8, 2, 4, 256)],
+                         ids=lambda c: f"T{c[0]}b{c[5]}bs{c[6]}")
+def test_qmoe_decode_per_code_conversion(pkg, orc, dev, case):
+    """int4 decode with the per-code conversion (MOE_B200_QDEC_RAW4=0) in the exact-code
+    modes (one scale per row, or blocks of whole 128-wide chunks): the same outputs as
+    the oracle and, within the tolerance, as the default biased-code kernel."""
+    T, H, I, E, k, bits, bs = case
+    q = orc.make_qmoe_inputs(T=T, H=H, I=I, E=E, k=k, bits=bits, block_size=bs,
+                             scale_mu=-5.0, scale_sigma=0.3, seed=T * 7 + bs)
+    attrs = dict(q["attrs"], k=k)
+    ref = orc.qmoe(q["x"], q["router_probs"], q["fc1_q"], q["fc1_scales"], None, q["fc2_q"],
+                   q["fc2_scales"], None, q["fc3_q"], q["fc3_scales"], None, **attrs)
+    default = _qmoe_run(pkg, dev, q, attrs)
+    os.environ["MOE_B200_QDEC_RAW4"] = "0"
+    try:
+        conv = _qmoe_run(pkg, dev, q, attrs)
+    finally:
+        del os.environ["MOE_B200_QDEC_RAW4"]
+    assert np.isfinite(as_np(conv)).all()
+    np.testing.assert_allclose(as_np(conv), ref, **TOL["float16"])
+    np.testing.assert_allclose(as_np(conv), as_np(default), **TOL["float16"])
+
+
 @pytest.mark.parametrize("shape", [(6, 4, 64), (300, 4, 0), (300, 8, 0), (300, 4, 64)],
                          ids=["decode_int4_bs64", "prefill_int4_rowscale", "prefill_int8_rowscale",
                               "prefill_int4_bs64"])

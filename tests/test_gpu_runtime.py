@@ -172,3 +172,44 @@ def test_kernel_compute_on_user_stream(pkg, orc, dev):
         pkg.check(L.moe_b200_notification_destroy(ev))
         pkg.check(L.moe_b200_stream_destroy(sp))
         pkg.check(L.moe_b200_stream_destroy(sc))
+
+
+_TRACE_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+import __graft_entry__ as ge
+pkg, orc = ge.load_package(), ge.load_oracle()
+inp = orc.make_moe_inputs(T=40, H=128, I=128, E=4, k=2, act="silu", gated=True,
+                          dtype="float16", seed=2)
+t = lambda a: None if a is None else torch.from_numpy(a).cuda()
+op = pkg.MoE(**inp["attrs"])
+for _ in range(2):
+    op([t(inp["x"]), t(inp["router_probs"]), t(inp["fc1_w"]), None, t(inp["fc2_w"]), None,
+        t(inp["fc3_w"]), None])
+torch.cuda.synchronize()
+op.release()
+"""
+
+
+def test_kernel_trace_lines(dev):
+    """MOE_B200_TRACE_KERNELS prints CREATE / BEGIN / END / RELEASE lines per kernel
+    object (the reference's MUSA_EP_TRACE_KERNELS), END carrying the status; with
+    MOE_B200_TRACE_SYNC each compute is synchronised before END."""
+    import os
+    import pathlib
+    import subprocess
+    import sys
+    root = str(pathlib.Path(__file__).resolve().parents[1])
+    env = dict(os.environ, MOE_B200_TRACE_KERNELS="1", MOE_B200_TRACE_SYNC="1")
+    r = subprocess.run([sys.executable, "-c", _TRACE_SCRIPT, root], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stderr.splitlines() if ln.startswith("MOE_B200_KERNEL_")]
+    kinds = [ln.split()[0] for ln in lines]
+    assert kinds == ["MOE_B200_KERNEL_CREATE", "MOE_B200_KERNEL_BEGIN", "MOE_B200_KERNEL_END",
+                     "MOE_B200_KERNEL_BEGIN", "MOE_B200_KERNEL_END",
+                     "MOE_B200_KERNEL_RELEASE"], lines
+    impl = {ln.split()[2] for ln in lines}
+    assert len(impl) == 1, lines
+    assert all(ln.endswith("status=0") for ln in lines if "KERNEL_END" in ln), lines
+    assert all(" MoE " in ln for ln in lines), lines
