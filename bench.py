@@ -606,8 +606,22 @@ def bench_ep(args, cfg, rank, world, dev):
     g = torch.Generator(device=dev).manual_seed(7000 + rank)
     T, H, E = cfg["T"], cfg["H"], cfg["E"]
     L["x"] = torch.randn(T, H, device=dev, generator=g).to(L["x"].dtype)
-    L["router_probs"] = torch.randn(T, E, device=dev, generator=g).to(L["router_probs"].dtype)
+    logits = torch.randn(T, E, device=dev, generator=g)
+    if cfg.get("zipf"):  # the same per-expert bias on every rank (seeded as make_layer's)
+        import numpy as np
+        z = np.random.default_rng(20261202).zipf(1.1, E).astype(np.float64)
+        span = z.max() - z.min()
+        bias_e = 3.0 * (z - z.min()) / span if span > 0 else np.zeros(E)
+        logits = logits + torch.tensor(bias_e, device=dev, dtype=torch.float32)[None, :]
+    L["router_probs"] = logits.to(L["router_probs"].dtype)
     out = torch.empty_like(L["x"])
+    # Load per rank: routed rows each rank's experts receive from all ranks (one routing
+    # pass outside the timed region); imbalance = max over ranks / mean.
+    ridx, _ = pkg.route(L["router_probs"], cfg["k"], 1)
+    per_rank = torch.bincount((ridx.long() // (E // world)).flatten(), minlength=world)
+    dist.all_reduce(per_rank)
+    loads = [int(v) for v in per_rank.cpu()]
+    imbalance = max(loads) / (sum(loads) / world)
     prob, tens, inputs, op_attrs, op_type = problem_and_tensors(pkg, cfg, L, out)
     names = ["fc1_weights", "fc1_scales", "fc1_bias", "fc2_weights", "fc2_scales", "fc2_bias",
              "fc3_weights", "fc3_scales", "fc3_bias"]
@@ -670,6 +684,7 @@ def bench_ep(args, cfg, rank, world, dev):
         "config": {"workload": cfg["desc"].format(T=T), "global_batch": T * world,
                    "tokens_per_gpu": T, "parallelism": f"ep{world}", "ep_chunks": chunks,
                    "ep_transport": layer.transport,
+                   "rows_per_rank": loads, "imbalance_max_over_mean": round(imbalance, 4),
                    "l2": "inputs larger than L2 (weights streamed every step)"},
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": hx.numel() * es + hl.numel() * es,

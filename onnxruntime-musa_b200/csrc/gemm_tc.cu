@@ -234,6 +234,13 @@ __device__ __forceinline__ void q_scale_cols(float (&v)[n], const __half* scales
   }
 }
 
+// Scale of output column `col` of expert e (stored-row addressing), for the swapped tiles.
+__device__ __forceinline__ float q_scale_at(const __half* scales, int rows_e, int G, int g,
+                                            int noff, int e, int col) {
+  return __half2float(__ldg(scales + static_cast<int64_t>(e) * rows_e +
+                            static_cast<int64_t>(col + noff) * G + g));
+}
+
 template <typename T>
 __device__ __forceinline__ void epilogue_rows(const TcParams& p, uint32_t taddr, int row,
                                               bool valid, int e, int n0, int c0, int c1,
@@ -555,6 +562,11 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
     const int slot = (q & 1) * 2 + half;
     float* buf = x.buf + slot * 16 * 32;
     const float own_bias = lin ? bias_val<T>(p.bias3, t.e, fc, p) : bias_val<T>(p.bias1, t.e, fc, p);
+    // qepi 1 (exact codes, one scale per output column): scale, then bias.
+    const float own_scale =
+        !p.qepi ? 1.f
+        : lin   ? q_scale_at(p.scales3, p.b3_rows, p.b3_G, p.b3_g, p.b3_noff, t.e, fc)
+                : q_scale_at(p.scales1, p.b1_rows, p.b1_G, p.b1_g, p.b1_noff, t.e, fc);
 #pragma unroll 1
     for (int c = c_first; c < t.nt; c += 32, ++xuse) {
       const uint32_t par = xuse & 1;
@@ -564,7 +576,7 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
       if (lin) {
         if (!mbar_wait(&x.empty[slot], par ^ 1)) return false;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) buf[j * 32 + lane] = v[j] + own_bias;
+        for (int j = 0; j < 16; ++j) buf[j * 32 + lane] = v[j] * own_scale + own_bias;
         mbar_arrive(&x.full[slot]);
       } else {
         if (!mbar_wait(&x.full[slot], par)) return false;
@@ -573,7 +585,7 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
         for (int j = 0; j < 16; ++j) u[j] = buf[j * 32 + lane];
         mbar_arrive(&x.empty[slot]);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] += own_bias;
+        for (int j = 0; j < 16; ++j) v[j] = v[j] * own_scale + own_bias;
         act_gated_chunk<16>(p.ap, v, u);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -586,6 +598,9 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
     const int f = t.n * BN + rank * (BN / 2) + q * 32 + lane;
     const bool fok = f < p.N;
     const float b = bias_val<T>(p.bias1, t.e, min(f, p.N - 1), p);
+    const float sc = p.qepi ? q_scale_at(p.scales1, p.b1_rows, p.b1_G, p.b1_g, p.b1_noff, t.e,
+                                         min(f, p.N - 1))
+                            : 1.f;
 #pragma unroll 1
     for (int c = c_first; c < t.nt; c += 32) {
       float v[16];
@@ -596,7 +611,7 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
       const unsigned long long my_row =
           my_tok < t.rows ? reinterpret_cast<unsigned long long>(out_row<T>(p, t.r0 + my_tok)) : 0ull;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] += b;
+      for (int j = 0; j < 16; ++j) v[j] = v[j] * sc + b;
       act_chunk<16>(p.ap.act, v);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -1422,6 +1437,20 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
   p.nseg = g.nseg;
   p.remap_world = g.remap_world;
   for (int i = 0; i < kMaxEpRanks; ++i) p.out_peers[i] = g.out_peers[i];
+  // Weights holding exact integer codes with one fp16 scale per output row (qepi 1): the
+  // epilogues scale the fp32 sums.  Biased codes (qepi 2) exist only in the packed kernel.
+  if (g.qepi == 2 || (g.qepi == 1 && (g.dtype != kDtF16 || g.b1.scales == nullptr ||
+                                      (g.gated && g.b3.scales == nullptr))))
+    return cudaErrorInvalidValue;
+  p.qepi = g.qepi;
+  if (g.qepi) {
+    p.scales1 = static_cast<const __half*>(g.b1.scales);
+    p.scales3 = static_cast<const __half*>(g.gated ? g.b3.scales : g.b1.scales);
+    p.b1_G = g.b1.G;
+    p.b3_G = g.gated ? g.b3.G : 1;
+    p.b1_rows = g.b1.n_rows;
+    p.b3_rows = g.gated ? g.b3.n_rows : g.b1.n_rows;
+  }
   p.a_src = gather ? g.gather_src : nullptr;
   p.a_k = gather ? g.gather_k : 1;
   const char* trace_path = pair ? std::getenv("MOE_B200_GEMM_TRACE") : nullptr;

@@ -294,6 +294,8 @@ cudaError_t run_gemm(GemmArgs& g, cudaStream_t s) {
     if (env_flag("MOE_B200_PAIR_STATIC")) g.tile_counter = nullptr;
     return launch_gemm_tc(g, device_sm_count(), mode, s);
   }
+  // The FFMA kernels apply no per-row scales: exact-code weights need the tensor cores.
+  if (g.qepi != 0) return cudaErrorInvalidValue;
   return launch_gemm_simt(g, s);
 }
 
@@ -489,7 +491,11 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   // MOE_B200_TEST_STALL=1 (tests only): the GEMM producers issue no loads, the kernel's
   // bounded waits expire and the call reports the device error instead of hanging.
   g1.test_stall = env_flag("MOE_B200_TEST_STALL") ? 1 : 0;
-  if (fused_q) set_quantized(p, g1, t.fc1_scales, t.fc3_scales);
+  // Dequantised copies holding exact codes: the epilogue applies the per-row scales.
+  const bool row_scaled = !fused_q && p.attrs.expert_weight_bits != 0 &&
+                          qmoe_dequantized_exact(p);
+  if (fused_q || row_scaled) set_quantized(p, g1, t.fc1_scales, t.fc3_scales);
+  if (row_scaled) g1.qepi = 1;
   // Per-row scales (block_size 0): the scale moves to the epilogue.  int8 codes go to the
   // tensor cores biased (1024 + q) and the epilogue subtracts (1024 + 128) * rowsum: the
   // constant part is ~15x the signal (|q - 128| ~ 74), within what the fp32 accumulation
@@ -502,7 +508,7 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
     const char* v = std::getenv("MOE_B200_QGEMM_EPI");
     qepi = v != nullptr ? std::atoi(v) : (p.attrs.expert_weight_bits == 8 ? 2 : 1);
   }
-  g1.qepi = qepi;
+  if (fused_q) g1.qepi = qepi;
   g1.rowsum = qepi == 2 ? rowsum : nullptr;
   mark(kStFc1);
   if (fused_q) {
@@ -526,8 +532,8 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   g2.err = err;
   g2.tile_counter = err + 2;
   g2.test_stall = g1.test_stall;
-  if (fused_q) set_quantized(p, g2, t.fc2_scales, nullptr);
-  g2.qepi = qepi;
+  if (fused_q || row_scaled) set_quantized(p, g2, t.fc2_scales, nullptr);
+  g2.qepi = row_scaled ? 1 : qepi;
   g2.rowsum = qepi == 2 ? rowsum : nullptr;
   mark(kStFc2);
   if (fused_q) {

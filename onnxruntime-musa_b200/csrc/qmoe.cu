@@ -22,9 +22,9 @@ dequant_vec8_kernel(const uint8_t* __restrict__ q, const T* __restrict__ scales,
        gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = gi / groups_per_row;
     const int k0 = static_cast<int>(gi - r * groups_per_row) * 8;
-    const float s = block_size == 0
-                        ? to_f(scales[r])
-                        : to_f(scales[r * num_blocks + k0 / block_size]);
+    const float s = scales == nullptr ? 1.f
+                    : block_size == 0  ? to_f(scales[r])
+                                       : to_f(scales[r * num_blocks + k0 / block_size]);
     float v[8];
     if (kBits == 4) {
       const uint32_t word =
@@ -64,7 +64,9 @@ dequant_scalar_kernel(const uint8_t* __restrict__ q, const T* __restrict__ scale
     } else {
       code = static_cast<int>(q[r * row_bytes + c]) - 128;
     }
-    const float s = block_size == 0 ? to_f(scales[r]) : to_f(scales[r * num_blocks + c / block_size]);
+    const float s = scales == nullptr ? 1.f
+                    : block_size == 0  ? to_f(scales[r])
+                                       : to_f(scales[r * num_blocks + c / block_size]);
     out[i] = from_f<T>(static_cast<float>(code) * s);
   }
 }
@@ -322,6 +324,10 @@ size_t qmoe_workspace_bytes(const moe_b200_problem& p) {
   return qmoe_dequantized_bytes(p);
 }
 
+bool qmoe_dequantized_exact(const moe_b200_problem& p) {
+  return p.attrs.expert_weight_bits != 0 && p.attrs.block_size == 0 && p.dtype == kDtF16;
+}
+
 size_t qmoe_dequantized_bytes(const moe_b200_problem& p) {
   const size_t es = dtype_bytes(p.dtype);
   const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
@@ -340,12 +346,18 @@ int qmoe_dequantize_into(const moe_b200_problem& p, const moe_b200_tensors& t, u
   uint8_t* w1 = dst;
   uint8_t* w2 = w1 + align256(E * fc1_rows(p) * H * es);
   uint8_t* w3 = w2 + align256(E * H * I * es);
-  cudaError_t st = dequant(p.dtype, t.fc1_weights, t.fc1_scales, E * fc1_rows(p),
+  // Per-row scales: the copies hold the exact codes (q - zero point) and the GEMM
+  // epilogues apply the scale to the fp32 sums, so the weights carry no fp16 rounding.
+  const bool exact = qmoe_dequantized_exact(p);
+  auto sc = [&](const void* scales) { return exact ? nullptr : scales; };
+  cudaError_t st = dequant(p.dtype, t.fc1_weights, sc(t.fc1_scales), E * fc1_rows(p),
                            static_cast<int>(H), bits, bs, w1, s);
   if (st == cudaSuccess)
-    st = dequant(p.dtype, t.fc2_weights, t.fc2_scales, E * H, static_cast<int>(I), bits, bs, w2, s);
+    st = dequant(p.dtype, t.fc2_weights, sc(t.fc2_scales), E * H, static_cast<int>(I), bits, bs,
+                 w2, s);
   if (st == cudaSuccess && p.has_fc3)
-    st = dequant(p.dtype, t.fc3_weights, t.fc3_scales, E * I, static_cast<int>(H), bits, bs, w3, s);
+    st = dequant(p.dtype, t.fc3_weights, sc(t.fc3_scales), E * I, static_cast<int>(H), bits, bs,
+                 w3, s);
   if (st != cudaSuccess) return MOE_B200_EP_FAIL;
   out->w1 = w1;
   out->w2 = w2;

@@ -43,6 +43,10 @@ int qmoe_decode_combine(const moe_b200_problem& p, const moe_b200_tensors& t, co
 // each matrix 256-byte aligned).
 size_t qmoe_dequantized_bytes(const moe_b200_problem& p);
 
+// True when the dequantised copies hold exact codes (q - zero point) and the scale, one per
+// output row, is left to the GEMM epilogue (fp16 QMoE with block_size 0).
+bool qmoe_dequantized_exact(const moe_b200_problem& p);
+
 // Dequantises fc1/fc2(/fc3) of every expert into `dst` (qmoe_dequantized_bytes(p) bytes).
 int qmoe_dequantize_into(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* dst,
                          QmoeDequantOut* out, cudaStream_t s);
