@@ -248,6 +248,33 @@ int moe_b200_device_count(int32_t* count);
 int moe_b200_device_props_get(int32_t device_id, moe_b200_device_props* props);
 int moe_b200_set_device(int32_t device_id);
 
+/* Provider options of one session, parsed from the option key/value strings the
+ * session carries (ParseMusaProviderOptionsFromSession + ValidateMusaProviderOptions,
+ * musa/ep/src/ep_factory.cc:106-202, and the session entry
+ * ep.musa.enable_prepack_weight_sharing read in CreateEpImpl, :472-478).  Keys:
+ * device_id, has_user_compute_stream, user_compute_stream (a cudaStream_t address in
+ * decimal or 0x-hex; "", "0" and "nullptr" mean none), use_ep_level_unified_stream,
+ * do_copy_in_default_stream, ep.musa.enable_prepack_weight_sharing, and the
+ * expert-parallel keys ep_world_size / ep_rank.  Unknown keys are ignored (they belong
+ * to other providers).  Integers must be whole decimal strings; the flags must be 0 or
+ * 1; device_id >= 0; a user stream implies has_user_compute_stream = 1 and
+ * use_ep_level_unified_stream = 1.  Any violation returns INVALID_ARGUMENT naming the
+ * option. */
+typedef struct moe_b200_provider_options {
+  int32_t device_id;                     /* default 0 */
+  int32_t has_user_compute_stream;       /* default 0 */
+  void* user_compute_stream;             /* default NULL */
+  int32_t use_ep_level_unified_stream;   /* default 0 */
+  int32_t do_copy_in_default_stream;     /* default 1 */
+  int32_t enable_prepack_weight_sharing; /* default 0 */
+  int32_t ep_world_size;                 /* default 1 */
+  int32_t ep_rank;                       /* default 0 */
+} moe_b200_provider_options;
+
+int moe_b200_provider_options_parse(int32_t num_options, const char* const* keys,
+                                    const char* const* values,
+                                    moe_b200_provider_options* options);
+
 /* Allocator (musa/ep/src/ep_allocator.h:86-321). */
 int moe_b200_alloc(size_t bytes, void** ptr);
 int moe_b200_free(void* ptr);

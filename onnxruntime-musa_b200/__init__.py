@@ -87,6 +87,15 @@ class TensorRef(ctypes.Structure):
                 ("rank", ctypes.c_int32), ("dims", ctypes.c_int64 * 4)]
 
 
+class ProviderOptions(ctypes.Structure):
+    _fields_ = [("device_id", ctypes.c_int32), ("has_user_compute_stream", ctypes.c_int32),
+                ("user_compute_stream", ctypes.c_void_p),
+                ("use_ep_level_unified_stream", ctypes.c_int32),
+                ("do_copy_in_default_stream", ctypes.c_int32),
+                ("enable_prepack_weight_sharing", ctypes.c_int32),
+                ("ep_world_size", ctypes.c_int32), ("ep_rank", ctypes.c_int32)]
+
+
 class DeviceProps(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 256), ("vendor_id", ctypes.c_uint32),
                 ("device_id", ctypes.c_int32), ("sm_count", ctypes.c_int32),
@@ -155,6 +164,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "moe_b200_device_count": (ctypes.c_int, [_PI32]),
     "moe_b200_device_props_get": (ctypes.c_int, [_I32, ctypes.POINTER(DeviceProps)]),
     "moe_b200_set_device": (ctypes.c_int, [_I32]),
+    "moe_b200_provider_options_parse": (ctypes.c_int, [_I32, ctypes.POINTER(ctypes.c_char_p),
+                                                       ctypes.POINTER(ctypes.c_char_p),
+                                                       ctypes.POINTER(ProviderOptions)]),
     "moe_b200_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP)]),
     "moe_b200_free": (ctypes.c_int, [_VP]),
     "moe_b200_alloc_pinned": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP)]),
@@ -249,6 +261,20 @@ def make_provider_options(*, device_id: int = 0, user_compute_stream: Any = None
             raise ValueError("ep_world_size >= 1 and 0 <= ep_rank < ep_world_size required")
         opts.update(ep_world_size=str(ep_world_size), ep_rank=str(ep_rank))
     return opts
+
+
+def parse_provider_options(options: Mapping[str, str]) -> dict[str, Any]:
+    """The session's provider options as the library parses them
+    (``moe_b200_provider_options_parse``): defaults filled in, validated, the user stream
+    implying the unified stream.  Raises InvalidArgument on a malformed option."""
+    keys = [str(k).encode() for k in options]
+    vals = [str(v).encode() for v in options.values()]
+    n = len(keys)
+    ak = (ctypes.c_char_p * max(n, 1))(*keys)
+    av = (ctypes.c_char_p * max(n, 1))(*vals)
+    o = ProviderOptions()
+    check(lib().moe_b200_provider_options_parse(n, ak, av, ctypes.byref(o)))
+    return {name: getattr(o, name) for name, _ in ProviderOptions._fields_}
 
 
 # --------------------------------------------------------------------- devices

@@ -8,6 +8,7 @@
 // allocation, the role of DeferredDeviceFreeQueue / AllocateDeviceMemoryOnStream
 // (kernels/shared_inc/kernel_memory.h:67-252).
 #include <cerrno>
+#include <cstdint>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -446,6 +447,90 @@ int moe_b200_kernel_release(moe_b200_kernel* kern) {
     kern->pk = nullptr;
   }
   delete kern;
+  return MOE_B200_OK;
+}
+
+// ------------------------------------------------------------- provider options
+namespace {
+
+bool parse_whole_int(const char* v, int32_t* out) {
+  if (v == nullptr || *v == '\0') return false;
+  char* end = nullptr;
+  errno = 0;
+  const long x = std::strtol(v, &end, 10);
+  if (errno != 0 || end == v || *end != '\0' || x < INT32_MIN || x > INT32_MAX) return false;
+  *out = static_cast<int32_t>(x);
+  return true;
+}
+
+}  // namespace
+
+int moe_b200_provider_options_parse(int32_t num_options, const char* const* keys,
+                                    const char* const* values,
+                                    moe_b200_provider_options* o) {
+  if (o == nullptr || num_options < 0 || (num_options > 0 && (keys == nullptr || values == nullptr)))
+    return (efail(MOE_B200_INVALID_ARGUMENT, "options, keys and values must be non-NULL"));
+  moe_b200_provider_options r{};
+  r.do_copy_in_default_stream = 1;
+  r.ep_world_size = 1;
+  struct IntKey { const char* name; int32_t* dst; };
+  const IntKey ints[] = {{"device_id", &r.device_id},
+                         {"has_user_compute_stream", &r.has_user_compute_stream},
+                         {"use_ep_level_unified_stream", &r.use_ep_level_unified_stream},
+                         {"do_copy_in_default_stream", &r.do_copy_in_default_stream},
+                         {"ep_world_size", &r.ep_world_size},
+                         {"ep_rank", &r.ep_rank}};
+  for (int i = 0; i < num_options; ++i) {
+    const char* k = keys[i];
+    const char* v = values[i] != nullptr ? values[i] : "";
+    if (k == nullptr) return (efail(MOE_B200_INVALID_ARGUMENT, "option key %d is NULL", i));
+    bool known = false;
+    for (const IntKey& ik : ints) {
+      if (std::strcmp(k, ik.name) != 0) continue;
+      known = true;
+      if (!parse_whole_int(v, ik.dst))
+        return (efail(MOE_B200_INVALID_ARGUMENT,
+                      "Invalid provider option '%s': expected integer, got '%s'.", k, v));
+    }
+    if (known) continue;
+    if (!std::strcmp(k, "user_compute_stream")) {
+      if (*v == '\0' || !std::strcmp(v, "0") || !std::strcmp(v, "nullptr")) {
+        r.user_compute_stream = nullptr;
+        continue;
+      }
+      char* end = nullptr;
+      errno = 0;
+      const unsigned long long x = std::strtoull(v, &end, 0);
+      if (errno != 0 || end == v || *end != '\0')
+        return (efail(MOE_B200_INVALID_ARGUMENT,
+                      "Invalid provider option 'user_compute_stream': expected uintptr_t "
+                      "string, got '%s'.", v));
+      r.user_compute_stream = reinterpret_cast<void*>(static_cast<uintptr_t>(x));
+    } else if (!std::strcmp(k, "ep.musa.enable_prepack_weight_sharing")) {
+      r.enable_prepack_weight_sharing = std::strcmp(v, "1") == 0 ? 1 : 0;  // "1" enables
+    }
+  }
+  if (r.user_compute_stream != nullptr) r.has_user_compute_stream = 1;
+  if (r.device_id < 0)
+    return (efail(MOE_B200_INVALID_ARGUMENT,
+                  "Provider option 'device_id' must be a non-negative integer."));
+  const IntKey flags[] = {{"has_user_compute_stream", &r.has_user_compute_stream},
+                          {"use_ep_level_unified_stream", &r.use_ep_level_unified_stream},
+                          {"do_copy_in_default_stream", &r.do_copy_in_default_stream}};
+  for (const IntKey& f : flags)
+    if (*f.dst != 0 && *f.dst != 1)
+      return (efail(MOE_B200_INVALID_ARGUMENT,
+                    "Invalid provider option '%s': expected 0 or 1, got %d.", f.name, *f.dst));
+  if (r.has_user_compute_stream && r.user_compute_stream == nullptr)
+    return (efail(MOE_B200_INVALID_ARGUMENT,
+                  "Provider option 'has_user_compute_stream' is set but "
+                  "'user_compute_stream' is null."));
+  if (r.has_user_compute_stream) r.use_ep_level_unified_stream = 1;
+  if (r.ep_world_size < 1 || r.ep_rank < 0 || r.ep_rank >= r.ep_world_size)
+    return (efail(MOE_B200_INVALID_ARGUMENT,
+                  "ep_world_size >= 1 and 0 <= ep_rank < ep_world_size required (got %d / %d)",
+                  r.ep_world_size, r.ep_rank));
+  *o = r;
   return MOE_B200_OK;
 }
 

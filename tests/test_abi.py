@@ -320,3 +320,34 @@ def test_kernel_compute_rejects_bad_inputs_on_the_host(pkg):
         assert _compute(pkg, q, specs, (T, H), F16) == NI
     finally:
         q.release()
+
+
+def test_provider_options_parse(pkg):
+    """The C++ option parser: defaults, the user-stream rules and the validation
+    messages of the reference's ParseMusaProviderOptionsFromSession."""
+    d = pkg.parse_provider_options({})
+    assert d == dict(device_id=0, has_user_compute_stream=0, user_compute_stream=None,
+                     use_ep_level_unified_stream=0, do_copy_in_default_stream=1,
+                     enable_prepack_weight_sharing=0, ep_world_size=1, ep_rank=0)
+    d = pkg.parse_provider_options(pkg.make_provider_options(device_id=3,
+                                                             user_compute_stream=0x7f00))
+    assert d["device_id"] == 3 and d["user_compute_stream"] == 0x7f00
+    assert d["has_user_compute_stream"] == 1 and d["use_ep_level_unified_stream"] == 1
+    d = pkg.parse_provider_options({"user_compute_stream": "0x10", "other.key": "x",
+                                    "ep.musa.enable_prepack_weight_sharing": "1",
+                                    "ep_world_size": "4", "ep_rank": "3",
+                                    "do_copy_in_default_stream": "0"})
+    assert d["user_compute_stream"] == 16 and d["has_user_compute_stream"] == 1
+    assert d["enable_prepack_weight_sharing"] == 1 and d["do_copy_in_default_stream"] == 0
+    assert (d["ep_world_size"], d["ep_rank"]) == (4, 3)
+    assert pkg.parse_provider_options({"user_compute_stream": "nullptr"})[
+        "user_compute_stream"] is None
+    bad = [({"device_id": "-1"}, "non-negative"), ({"device_id": "1x"}, "expected integer"),
+           ({"device_id": ""}, "expected integer"), ({"device_id": "99999999999"}, "integer"),
+           ({"do_copy_in_default_stream": "2"}, "expected 0 or 1"),
+           ({"has_user_compute_stream": "1"}, "is null"),
+           ({"user_compute_stream": "abc"}, "uintptr_t"),
+           ({"ep_world_size": "2", "ep_rank": "2"}, "ep_rank")]
+    for opts, msg in bad:
+        with pytest.raises(pkg.InvalidArgument, match=msg):
+            pkg.parse_provider_options(opts)
