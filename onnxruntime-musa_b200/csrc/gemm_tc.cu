@@ -96,6 +96,13 @@ struct TcParams {
   // four rows per lane of the producer warp); nullptr = A rows p of the map's tensor.
   const int32_t* a_src;
   int a_k;
+  // Fused routing-weighted combine (GemmArgs.comb_*; comb_cnt == nullptr: off).
+  unsigned* comb_cnt;
+  const int32_t* comb_src;
+  const int32_t* comb_pos;
+  const float* comb_w;
+  void* comb_out;
+  int comb_k;
 };
 
 // Per-tile phase trace of CTA 0 (diagnostics only).  Entry i: [2i] = %globaltimer ns,
@@ -234,6 +241,68 @@ __device__ __forceinline__ void q_scale_cols(float (&v)[n], const __half* scales
   }
 }
 
+// Fused combine of the (token, 32-column segment) items a warp completed: item (s, l) for
+// each bit l of masks[s], token = lane l's `tok`, columns col_base + s * 32 + [0, 32).
+// Four lanes take an item (8 columns each, one 16-byte load per slot row), eight items per
+// pass; each sums the token's k fc2 rows, read from L2 (other CTAs wrote them), in slot
+// order in fp32, exactly as the separate combine kernel sums them.
+template <typename T, int S>
+__device__ __forceinline__ void combine_items(const TcParams& p, const unsigned (&masks)[S],
+                                              int tok, int col_base, int lane) {
+  int total = 0;
+#pragma unroll
+  for (int s = 0; s < S; ++s) total += __popc(masks[s]);
+  const int k = p.comb_k;
+  const T* y = static_cast<const T*>(p.out);
+#pragma unroll 1
+  for (int it0 = 0; it0 < total; it0 += 8) {
+    const int it = it0 + (lane >> 2);
+    int s_sel = -1, l_sel = 0, rem = it;
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      const int c = __popc(masks[s]);
+      if (s_sel < 0 && it < total) {
+        if (rem < c) {
+          s_sel = s;
+          l_sel = static_cast<int>(__fns(masks[s], 0, rem + 1));
+        } else {
+          rem -= c;
+        }
+      }
+    }
+    const int t = __shfl_sync(0xffffffffu, tok, l_sel);
+    const int col = col_base + s_sel * 32 + (lane & 3) * 8;
+    if (s_sel < 0 || col >= p.N) continue;
+    const int32_t* pos = p.comb_pos + static_cast<int64_t>(t) * k;
+    const float* w = p.comb_w + static_cast<int64_t>(t) * k;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int j = 0; j < k; ++j) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(
+          y + static_cast<int64_t>(__ldg(pos + j)) * p.ldo + col));
+      const T* e = reinterpret_cast<const T*>(&v);
+      const float wj = __ldg(w + j);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += wj * to_f(e[q]);
+    }
+    uint4 o;
+    o.x = pack2<T>(acc[0], acc[1]);
+    o.y = pack2<T>(acc[2], acc[3]);
+    o.z = pack2<T>(acc[4], acc[5]);
+    o.w = pack2<T>(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(static_cast<T*>(p.comb_out) + static_cast<int64_t>(t) * p.N + col) = o;
+  }
+}
+
+// One arrival of permuted row `row` at 32-column segment `seg` (after the caller's
+// stores of that segment and a device-scope fence): true when it completes the token's
+// k rows, the caller then owns the segment's combine.
+__device__ __forceinline__ bool combine_arrive(const TcParams& p, int row, int seg, int& tok) {
+  tok = __ldg(p.comb_src + row) / p.comb_k;
+  unsigned* c = p.comb_cnt + static_cast<int64_t>(tok) * ((p.N + 31) / 32) + seg;
+  return atomicAdd(c, 1u) == static_cast<unsigned>(p.comb_k - 1);
+}
+
 // Scale of output column `col` of expert e (stored-row addressing), for the swapped tiles.
 __device__ __forceinline__ float q_scale_at(const __half* scales, int rows_e, int G, int g,
                                             int noff, int e, int col) {
@@ -299,6 +368,30 @@ __device__ __forceinline__ void epilogue_rows(const TcParams& p, uint32_t taddr,
     }
     __syncwarp();
   }
+}
+
+// Fused combine after a row tile's stores (called once the tile's TMEM accumulator is
+// released, so the MMA of the next tile overlaps it): publish the warp's stores of rows
+// [32] x columns [n0 + c0, n0 + c1), count each row's arrival at every 32-column segment
+// (one lane's atomics are independent and overlap), and combine the segments this warp
+// completed.
+template <typename T>
+__device__ __forceinline__ void combine_rows(const TcParams& p, int row, bool valid, int n0,
+                                             int c0, int c1, int lane) {
+  __threadfence();
+  __syncwarp();
+  constexpr int kSeg = BN / 2 / 32;  // a warp's columns: half of an (ungated) tile
+  unsigned masks[kSeg];
+  int tok = 0;
+#pragma unroll
+  for (int i = 0; i < kSeg; ++i) {
+    const int c = c0 + i * 32;
+    const bool last = valid && c < c1 && n0 + c < p.N && combine_arrive(p, row, (n0 + c) / 32, tok);
+    masks[i] = __ballot_sync(0xffffffffu, last);
+  }
+  __threadfence();
+  combine_items<T, kSeg>(p, masks, tok, n0 + c0, lane);
+  __syncwarp();
 }
 
 // Column range of epilogue warp `w` (2..9): warps 2..5 take the first half of the
@@ -477,6 +570,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (p.comb_cnt != nullptr) combine_rows<T>(p, row, valid, n * BN, ec0, ec1, lane);
     }
   }
 
@@ -617,6 +711,20 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
       for (int j = 0; j < 16; ++j) {
         T* row = reinterpret_cast<T*>(__shfl_sync(0xffffffffu, my_row, j));
         if (fok && c + j < t.rows) row[f] = from_f<T>(v[j]);
+      }
+      if (p.comb_cnt != nullptr) {
+        // Rows c .. c+15 of this warp's 32 columns are stored: lane j < 16 counts row c + j's
+        // arrival at the segment and, if it completes it, combines it.
+        __threadfence();
+        __syncwarp();
+        const int seg_col = t.n * BN + rank * (BN / 2) + q * 32;
+        int tok = 0;
+        const bool done = lane < 16 && c + lane < t.rows && seg_col < p.N &&
+                          combine_arrive(p, t.r0 + c + lane, seg_col / 32, tok);
+        const unsigned masks[1] = {__ballot_sync(0xffffffffu, done)};
+        __threadfence();
+        combine_items<T, 1>(p, masks, tok, seg_col, lane);
+        __syncwarp();
       }
     }
   }
@@ -939,6 +1047,9 @@ tc_pair_grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
       __syncwarp();
       if (warp == 2 && lane == 0) trace(p, kTrEpiDone, L);
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      if (p.comb_cnt != nullptr && !t.nt)
+        combine_rows<T>(p, t.r0 + r_in_tile, t.r0 + r_in_tile < t.r0 + t.rows, t.n * BN, ec0,
+                        ec1, lane);
     }
   }
 
@@ -1451,6 +1562,14 @@ cudaError_t launch_t(const GemmArgs& g, int num_sms, bool pair, cudaStream_t s) 
     p.b1_rows = g.b1.n_rows;
     p.b3_rows = g.gated ? g.b3.n_rows : g.b1.n_rows;
   }
+  if (g.comb_cnt != nullptr && (g.gated || g.seg_start != nullptr || g.N % 8 != 0))
+    return cudaErrorInvalidValue;
+  p.comb_cnt = g.comb_cnt;
+  p.comb_src = g.comb_src;
+  p.comb_pos = g.comb_pos;
+  p.comb_w = g.comb_w;
+  p.comb_out = g.comb_out;
+  p.comb_k = g.comb_k;
   p.a_src = gather ? g.gather_src : nullptr;
   p.a_k = gather ? g.gather_k : 1;
   const char* trace_path = pair ? std::getenv("MOE_B200_GEMM_TRACE") : nullptr;

@@ -106,8 +106,11 @@ bool is_float_type(int dt) {
 // ------------------------------------------------------------ workspace plan
 struct WsLayout {
   size_t idx, w, chunk_counts, chunk_base, offsets, tiles128, tiles64, tiles256, pos, src, err;
-  size_t rowsum, xp, act, qmoe, total;
+  size_t rowsum, comb, xp, act, qmoe, total;
 };
+
+// Smallest inter_size (fc2's K) at which the combine runs inside the fc2 epilogue.
+constexpr int64_t kFusedCombineMinInter = 4096;
 
 bool swiglu_fused(const moe_b200_problem& p) {
   return p.attrs.activation_type == MOE_B200_ACT_SWIGLU && p.attrs.swiglu_fusion != 0;
@@ -134,6 +137,7 @@ WsLayout plan_workspace(const moe_b200_problem& p, bool prepacked = false) {
   L.src = take(R * 4);
   L.err = take(16);
   L.rowsum = take(R * 4);                // A row sums of the packed (QMoE) GEMMs
+  L.comb = take(T * ((p.hidden_size + 31) / 32) * 4);  // fused-combine arrival counters
   L.xp = take(R * p.hidden_size * es);   // gathered input, later fc2 output
   L.act = take(R * p.inter_size * es);
   L.qmoe = take(prepacked ? 0 : qmoe_workspace_bytes(p));
@@ -535,6 +539,29 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   if (fused_q || row_scaled) set_quantized(p, g2, t.fc2_scales, nullptr);
   g2.qepi = row_scaled ? 1 : qepi;
   g2.rowsum = qepi == 2 ? rowsum : nullptr;
+  // Combine fused into the fc2 epilogue: the epilogue counts the arrivals of each token's
+  // k rows per 32-column segment and the completing one sums them into the output, so no
+  // separate combine pass runs.  It pays where fc2's tiles are long enough (K = inter_size)
+  // for the MMA to hide the epilogue's extra reads: C2 (I = 14336) 2.51 -> 2.46 ms per
+  // layer; at C4 (I = 768, k = 8) the epilogue was already as long as the MMA and fc2 grew
+  // by more than the 0.12 ms combine pass.  MOE_B200_FUSED_COMBINE=0/1 forces it.
+  const char* fc_env = std::getenv("MOE_B200_FUSED_COMBINE");
+  const bool fuse_wanted = fc_env != nullptr ? (fc_env[0] != '\0' && std::strcmp(fc_env, "0") != 0)
+                                             : p.inter_size >= kFusedCombineMinInter;
+  const bool fuse_combine = !fused_q && p.num_rows > 0 && fuse_wanted &&
+                            !env_flag("MOE_B200_FORCE_SIMT") && tc_supported(g2) &&
+                            H % 8 == 0;
+  if (fuse_combine) {
+    g2.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb);
+    g2.comb_src = src;
+    g2.comb_pos = pos;
+    g2.comb_w = w;
+    g2.comb_out = t.output;
+    g2.comb_k = k;
+    MOE_CUDA_CHECK(cudaMemsetAsync(ws + L.comb, 0,
+                                   static_cast<size_t>(T) * ((H + 31) / 32) * 4, s),
+                   "combine counters");
+  }
   mark(kStFc2);
   if (fused_q) {
     if (!tc_q_supported(g2))
@@ -546,7 +573,8 @@ int forward_impl(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* 
   }
 
   mark(kStCombine);
-  MOE_CUDA_CHECK(launch_combine(p.dtype, xp, pos, w, T, k, H, t.output, s), "combine");
+  if (!fuse_combine)
+    MOE_CUDA_CHECK(launch_combine(p.dtype, xp, pos, w, T, k, H, t.output, s), "combine");
   mark(kNumStages);
 
   if (env_flag("MOE_B200_TRACE_SYNC")) {

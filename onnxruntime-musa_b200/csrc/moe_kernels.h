@@ -149,6 +149,18 @@ struct GemmArgs {
   const int32_t* gather_src = nullptr;
   int gather_k = 1;
   int64_t gather_x_rows = 0;
+  // fc2 with the routing-weighted combine fused into the epilogue (plain, ungated GEMM on
+  // the single-device path): after storing its part of an output row (permuted row p,
+  // token comb_src[p] / comb_k) in `out`, the epilogue counts one arrival per (token,
+  // 32-column segment) in comb_cnt (zeroed, [tokens, N / 32]); the arrival that completes
+  // the k rows of a segment sums them in slot order, w[t,j] * Y[pos[t,j]], into
+  // comb_out[t] (fp32 accumulation, the order of the separate combine kernel).
+  unsigned* comb_cnt = nullptr;
+  const int32_t* comb_src = nullptr;
+  const int32_t* comb_pos = nullptr;
+  const float* comb_w = nullptr;
+  void* comb_out = nullptr;
+  int comb_k = 1;
 };
 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t s);

@@ -519,3 +519,39 @@ def test_gather_fused_into_pair_gemm(pkg, orc, dev, dtype_name, case):
                 os.environ[n] = v
     np.testing.assert_array_equal(as_np(fused), as_np(plain))
     np.testing.assert_allclose(as_np(fused), oracle_out(orc, h, attrs), **TOL[dtype_name])
+
+
+@pytest.mark.parametrize("case", [
+    (300, 256, 384, 8, 2, "silu", True, False, "float16"),
+    (1000, 512, 256, 16, 4, "gelu", False, True, "bfloat16"),
+    (5, 128, 128, 64, 8, "silu", True, True, "float16"),        # swapped tail tiles only
+    (700, 256, 520, 4, 1, "relu", True, False, "bfloat16"),     # k = 1
+    (2048, 1024, 768, 64, 8, "silu", True, False, "float16"),   # C4-like, Zipf-free
+    (3000, 520, 256, 8, 2, "silu", True, False, "float16"),     # H not a multiple of 32
+], ids=lambda c: f"T{c[0]}H{c[1]}I{c[2]}E{c[3]}k{c[4]}{c[8]}")
+def test_combine_fused_into_fc2_epilogue(pkg, orc, dev, case):
+    """MOE_B200_FUSED_COMBINE=1: the fc2 epilogue combines each token's k rows (arrival
+    count per 32-column segment, the completing row sums them in slot order).  Outputs
+    are bit-identical to the separate combine kernel's, deterministic across calls, and
+    within the tolerance of the oracle, for both tensor-core kernels."""
+    import torch
+    T, H, I, E, k, act, gated, bias, dtype_name = case
+    inp = orc.make_moe_inputs(T=T, H=H, I=I, E=E, k=k, act=act, gated=gated, dtype="float32",
+                              bias=bias, normalize=1, seed=T + E + 5)
+    d, h = moe_inputs_on(dev, inp, dtype_name)
+    ref = run_moe(pkg, d, inp["attrs"])
+    for mode in ("1", "2"):
+        os.environ["MOE_B200_FUSED_COMBINE"] = "1"
+        os.environ["MOE_B200_TC_MODE"] = mode
+        try:
+            out1 = run_moe(pkg, d, inp["attrs"])
+            out2 = run_moe(pkg, d, inp["attrs"])
+            os.environ["MOE_B200_FUSED_COMBINE"] = "0"
+            plain = run_moe(pkg, d, inp["attrs"])
+        finally:
+            del os.environ["MOE_B200_FUSED_COMBINE"]
+            del os.environ["MOE_B200_TC_MODE"]
+        assert torch.equal(out1, out2), "fused combine is not deterministic"
+        assert torch.equal(out1, plain), f"mode {mode}: fused combine differs from the combine kernel"
+    np.testing.assert_allclose(as_np(out1), oracle_out(orc, h, inp["attrs"]), **TOL[dtype_name])
+    assert torch.equal(ref, plain)
