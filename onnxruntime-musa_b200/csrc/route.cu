@@ -63,10 +63,20 @@ __device__ __forceinline__ void sparse_mixer_row(const float (&v)[kPerLane], int
   }
 }
 
+// Order-preserving map of fp32 bits to uint32 (larger float -> larger key; NaN is never
+// passed) and its inverse.
+__device__ __forceinline__ uint32_t float_key(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Lane l's logits of one row (l, l + 32, ...), fp32; NaN and absent experts read -inf.
 template <typename T, int kPerLane>
-__device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int k, int normalize,
-                                          int lane, int& my_idx, float& my_w) {
-  float v[kPerLane];
+__device__ __forceinline__ void load_row(const T* __restrict__ row, int E, int lane,
+                                         float (&v)[kPerLane]) {
 #pragma unroll
   for (int j = 0; j < kPerLane; ++j) {
     const int e = lane + 32 * j;
@@ -77,45 +87,59 @@ __device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int 
     }
     v[j] = x;
   }
+}
+
+// Routing of one row from its logits in registers (see route_row).
+template <int kPerLane>
+__device__ __forceinline__ void route_vals(const float (&v)[kPerLane], int E, int k,
+                                           int normalize, int lane, int& my_idx, float& my_w) {
   if (normalize == kRouteSparseMixer) {
     my_idx = 0;
     my_w = 0.f;
     sparse_mixer_row<kPerLane>(v, E, lane, my_idx, my_w);
     return;
   }
-  // Row max and softmax denominator (fixed butterfly order: deterministic).
-  float m = v[0];
+  // Selection runs on order-preserving unsigned keys of the fp32 logits (-0 read as +0,
+  // so equal values have equal keys): one warp max-reduction finds the largest remaining
+  // value and one min-reduction the lowest expert index holding it (ties -> lower index),
+  // the rule of the reference TopK.  The softmax denominator of the full row (only for
+  // normalize == 0) keeps a fixed butterfly order: deterministic.
+  uint32_t key[kPerLane];
 #pragma unroll
-  for (int j = 1; j < kPerLane; ++j) m = fmaxf(m, v[j]);
+  for (int j = 0; j < kPerLane; ++j) key[j] = float_key(v[j] + 0.0f);
+  float s = 0.f, m = 0.f;
+  if (!normalize) {
+    uint32_t km = key[0];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  float s = 0.f;
+    for (int j = 1; j < kPerLane; ++j) km = max(km, key[j]);
+    m = key_float(__reduce_max_sync(0xffffffffu, km));
 #pragma unroll
-  for (int j = 0; j < kPerLane; ++j)
-    if (lane + 32 * j < E) s += expf(v[j] - m);
+    for (int j = 0; j < kPerLane; ++j)
+      if (lane + 32 * j < E) s += expf(v[j] - m);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  }
 
   uint32_t taken = 0;  // bit j: v[j] already selected
   float top_val = 0.f, sel_sum = 0.f, my_val = 0.f;
   my_idx = 0;
   for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
+    uint32_t bk = 0;
     int bi = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < kPerLane; ++j) {
       const int e = lane + 32 * j;
-      if (e < E && !(taken & (1u << j)) && (v[j] > bv || (v[j] == bv && e < bi))) {
-        bv = v[j];
+      // Strictly greater (or the first valid): among this lane's equal keys the lowest
+      // index, which comes first, stays.
+      if (e < E && !(taken & (1u << j)) && (bi == 0x7fffffff || key[j] > bk)) {
+        bk = key[j];
         bi = e;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
+    const uint32_t wk = __reduce_max_sync(0xffffffffu, bi == 0x7fffffff ? 0u : bk);
+    bi = static_cast<int>(__reduce_min_sync(
+        0xffffffffu, (bi != 0x7fffffff && bk == wk) ? static_cast<uint32_t>(bi) : 0x7fffffffu));
+    const float bv = key_float(wk);
     if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
     if (r == 0) top_val = bv;
     const float ex = normalize ? expf(bv - top_val) : expf(bv - m);
@@ -125,9 +149,20 @@ __device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int 
   my_w = normalize ? my_val / sel_sum : my_val / s;
 }
 
+template <typename T, int kPerLane>
+__device__ __forceinline__ void route_row(const T* __restrict__ row, int E, int k, int normalize,
+                                          int lane, int& my_idx, float& my_w) {
+  float v[kPerLane];
+  load_row<T, kPerLane>(row, E, lane, v);
+  route_vals<kPerLane>(v, E, k, normalize, lane, my_idx, my_w);
+}
+
+// Threads of a routing CTA: 16 warps share a chunk's rows (more rows in flight per SM).
+constexpr int kRouteKernelThreads = 512;
+
 // One warp per row, `chunk` rows per CTA; also the CTA's expert histogram.
 template <typename T, int kPerLane>
-__global__ void __launch_bounds__(kRouteThreads)
+__global__ void __launch_bounds__(kRouteKernelThreads)
 route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int normalize,
              int32_t* __restrict__ expert_idx, float* __restrict__ route_w,
              int32_t* __restrict__ chunk_counts, int chunk, int* __restrict__ clear) {
@@ -140,10 +175,20 @@ route_kernel(const T* __restrict__ logits, int num_rows, int E, int k, int norma
   const int warp = threadIdx.x >> 5;
   const int row0 = blockIdx.x * chunk;
   const int row_end = min(row0 + chunk, num_rows);
-  for (int t = row0 + warp; t < row_end; t += kRouteThreads / 32) {
+  constexpr int kStride = kRouteKernelThreads / 32;
+  // The next row's logits load while this row is routed (hides the load latency).
+  float vn[kPerLane];
+  if (row0 + warp < row_end)
+    load_row<T, kPerLane>(logits + static_cast<int64_t>(row0 + warp) * E, E, lane, vn);
+  for (int t = row0 + warp; t < row_end; t += kStride) {
+    float v[kPerLane];
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) v[j] = vn[j];
+    if (t + kStride < row_end)
+      load_row<T, kPerLane>(logits + static_cast<int64_t>(t + kStride) * E, E, lane, vn);
     int my_idx;
     float w;
-    route_row<T, kPerLane>(logits + static_cast<int64_t>(t) * E, E, k, normalize, lane, my_idx, w);
+    route_vals<kPerLane>(v, E, k, normalize, lane, my_idx, w);
     if (lane < k) {
       expert_idx[static_cast<int64_t>(t) * k + lane] = my_idx;
       route_w[static_cast<int64_t>(t) * k + lane] = w;
@@ -231,6 +276,7 @@ histogram_kernel(const int32_t* __restrict__ expert_idx, int num_rows, int k, in
 }
 
 // ---------------------------------------------------------------------- scan
+constexpr int kScanParts = 16;  // most threads per expert in the column scan
 // Single CTA.  Column scan over chunks per expert (chunk_base), then an exclusive
 // scan over experts (expert_offsets) and the prefix of 128-row and 64-row tile
 // counts used by the grouped-GEMM schedulers.
@@ -241,15 +287,32 @@ scan_kernel(const int32_t* __restrict__ chunk_counts, int num_chunks, int E,
             int32_t* __restrict__ tiles256) {
   pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
   pdl_launch_dependents();
-  extern __shared__ int32_t s_cnt[];  // [E]
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+  extern __shared__ int32_t s_cnt[];  // [E], then [kScanParts][E] part sums
+  // P threads per expert (P = blockDim / E rounded down to a power of two, <= 16) each
+  // sum a contiguous range of chunks (independent loads), then write that range's running
+  // bases from the exclusive prefix of the earlier parts.
+  int P = 1;
+  while (P * 2 * E <= static_cast<int>(blockDim.x) && P < kScanParts) P *= 2;
+  int32_t* s_part = s_cnt + E;
+  const int e = threadIdx.x / P, part = threadIdx.x % P;
+  const int per = (num_chunks + P - 1) / P;
+  const int c0 = min(num_chunks, part * per), c1 = min(num_chunks, c0 + per);
+  int32_t sum = 0;
+  if (e < E) {
+#pragma unroll 8
+    for (int c = c0; c < c1; ++c) sum += chunk_counts[static_cast<int64_t>(c) * E + e];
+    s_part[part * E + e] = sum;
+  }
+  __syncthreads();
+  if (e < E) {
     int32_t run = 0;
-    for (int c = 0; c < num_chunks; ++c) {
+    for (int q = 0; q < part; ++q) run += s_part[q * E + e];
+    for (int c = c0; c < c1; ++c) {
       const int64_t i = static_cast<int64_t>(c) * E + e;
       chunk_base[i] = run;
       run += chunk_counts[i];
     }
-    s_cnt[e] = run;
+    if (part == P - 1) s_cnt[e] = run;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -448,13 +511,13 @@ static cudaError_t launch_route_t(const void* logits, int T_, int E, int k, int 
   const T* l = static_cast<const T*>(logits);
   const int per_lane = (E + 31) / 32;
   if (per_lane <= 1)
-    route_kernel<T, 1><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
+    route_kernel<T, 1><<<chunks, kRouteKernelThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   else if (per_lane <= 2)
-    route_kernel<T, 2><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
+    route_kernel<T, 2><<<chunks, kRouteKernelThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   else if (per_lane <= 4)
-    route_kernel<T, 4><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
+    route_kernel<T, 4><<<chunks, kRouteKernelThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   else
-    route_kernel<T, 8><<<chunks, kRouteThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
+    route_kernel<T, 8><<<chunks, kRouteKernelThreads, sm, s>>>(l, T_, E, k, normalize, idx, w, chunk_counts, chunk, clear);
   return cudaGetLastError();
 }
 
@@ -512,7 +575,8 @@ cudaError_t launch_plan(const int32_t* idx, int T_, int k, int E, const int32_t*
                         int32_t* tiles64, int32_t* tiles256, int32_t* pos, int32_t* src,
                         cudaStream_t s, int chunk) {
   const int chunks = num_route_chunks(T_, chunk);
-  cudaError_t st = launch_dependent(pdl_layer_enabled(), scan_kernel, dim3(1), dim3(1024), E * sizeof(int32_t), s,
+  cudaError_t st = launch_dependent(pdl_layer_enabled(), scan_kernel, dim3(1), dim3(1024),
+                                    (1 + kScanParts) * E * sizeof(int32_t), s,
                                     chunk_counts, chunks, E, chunk_base, offsets, tiles128,
                                     tiles64, tiles256);
   if (st != cudaSuccess || T_ == 0) return st;
