@@ -652,6 +652,29 @@ def bench_ep(args, cfg, rank, world, dev):
     chunks = args.ep_chunks or 1
     with ClockSampler(dev.index) as clk:
         ms = timed(lambda: layer.forward(x, lg, chunks=chunks))
+    # Per-phase device times of the p2p exchange (a second run of `steps` calls with phase
+    # events on the stream, no synchronisation between calls): median per rank, then the
+    # max over ranks per phase.
+    phase_ms = None
+    if layer.transport == "p2p":
+        n_ev = len(pkg.EP_PHASES) + 1
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+               for _ in range(args.steps)]
+        for row in evs:
+            for ev in row:
+                ev.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        for row in evs:
+            layer.forward(x, lg, events=row)
+        torch.cuda.synchronize(dev)
+        med = torch.tensor([statistics.median(row[i].elapsed_time(row[i + 1]) for row in evs)
+                            for i in range(n_ev - 1)], dtype=torch.float64, device=dev)
+        every = [torch.empty_like(med) for _ in range(world)]
+        dist.all_gather(every, med)
+        phase_ms = {name: {"max_over_ranks": round(max(float(e[i]) for e in every), 4),
+                           "per_rank": [round(float(e[i]), 4) for e in every]}
+                    for i, name in enumerate(pkg.EP_PHASES)}
     hx, hl = x.cpu().pin_memory(), lg.cpu().pin_memory()
     hout = torch.empty_like(hx).pin_memory()
     # End to end: every step copies its tokens and logits from pinned host memory and its
@@ -699,6 +722,7 @@ def bench_ep(args, cfg, rank, world, dev):
         # permute, gather, fc1, fc2, un-permute) + combine
         # p2p: route, scan, permute, counts, send, signal, wait, fc1, fc2, signal, wait,
         # combine; collective: 13 per chunk
+        "ep_phase_ms": phase_ms,
         "gpu_launches": (12 if layer.transport == "p2p" else 13 * chunks) * args.steps,
         "clocks": clk.summary(),
     }

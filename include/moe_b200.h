@@ -353,6 +353,16 @@ int moe_b200_ep_forward(moe_b200_ep_comm* comm, const moe_b200_problem* problem,
                         const moe_b200_tensors* t, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* moe_b200_ep_forward that also records the caller's CUDA events (num_events >= 9; NULL
+ * entries skipped) on `stream` at the phase boundaries: events[i] .. events[i+1] brackets
+ * route + plan, count exchange, row sends, wait for rows, fc1, fc2 with the return
+ * stores, wait for the returned rows, combine.  A measurement aid; no counterpart in the
+ * reference. */
+int moe_b200_ep_forward_staged(moe_b200_ep_comm* comm, const moe_b200_problem* problem,
+                               const moe_b200_tensors* t, void* workspace,
+                               size_t workspace_bytes, void* stream, void* const* events,
+                               int32_t num_events);
+
 /* ------------------------------------------------ host-buffer call pipeline */
 
 /* Calls of one layer on host-resident input, router logits and output (weights stay on

@@ -134,6 +134,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                                   ctypes.POINTER(_SZ)]),
     "moe_b200_ep_forward": (ctypes.c_int, [_VP, ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
                                            _VP, _SZ, _VP]),
+    "moe_b200_ep_forward_staged": (ctypes.c_int, [_VP, ctypes.POINTER(Problem),
+                                                  ctypes.POINTER(Tensors), _VP, _SZ, _VP,
+                                                  ctypes.POINTER(_VP), _I32]),
     "moe_b200_norm_router": (ctypes.c_int, [_I32, _I64, _I64, _I64, _VP, _VP, _VP,
                                             ctypes.c_float, _VP, _VP, _VP, _VP, _VP]),
     "moe_b200_pipeline_create": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Tensors),
@@ -584,6 +587,11 @@ def forward_staged(problem: Problem, tensors: Mapping[str, Any], workspace, even
                                         _stream_handle(stream), handles, len(events)))
 
 
+# Phases of one device-side expert-parallel call (moe_b200_ep_forward_staged).
+EP_PHASES = ("route_plan", "counts", "send_rows", "wait_rows", "fc1", "fc2_return",
+             "wait_return", "combine")
+
+
 class EpComm:
     """This rank's region of the device-side expert-parallel exchange
     (``moe_b200_ep_comm_*``).  ``handle()`` is exported to the other ranks, whose handles
@@ -621,6 +629,19 @@ class EpComm:
         check(lib().moe_b200_ep_forward(self._h, ctypes.byref(problem), ctypes.byref(t),
                                         workspace.data_ptr(), workspace.numel(),
                                         _stream_handle(stream)))
+
+    def forward_staged(self, problem: Problem, tensors: Mapping[str, Any], workspace, events,
+                       stream=None):
+        """``forward`` recording ``events`` (EP_PHASES + 1 timing events, each recorded
+        once before) at the phase boundaries, without synchronising."""
+        t = Tensors()
+        for name, _ in Tensors._fields_:
+            v = tensors.get(name)
+            setattr(t, name, None if v is None else (v if isinstance(v, int) else v.data_ptr()))
+        handles = (_VP * len(events))(*[None if ev is None else ev.cuda_event for ev in events])
+        check(lib().moe_b200_ep_forward_staged(self._h, ctypes.byref(problem), ctypes.byref(t),
+                                               workspace.data_ptr(), workspace.numel(),
+                                               _stream_handle(stream), handles, len(events)))
 
     def close(self) -> None:
         if self._h:

@@ -446,4 +446,21 @@ int moe_b200_ep_forward(moe_b200_ep_comm* c, const moe_b200_problem* problem,
                               static_cast<cudaStream_t>(stream));
 }
 
+int moe_b200_ep_forward_staged(moe_b200_ep_comm* c, const moe_b200_problem* problem,
+                               const moe_b200_tensors* t, void* workspace,
+                               size_t workspace_bytes, void* stream, void* const* events,
+                               int32_t num_events) {
+  moe::clear_stale_cuda_error();
+  if (c == nullptr || problem == nullptr || t == nullptr || events == nullptr ||
+      num_events < moe::kEpNumPhases + 1)
+    return moe::set_error(MOE_B200_INVALID_ARGUMENT,
+                          "comm, problem, tensors non-NULL and >= %d events required",
+                          moe::kEpNumPhases + 1);
+  if (!c->connected) return moe::set_error(MOE_B200_INVALID_ARGUMENT, "comm is not connected");
+  cudaEvent_t ev[moe::kEpNumPhases + 1];
+  for (int i = 0; i <= moe::kEpNumPhases; ++i) ev[i] = static_cast<cudaEvent_t>(events[i]);
+  return moe::ep_forward_impl(c, *problem, *t, static_cast<uint8_t*>(workspace), workspace_bytes,
+                              static_cast<cudaStream_t>(stream), ev);
+}
+
 }  // extern "C"

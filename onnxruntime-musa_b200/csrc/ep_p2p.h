@@ -72,7 +72,8 @@ struct moe_b200_ep_comm {
 
 namespace moe {
 // Layer call of the device-side expert-parallel path (moe_api.cu).
+constexpr int kEpNumPhases = 8;
 int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b200_tensors& t,
-                    uint8_t* ws, size_t ws_bytes, cudaStream_t s);
+                    uint8_t* ws, size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev = nullptr);
 size_t ep_workspace_bytes(const moe_b200_ep_comm* c, const moe_b200_problem& p);
 }  // namespace moe

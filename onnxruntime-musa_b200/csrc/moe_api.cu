@@ -635,7 +635,10 @@ size_t ep_workspace_bytes(const moe_b200_ep_comm* c, const moe_b200_problem& p) 
 // FFN on the received rows with the fc2 epilogue storing into the senders' return
 // buffers, combine.  Local weights: [E / W, ...].  No host synchronisation.
 int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b200_tensors& t,
-                    uint8_t* ws, size_t ws_bytes, cudaStream_t s) {
+                    uint8_t* ws, size_t ws_bytes, cudaStream_t s, cudaEvent_t* ev) {
+  // Phase boundaries (kEpNumPhases + 1 events when `ev` is non-NULL): route+plan, counts,
+  // send rows, wait rows, fc1, fc2 (with the return stores), wait return, combine.
+  auto mark = [&](int i) { if (ev && ev[i]) cudaEventRecord(ev[i], s); };
   const int W = c->world, E = c->num_experts, El = E / W, r = c->rank;
   moe_b200_problem global = p;  // routing is over all E experts (k <= E, not E / W)
   global.num_experts = E;
@@ -673,6 +676,7 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
   const int chunk = layer_route_chunk(T);
   const size_t es = dtype_bytes(p.dtype);
 
+  mark(0);
   // Route and plan over all E experts (expert-ordered rows of this rank's tokens).
   MOE_CUDA_CHECK(launch_route(p.dtype, t.router_probs, T, E, k,
                               route_mode(p), i32(L.idx),
@@ -685,9 +689,11 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
                    "plan");
   const EpTables tab{i32(L.send_base), i32(L.eoff), i32(L.rt128), i32(L.rt64), i32(L.rt256),
                      i32(L.seg_start), i32(L.seg_dst)};
+  mark(1);
   MOE_CUDA_CHECK(launch_ep_exchange_counts(c->peers, c->lay, r, W, E, epoch,
                                            T > 0 ? i32(L.myoff) : nullptr, tab, err, s),
                  "count exchange");
+  mark(2);
   MOE_CUDA_CHECK(launch_ep_send_rows(c->peers, c->lay, W, E, t.input, static_cast<int64_t>(H) * es,
                                      k, i32(L.idx), i32(L.src), R, tab.send_base, err, s),
                  "send rows");
@@ -696,8 +702,10 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
   const bool stall = env_flag("MOE_B200_TEST_STALL");
   if (!stall)
     MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpRows, epoch, s), "signal rows");
+  mark(3);
   MOE_CUDA_CHECK(launch_ep_wait(c->sym, c->lay, W, kEpRows, epoch, err, s), "wait rows");
 
+  mark(4);
   // Expert FFN on the received rows (row count known on the device only: the GEMMs are
   // sized for the communicator's capacity and schedule from the device offsets).
   void* act = ws + L.act;
@@ -727,6 +735,7 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
       return fail(MOE_B200_NOT_IMPLEMENTED, "expert-parallel fc1: tensor-core path unsupported");
     MOE_CUDA_CHECK(launch_gemm_tc(g1, device_sm_count(), 2, s), "fc1 grouped GEMM");
   }
+  mark(5);
   GemmArgs g2 = fc2_args(pl, t.fc2_weights, t.fc2_bias);
   g2.a = act;
   g2.rows = c->cap_rows;
@@ -757,10 +766,13 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
   if (!stall)
     MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpReturn, epoch, s),
                    "signal return");
+  mark(6);
   MOE_CUDA_CHECK(launch_ep_wait(c->sym, c->lay, W, kEpReturn, epoch, err, s), "wait return");
+  mark(7);
   MOE_CUDA_CHECK(launch_combine(p.dtype, c->sym + c->lay.ret, i32(L.pos),
                                 reinterpret_cast<float*>(ws + L.w), T, k, H, t.output, s),
                  "combine");
+  mark(8);
   if (env_flag("MOE_B200_TRACE_SYNC")) {
     MOE_CUDA_CHECK(cudaStreamSynchronize(s), "stream synchronize");
     int herr = 0;

@@ -130,6 +130,9 @@ int decode_splits(const moe_b200_problem& p, int64_t N, int64_t K) {
   const int64_t target = 148 * 4 * 8;  // 8 waves of 4 warps per SM
   const int s = static_cast<int>((target + tiles - 1) / tiles);
   const int chunks = static_cast<int>(K / 128);
+  // MOE_B200_QDEC_SPLITS fixes the split count (measurement runs).
+  if (const char* v = std::getenv("MOE_B200_QDEC_SPLITS"))
+    return std::max(1, std::min({std::atoi(v), kQmoeMaxSplits, chunks}));
   return std::max(1, std::min({s, kQmoeMaxSplits, chunks}));
 }
 int fc1_splits(const moe_b200_problem& p) { return decode_splits(p, p.inter_size, p.hidden_size); }

@@ -48,7 +48,10 @@ constexpr int QD_WARPS = 4;
 constexpr int QD_CHUNK = 128;
 // Stages of the per-warp ring: 6 for int4 and 3 for int8 (the same bytes in flight), sized
 // so four CTAs fit on one SM.
-template <int BITS> constexpr int qd_stages() { return BITS == 4 ? 6 : 3; }
+// Stages of the per-warp ring: 6 for int4 and 3 for int8 (the same bytes in flight), sized
+// so four CTAs fit on one SM.  (Shallower rings at 5-6 CTAs per SM for the one-group
+// passes measured slower: C3 T=1 0.0955 -> 0.1015 ms, C5 T=1 0.067 -> 0.074 ms.)
+template <int BITS, int NGMAX> constexpr int qd_stages() { return BITS == 4 ? 6 : 3; }
 
 enum ScaleMode { kScaleRow = 0, kScaleChunk = 1, kScaleElem = 2 };
 
@@ -81,11 +84,25 @@ __device__ __forceinline__ uint32_t deq4_exact(uint32_t byte) {
 }
 // Biased codes of the low nibbles i, i+4 (1024 + q) and, masked in place, of the high
 // nibbles i+1, i+5 (1024 + 16 q) of a word shifted right by 4i.
-__device__ __forceinline__ uint32_t raw4_lo(uint32_t shifted) {
-  return (shifted & 0x000F000Fu) | 0x64006400u;
+// One three-input logic op each, (shifted & mask) | bias, with the bias 0x64006400 held in
+// a register (`bias`, see opaque_bias): with both constants as immediates the compiler
+// emitted two logic ops per conversion (the instruction takes one immediate), which
+// doubled the kernel's logic-op count.
+__device__ __forceinline__ uint32_t raw4_lo(uint32_t shifted, uint32_t bias) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(shifted), "n"(0x000F000F), "r"(bias));
+  return d;
 }
-__device__ __forceinline__ uint32_t raw4_hi(uint32_t shifted) {
-  return (shifted & 0x00F000F0u) | 0x64006400u;
+__device__ __forceinline__ uint32_t raw4_hi(uint32_t shifted, uint32_t bias) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(shifted), "n"(0x00F000F0), "r"(bias));
+  return d;
+}
+// 0x64006400 in a register the compiler cannot fold back into an immediate.
+__device__ __forceinline__ uint32_t opaque_bias() {
+  uint32_t b;
+  asm volatile("mov.b32 %0, 0x64006400;" : "=r"(b));
+  return b;
 }
 // Bytes of a word selected by `sel` -> (b - 128) exact, optionally scaled.
 __device__ __forceinline__ uint32_t deq8(uint32_t word, uint32_t sel) {
@@ -113,7 +130,7 @@ __device__ __forceinline__ int64_t stored_row(const QOperand& b, int e, int n, i
          b.g;
 }
 
-template <int BITS, int NG, bool GATED, int kScale, bool RAW4>
+template <int BITS, int NG, bool GATED, int kScale, bool RAW4, int STAGES>
 __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_begin, int cnt,
                                          int tok0, int n0, int c_begin, int c_end, int split,
                                          uint8_t* ring) {
@@ -192,13 +209,94 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
 
   __syncwarp();
 #pragma unroll
-  for (int st = 0; st < qd_stages<BITS>() - 1; ++st) {
+  for (int st = 0; st < STAGES - 1; ++st) {
     if (c_begin + st < c_end) issue(c_begin + st, st);
     cp_async_commit();
   }
+  // Ring slots of the chunk consumed and of the chunk issued, and the block-scale index of
+  // the chunk (kScaleChunk: a block spans cpb whole chunks), advanced without divisions.
+  int stage = 0, stage_next = STAGES - 1;
+  const int cpb = kScale == kScaleChunk ? a.block_size / QD_CHUNK : 1;
+  int sblk = kScale == kScaleChunk ? c_begin / cpb : 0;
+  int ssub = kScale == kScaleChunk ? c_begin - sblk * cpb : 0;
+  // The next chunk's activations (and offset terms, and chunk scales) load while this chunk
+  // computes: they come from L2, and a load issued just before its use would stall the warp
+  // for a full L2 round trip every chunk.
+  [[maybe_unused]] const uint32_t bias6400 = opaque_bias();
+  // One-group passes only: wider passes hold too many registers for a second copy.
+  constexpr bool kPf = NG == 1;
+  constexpr int M = QD_CHUNK / 32;
+  uint4 xnext[M][NG];
+  float onext[NG][2];
+  float fnext0[NT], fnext8[NT];
+  auto load_x = [&](int cc) {
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi)
+        xnext[m][gi] = tok_ok[gi]
+                           ? __ldg(reinterpret_cast<const uint4*>(xrow[gi] + cc * QD_CHUNK + 8 * m))
+                           : make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (kRaw4) {
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        onext[gi][0] = __ldg(crow[gi][0] + cc);
+        onext[gi][1] = __ldg(crow[gi][1] + cc);
+      }
+    }
+  };
+  auto load_scales = [&](int si) {
+    if constexpr (kScale == kScaleChunk) {
+#pragma unroll
+      for (int x = 0; x < NT; ++x) {
+        fnext0[x] = __half2float(sc0[x][si]);
+        fnext8[x] = __half2float(sc8[x][si]);
+      }
+    }
+  };
+  if (kPf && c_begin < c_end) {
+    load_x(c_begin);
+    load_scales(sblk);
+  }
   for (int c = c_begin; c < c_end; ++c) {
-    const int stage = (c - c_begin) % qd_stages<BITS>();
-    cp_async_wait<qd_stages<BITS>() - 2>();
+    if (!kPf) {
+      if constexpr (kRaw4) {
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          onext[gi][0] = __ldg(crow[gi][0] + c);
+          onext[gi][1] = __ldg(crow[gi][1] + c);
+        }
+      }
+      load_scales(sblk);
+    }
+    uint4 xcur[M][NG];
+    float ocur[NG][2];
+    float fcur0[NT], fcur8[NT];
+    if constexpr (kPf) {
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) xcur[m][gi] = xnext[m][gi];
+    }
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) {
+      ocur[gi][0] = onext[gi][0];
+      ocur[gi][1] = onext[gi][1];
+    }
+#pragma unroll
+    for (int x = 0; x < NT; ++x) {
+      fcur0[x] = fnext0[x];
+      fcur8[x] = fnext8[x];
+    }
+    if (kScale == kScaleChunk && ++ssub == cpb) {
+      ssub = 0;
+      ++sblk;
+    }
+    if (kPf && c + 1 < c_end) {
+      load_x(c + 1);
+      load_scales(sblk);
+    }
+    cp_async_wait<STAGES - 2>();
     __syncwarp();
     const uint8_t* sb = ring + stage * STAGE;
     uint4 code[NT][2][BITS / 4];  // [tile][row g / g+8][16-byte words]
@@ -213,8 +311,10 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
       }
     }
     __syncwarp();
-    if (c + qd_stages<BITS>() - 1 < c_end) issue(c + qd_stages<BITS>() - 1, (c - c_begin + qd_stages<BITS>() - 1) % qd_stages<BITS>());
+    if (c + STAGES - 1 < c_end) issue(c + STAGES - 1, stage_next);
     cp_async_commit();
+    stage_next = stage_next + 1 == STAGES ? 0 : stage_next + 1;
+    stage = stage + 1 == STAGES ? 0 : stage + 1;
 
     __half2 s0[NT], s8[NT];
     if (kScale == kScaleElem) {
@@ -244,8 +344,9 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
       uint4 xv[NG];
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi)
-        xv[gi] = tok_ok[gi] ? __ldg(reinterpret_cast<const uint4*>(xrow[gi] + c * QD_CHUNK + 8 * m))
-                            : make_uint4(0u, 0u, 0u, 0u);
+        xv[gi] = kPf ? xcur[m][gi]
+             : (tok_ok[gi] ? __ldg(reinterpret_cast<const uint4*>(xrow[gi] + c * QD_CHUNK + 8 * m))
+                           : make_uint4(0u, 0u, 0u, 0u));
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int j = 2 * m + h;
@@ -258,8 +359,8 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
             uint32_t lo, hi;
             if (kRaw4) {
               const uint32_t word = w[m] >> (h * 8);  // pairs (0,4),(1,5) or (2,6),(3,7)
-              lo = raw4_lo(word);
-              hi = raw4_hi(word);
+              lo = raw4_lo(word, bias6400);
+              hi = raw4_hi(word, bias6400);
             } else if (BITS == 4 && kScale == kScaleElem) {
               const uint32_t word = w[m] >> (h * 16);
               const __half2 s2 = r ? s8[x] : s0[x];
@@ -303,7 +404,7 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
     if constexpr (kRaw4) {
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) {
-        const float o0 = __ldg(crow[gi][0] + c), o1 = __ldg(crow[gi][1] + c);
+        const float o0 = ocur[gi][0], o1 = ocur[gi][1];
 #pragma unroll
         for (int x = 0; x < NT; ++x) {
           float* d = kScale == kScaleChunk ? part[x < PX ? x : 0][gi < PG ? gi : 0] : acc[x][gi];
@@ -315,10 +416,9 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
       }
     }
     if (kScale == kScaleChunk) {
-      const int sidx = (c * QD_CHUNK) / a.block_size;
 #pragma unroll
       for (int x = 0; x < NT; ++x) {
-        const float f0 = __half2float(sc0[x][sidx]), f8 = __half2float(sc8[x][sidx]);
+        const float f0 = fcur0[x], f8 = fcur8[x];
 #pragma unroll
         for (int gi = 0; gi < NG; ++gi) {
           const float* pp = part[x < PX ? x : 0][gi < PG ? gi : 0];
@@ -417,8 +517,8 @@ qdec_prep_kernel(const __half* __restrict__ x, int64_t rows, int K, __half* __re
   }
 }
 
-template <int BITS, bool GATED>
-constexpr int ring_bytes() { return qd_stages<BITS>() * (GATED ? 2 : 1) * 16 * QD_CHUNK * BITS / 8; }
+template <int BITS, bool GATED, int NGMAX>
+constexpr int ring_bytes() { return qd_stages<BITS, NGMAX>() * (GATED ? 2 : 1) * 16 * QD_CHUNK * BITS / 8; }
 
 // NGMAX: most groups of 8 routed rows one pass takes (1, 2 or 4; the host bounds it by the
 // routed rows, so small calls compile only the narrow passes and keep their registers).
@@ -426,13 +526,15 @@ constexpr int ring_bytes() { return qd_stages<BITS>() * (GATED ? 2 : 1) * 16 * Q
 // with 128 and ~400 bytes of spills: 4% faster at C3 T=64 on B200; every other variant
 // measured the same or faster at 4 CTAs per SM.
 template <int BITS, bool GATED, int NGMAX>
-constexpr int qd_min_blocks() { return (BITS == 4 && GATED && NGMAX == 4) ? 3 : 4; }
+constexpr int qd_min_blocks() {
+  return (BITS == 4 && GATED && NGMAX == 4) ? 3 : 4;
+}
 
 template <int BITS, bool GATED, int kScale, bool RAW4, int NGMAX>
 __global__ void __launch_bounds__(QD_WARPS * 32, (qd_min_blocks<BITS, GATED, NGMAX>()))
 qmoe_decode_kernel(const QDecodeArgs a) {
   extern __shared__ __align__(128) uint8_t s_ring[];  // one ring per warp
-  uint8_t* ring = s_ring + (threadIdx.x >> 5) * ring_bytes<BITS, GATED>();
+  uint8_t* ring = s_ring + (threadIdx.x >> 5) * ring_bytes<BITS, GATED, NGMAX>();
   // Launched dependent: every input (offsets, activations) comes from earlier kernels.
   pdl_wait();
   pdl_launch_dependents();
@@ -495,11 +597,11 @@ qmoe_decode_kernel(const QDecodeArgs a) {
   for (int tok0 = 0; tok0 < cnt; tok0 += 8 * NGMAX) {
     const int groups = min(NGMAX, (cnt - tok0 + 7) / 8);
     if (NGMAX == 1 || groups <= 1)
-      run_pass<BITS, 1, GATED, kScale, RAW4>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 1, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>()>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
     else if (NGMAX == 2 || groups <= 2)
-      run_pass<BITS, 2, GATED, kScale, RAW4>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 2, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>()>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
     else
-      run_pass<BITS, 4, GATED, kScale, RAW4>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 4, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>()>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
   }
 }
 
@@ -587,7 +689,7 @@ combine_partials_kernel(const float* __restrict__ part, int splits, int64_t rows
 
 template <int BITS, bool GATED, int kScale, bool RAW4, int NGMAX>
 cudaError_t launch_decode_n(const QDecodeArgs& a, cudaStream_t s) {
-  constexpr int kSmem = QD_WARPS * ring_bytes<BITS, GATED>();
+  constexpr int kSmem = QD_WARPS * ring_bytes<BITS, GATED, NGMAX>();
   static bool attr_set = false;  // idempotent; a race between first callers is benign
   if (!attr_set) {
     cudaError_t st = cudaFuncSetAttribute(qmoe_decode_kernel<BITS, GATED, kScale, RAW4, NGMAX>,

@@ -148,7 +148,7 @@ class ExpertParallelMoE:
         comm.connect(handles)
         self._comm = comm
 
-    def _forward_p2p(self, x, router_probs):
+    def _forward_p2p(self, x, router_probs, events=None):
         T = x.shape[0]
         if self._comm is None:
             self._connect(T, x.device)
@@ -160,8 +160,11 @@ class ExpertParallelMoE:
         nbytes = self._comm.workspace_size(prob)
         if self._ws is None or self._ws.numel() < nbytes:
             self._ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
-        self._comm.forward(prob, dict(self.weights, input=x, router_probs=router_probs,
-                                      output=out), self._ws)
+        tensors = dict(self.weights, input=x, router_probs=router_probs, output=out)
+        if events is not None:
+            self._comm.forward_staged(prob, tensors, self._ws, events)
+        else:
+            self._comm.forward(prob, tensors, self._ws)
         return out
 
     def close(self) -> None:
@@ -172,9 +175,13 @@ class ExpertParallelMoE:
             self._comm.close()
             self._comm = None
 
-    def forward(self, x, router_probs, chunks: int | None = None):
+    def forward(self, x, router_probs, chunks: int | None = None, events=None):
+        """``events`` (p2p transport only): len(EP_PHASES) + 1 timing events recorded at the
+        phase boundaries of the call (``EpComm.forward_staged``)."""
         if self.transport == "p2p":
-            return self._forward_p2p(x, router_probs)
+            return self._forward_p2p(x, router_probs, events)
+        if events is not None:
+            raise ValueError("phase events need the p2p transport")
         return self._forward_collective(x, router_probs, chunks)
 
     def _forward_collective(self, x, router_probs, chunks: int | None = None):
