@@ -335,6 +335,9 @@ def cpu_baseline(cfg, L, budget_s=12.0):
     if n2 > n:
         n, dt = n2, run(n2)
     return {"value": n / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "label": f"C port of the CPU path (oracle/moe_oracle.c, cache-blocked fp32 FMA "
+                     f"GEMM) on {cores} host cores; not the ONNX Runtime CPU EP, which is "
+                     f"unavailable on this box",
             "sample": f"{n} of {T} tokens of the same layer, one call, {dt:.2f} s"}
 
 
