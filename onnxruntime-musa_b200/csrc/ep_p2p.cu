@@ -23,6 +23,7 @@
 // MoE path, fused into the gather and into the fc2 epilogue.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "../../include/moe_b200.h"
@@ -180,6 +181,9 @@ __global__ void __launch_bounds__(kCountsThreads) ep_exchange_counts_kernel(cons
 struct SendArgs {
   EpPeers peers;
   size_t recv_off;
+  size_t tok_off, gidx_off;  // dedup: token buffer and gather index (tok_off 0: off)
+  int rank;
+  int64_t max_rows;
   int E, El;
   const uint8_t* x;
   int64_t row_bytes;
@@ -203,9 +207,44 @@ __global__ void __launch_bounds__(256) ep_send_rows_kernel(const SendArgs a) {
     const int e = a.idx[sidx];
     const int d = e / a.El;
     const int64_t drow = static_cast<int64_t>(a.send_base[e]) + p;
-    const uint4* srow = reinterpret_cast<const uint4*>(a.x + (sidx / a.k) * a.row_bytes);
+    const int t = sidx / a.k;
+    const uint4* srow = reinterpret_cast<const uint4*>(a.x + t * a.row_bytes);
+    if (a.tok_off != 0) {
+      // Receive row drow is gathered from token row rank * max_rows + t at rank d; the
+      // token itself travels once: with its first slot that rank d owns.
+      const int64_t trow = static_cast<int64_t>(a.rank) * a.max_rows + t;
+      if (lane == 0)
+        reinterpret_cast<int32_t*>(a.peers.base[d] + a.gidx_off)[drow] = static_cast<int32_t>(trow);
+      const int j = sidx - t * a.k;
+      bool first = true;
+      for (int j2 = 0; j2 < j; ++j2) first &= a.idx[t * a.k + j2] / a.El != d;
+      if (!first) continue;
+      uint4* trow_ptr = reinterpret_cast<uint4*>(a.peers.base[d] + a.tok_off + trow * a.row_bytes);
+      for (int64_t i = lane; i < vecs; i += 32) trow_ptr[i] = srow[i];
+      continue;
+    }
     uint4* drow_ptr = reinterpret_cast<uint4*>(a.peers.base[d] + a.recv_off + drow * a.row_bytes);
     for (int64_t i = lane; i < vecs; i += 32) drow_ptr[i] = srow[i];
+  }
+}
+
+// Receive row x = token row gidx[x] (own region), one warp per row, rows below the
+// device-side count eoff_total[0].
+__global__ void __launch_bounds__(256)
+ep_gather_tokens_kernel(uint8_t* own, size_t recv_off, size_t tok_off, size_t gidx_off,
+                        int64_t row_bytes, const int32_t* eoff_total, const int* err) {
+  if (*reinterpret_cast<const volatile int*>(err) != 0) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = *eoff_total;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t vecs = row_bytes / 16;
+  const int32_t* gidx = reinterpret_cast<const int32_t*>(own + gidx_off);
+  for (int64_t x = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       x < total; x += warps) {
+    const int64_t trow = gidx[x];
+    const uint4* src = reinterpret_cast<const uint4*>(own + tok_off + trow * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(own + recv_off + x * row_bytes);
+    for (int64_t i = lane; i < vecs; i += 32) dst[i] = src[i];
   }
 }
 
@@ -233,15 +272,26 @@ cudaError_t launch_ep_exchange_counts(const EpPeers& peers, const EpLayout& lay,
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_send_rows(const EpPeers& peers, const EpLayout& lay, int W, int E,
+cudaError_t launch_ep_send_rows(const EpPeers& peers, const EpLayout& lay, int rank, int W, int E,
                                 const void* x, int64_t row_bytes, int k, const int32_t* idx,
                                 const int32_t* src, int64_t rows, const int32_t* send_base,
-                                const int* err, cudaStream_t s) {
+                                int64_t max_rows, bool dedup, const int* err, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
-  SendArgs a{peers, lay.recv, E, E / W, static_cast<const uint8_t*>(x), row_bytes, k, idx, src,
-             rows, send_base, err};
+  if (dedup && lay.tok == 0) return cudaErrorInvalidValue;
+  SendArgs a{peers, lay.recv, dedup ? lay.tok : 0, lay.gidx, rank, max_rows, E, E / W,
+             static_cast<const uint8_t*>(x), row_bytes, k, idx, src, rows, send_base, err};
   const int64_t blocks = std::min<int64_t>((rows + 7) / 8, 148 * 8);
   ep_send_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_gather_tokens(uint8_t* own, const EpLayout& lay, int64_t row_bytes,
+                                    const int32_t* eoff_total, int64_t cap_rows, const int* err,
+                                    cudaStream_t s) {
+  if (lay.tok == 0) return cudaErrorInvalidValue;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((cap_rows + 7) / 8, 148 * 8));
+  ep_gather_tokens_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+      own, lay.recv, lay.tok, lay.gidx, row_bytes, eoff_total, err);
   return cudaGetLastError();
 }
 
@@ -264,7 +314,8 @@ namespace {
 
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-moe::EpLayout ep_layout(int64_t cap_rows, int64_t ret_rows, int64_t row_bytes, int W, int E) {
+moe::EpLayout ep_layout(int64_t cap_rows, int64_t ret_rows, int64_t row_bytes, int W, int E,
+                        int64_t tok_rows) {
   moe::EpLayout l{};
   size_t o = 0;
   l.recv = o;
@@ -275,6 +326,12 @@ moe::EpLayout ep_layout(int64_t cap_rows, int64_t ret_rows, int64_t row_bytes, i
   o = align256(o + 2 * static_cast<size_t>(W) * E * sizeof(int32_t));
   l.flags = o;
   o = align256(o + 3 * moe::kMaxEpRanks * sizeof(uint32_t));
+  if (tok_rows > 0) {
+    l.tok = o;
+    o = align256(o + static_cast<size_t>(tok_rows) * row_bytes);
+    l.gidx = o;
+    o = align256(o + static_cast<size_t>(cap_rows) * sizeof(int32_t));
+  }
   l.total = o;
   return l;
 }
@@ -342,7 +399,8 @@ int moe_b200_ep_comm_create(int32_t rank, int32_t world, int64_t max_rows, int32
   c->cap_rows = static_cast<int64_t>(world) * max_rows * k_max;
   const int64_t row_bytes = hidden_size * 2;
   c->lay = ep_layout(c->cap_rows, max_rows * k_max, row_bytes, world,
-                     static_cast<int>(num_experts));
+                     static_cast<int>(num_experts),
+                     k_max >= moe::kEpDedupMinK ? static_cast<int64_t>(world) * max_rows : 0);
   cudaError_t e = cudaGetDevice(&c->device);
   if (e == cudaSuccess) e = cudaMalloc(&c->sym, c->lay.total);
   if (e == cudaSuccess) e = cudaMemset(c->sym + c->lay.cnt, 0, c->lay.total - c->lay.cnt);

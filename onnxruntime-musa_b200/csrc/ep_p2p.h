@@ -12,8 +12,17 @@ struct EpLayout {
   size_t ret;     // [max_rows * k_max, H]: FFN rows of this rank's tokens, in its permuted order
   size_t cnt;     // int32 [2][W][E]: per-source expert counts (by call parity)
   size_t flags;   // uint32 [3][kMaxEpRanks]: phase flags (epoch of the last signal per source)
+  // Deduplicated dispatch (k_max >= kEpDedupMinK): each token travels once per destination
+  // rank into tok ([W * max_rows, H], source s's token t at row s * max_rows + t), and
+  // gidx[x] (int32 [cap_rows]) names the tok row of receive row x; the receiver gathers
+  // its expert-ordered rows locally.  0 when the region has no such buffers.
+  size_t tok;
+  size_t gidx;
   size_t total;
 };
+
+// Smallest k at which dispatch sends each token once per destination rank.
+constexpr int kEpDedupMinK = 4;
 
 enum EpPhase : int { kEpCounts = 0, kEpRows = 1, kEpReturn = 2 };
 
@@ -39,11 +48,18 @@ struct EpTables {
 cudaError_t launch_ep_exchange_counts(const EpPeers& peers, const EpLayout& lay, int rank,
                                       int W, int E, uint32_t epoch, const int32_t* myoff,
                                       const EpTables& tab, int* err, cudaStream_t s);
-// Copies routed row p (token src[p] / k) into its expert's rank's receive buffer.
-cudaError_t launch_ep_send_rows(const EpPeers& peers, const EpLayout& lay, int W, int E,
+// Copies routed row p (token src[p] / k) into its expert's rank's receive buffer; with
+// `dedup` (lay.tok set) it copies each token once per destination rank into that rank's
+// token buffer (row rank * max_rows + t) and stores the receive row's tok row in gidx.
+cudaError_t launch_ep_send_rows(const EpPeers& peers, const EpLayout& lay, int rank, int W, int E,
                                 const void* x, int64_t row_bytes, int k, const int32_t* idx,
                                 const int32_t* src, int64_t rows, const int32_t* send_base,
-                                const int* err, cudaStream_t s);
+                                int64_t max_rows, bool dedup, const int* err, cudaStream_t s);
+// Receiver side of the deduplicated dispatch: receive row x < eoff[El] (a device count)
+// = token row gidx[x] of the own token buffer.
+cudaError_t launch_ep_gather_tokens(uint8_t* own, const EpLayout& lay, int64_t row_bytes,
+                                    const int32_t* eoff_total, int64_t cap_rows, const int* err,
+                                    cudaStream_t s);
 // After a system-scope fence, stores `epoch` into flag [phase][rank] of every rank.
 cudaError_t launch_ep_signal(const EpPeers& peers, const EpLayout& lay, int rank, int W,
                              int phase, uint32_t epoch, cudaStream_t s);

@@ -694,8 +694,14 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
                                            T > 0 ? i32(L.myoff) : nullptr, tab, err, s),
                  "count exchange");
   mark(2);
-  MOE_CUDA_CHECK(launch_ep_send_rows(c->peers, c->lay, W, E, t.input, static_cast<int64_t>(H) * es,
-                                     k, i32(L.idx), i32(L.src), R, tab.send_base, err, s),
+  // Deduplicated dispatch when a token's k experts often share a rank (k >= 4): each
+  // token crosses NVLink once per destination and the receiver gathers its rows locally.
+  // MOE_B200_EP_DEDUP=0/1 forces it (1 needs a region created with k_max >= 4).
+  const char* dd = std::getenv("MOE_B200_EP_DEDUP");
+  const bool dedup = c->lay.tok != 0 && (dd != nullptr ? dd[0] != '0' : k >= kEpDedupMinK);
+  MOE_CUDA_CHECK(launch_ep_send_rows(c->peers, c->lay, r, W, E, t.input,
+                                     static_cast<int64_t>(H) * es, k, i32(L.idx), i32(L.src), R,
+                                     tab.send_base, c->max_rows, dedup, err, s),
                  "send rows");
   // MOE_B200_TEST_STALL=1 (tests only): the rows and return flags are never raised, so the
   // bounded waits expire and the call reports device error kErrTimeoutPeer.
@@ -704,6 +710,10 @@ int ep_forward_impl(moe_b200_ep_comm* c, const moe_b200_problem& p, const moe_b2
     MOE_CUDA_CHECK(launch_ep_signal(c->peers, c->lay, r, W, kEpRows, epoch, s), "signal rows");
   mark(3);
   MOE_CUDA_CHECK(launch_ep_wait(c->sym, c->lay, W, kEpRows, epoch, err, s), "wait rows");
+  if (dedup)
+    MOE_CUDA_CHECK(launch_ep_gather_tokens(c->sym, c->lay, static_cast<int64_t>(H) * es,
+                                           tab.eoff + El, c->cap_rows, err, s),
+                   "gather received tokens");
 
   mark(4);
   // Expert FFN on the received rows (row count known on the device only: the GEMMs are

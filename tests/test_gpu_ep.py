@@ -100,6 +100,33 @@ def test_ep_p2p_single_rank_ragged_calls(pkg, orc, dev):
     layer.close()
 
 
+def test_ep_p2p_dedup_dispatch_is_bit_identical(pkg, orc, dev):
+    """k >= 4: each token crosses to a rank once and the receiver gathers its expert rows
+    locally (MOE_B200_EP_DEDUP); the expert rows, and so the outputs, are the same bits as
+    with one copy per (token, expert)."""
+    import torch
+    from onnxruntime_musa_b200 import ep
+    d, weights, attrs = _moe_case(orc, dev, 500, 256, 384, 16, 8, 29, "float16")
+    outs = []
+    for flag in ("1", "0"):
+        os.environ["MOE_B200_EP_DEDUP"] = flag
+        try:
+            layer = ep.ExpertParallelMoE(pkg, num_experts=16, hidden_size=256, inter_size=384,
+                                         dtype=pkg.FLOAT16, has_fc3=True, local_weights=weights,
+                                         transport="p2p", **attrs)
+            outs.append(layer.forward(d["x"], d["router_probs"]))
+            outs.append(layer.forward(d["x"][:123].contiguous(), d["router_probs"][:123].contiguous()))
+            torch.cuda.synchronize()
+            layer.close()
+        finally:
+            del os.environ["MOE_B200_EP_DEDUP"]
+    assert torch.equal(outs[0], outs[2]) and torch.equal(outs[1], outs[3])
+    h = {n: as_np(v) for n, v in d.items()}
+    ref = orc.moe(h["x"], h["router_probs"], h["fc1_w"], h["fc1_b"], h["fc2_w"], h["fc2_b"],
+                  h["fc3_w"], h["fc3_b"], **attrs)
+    np.testing.assert_allclose(as_np(outs[0]), ref, **TOL["float16"])
+
+
 def _nccl_worker(rank, world, port, q, transport="p2p", E=8, kind="moe"):
     """One rank of a `world`-rank expert-parallel layer over NCCL (device-side p2p exchange
     or NCCL all-to-all).  Each rank routes its own tokens; two calls, the second ragged
@@ -116,9 +143,9 @@ def _nccl_worker(rank, world, port, q, transport="p2p", E=8, kind="moe"):
         pkg, orc = ge.load_package(), ge.load_oracle()
         from onnxruntime_musa_b200 import ep
         T_r = 256
-        if kind == "moe":
-            d, weights, attrs = _moe_case(orc, dev, T_r * world, 512, 256, E, 2, 33 + E,
-                                          "float16")
+        if kind in ("moe", "moe_k8"):
+            d, weights, attrs = _moe_case(orc, dev, T_r * world, 512, 256, E,
+                                          8 if kind == "moe_k8" else 2, 33 + E, "float16")
             h = {n: as_np(v) for n, v in d.items()}
             ref_fn = lambda x, lg: orc.moe(x, lg, h["fc1_w"], h["fc1_b"], h["fc2_w"],
                                            h["fc2_b"], h["fc3_w"], h["fc3_b"], **attrs)
@@ -164,6 +191,7 @@ def _nccl_worker(rank, world, port, q, transport="p2p", E=8, kind="moe"):
 
 @pytest.mark.parametrize("world,transport,E,kind", [
     (2, "p2p", 8, "moe"), (2, "collective", 8, "moe"), (2, "p2p", 2, "moe"),
+    (2, "p2p", 16, "moe_k8"), (8, "p2p", 64, "moe_k8"),
     (2, "p2p", 8, "qmoe4"), (2, "p2p", 16, "qmoe8"), (2, "collective", 8, "qmoe4"),
     (4, "p2p", 8, "moe"), (4, "p2p", 16, "qmoe8"), (8, "p2p", 64, "moe"), (8, "p2p", 16, "qmoe8")],
     ids=lambda v: str(v))
