@@ -342,6 +342,47 @@ def cpu_baseline(cfg, L, budget_s=12.0):
 
 
 # ------------------------------------------------------------------ our arm
+def host_copy_ceiling(hx, hl, hout, dev, steps, warmup, world):
+    """The host-copy part of an e2e step alone: per step the H2D copies of the step's
+    tokens and logits (one stream) and the D2H copy of an output-sized buffer (another
+    stream), back to back with no compute, on every rank at once (wall clock, max over
+    ranks).  If the e2e step is not longer than this, the host copies bound it."""
+    import torch
+    import torch.distributed as dist
+    dx = torch.empty(hx.shape, dtype=hx.dtype, device=dev)
+    dl = torch.empty(hl.shape, dtype=hl.dtype, device=dev)
+    dout = torch.zeros(hout.shape, dtype=hout.dtype, device=dev)
+    cin, cout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def step():
+        with torch.cuda.stream(cin):
+            dx.copy_(hx, non_blocking=True)
+            dl.copy_(hl, non_blocking=True)
+        with torch.cuda.stream(cout):
+            hout.copy_(dout, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize(dev)
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    nbytes = (hx.numel() * hx.element_size() + hl.numel() * hl.element_size() +
+              hout.numel() * hout.element_size())
+    return {"copy_only_ms_per_step": round(ms, 4),
+            "host_copy_gbs_per_gpu": round(nbytes / (ms / 1e3) / 1e9, 1),
+            "host_copy_gbs_all_gpus": round(world * nbytes / (ms / 1e3) / 1e9, 1)}
+
+
+
 def adjacent_ops(pkg, cfg, L, dev, stream, args, pk):
     """The pre-MoE rows of the same tokens (residual add + RMS norm + router MatMul,
     moe_b200_norm_router), timed with CUDA events against the HBM roofline."""
@@ -509,7 +550,9 @@ def bench_ours(args, cfg, rank, world, dev):
            "d2h_bytes_per_step": hout.numel() * es,
            "api": "moe_b200_pipeline_submit (host buffers, copies overlapped across steps)",
            "serial_value": world * T / (serial_ms / 1e3),
-           "serial_api": "moe_b200_kernel_compute, one call at a time (H2D, layer, D2H)"}
+           "serial_api": "moe_b200_kernel_compute, one call at a time (H2D, layer, D2H)",
+           "host_copies_alone": host_copy_ceiling(hx, hl, hout, dev, args.steps, args.warmup,
+                                                  world)}
 
     pk = peaks()
     adjacent = adjacent_ops(pkg, cfg, L, dev, stream, args, pk)
@@ -697,6 +740,7 @@ def bench_ep(args, cfg, rank, world, dev):
     dist.all_reduce(tw, op=dist.ReduceOp.MAX)
     e2e_ms = float(tw.item())
     dist.barrier()
+    copy_ceiling = host_copy_ceiling(hx, hl, hout, dev, args.steps, args.warmup, world)
     pk = peaks()
     alg = algorithmic(cfg, L, pkg)
     es = hx.element_size()
@@ -716,7 +760,8 @@ def bench_ep(args, cfg, rank, world, dev):
                 "h2d_bytes_per_step": hx.numel() * es + hl.numel() * es,
                 "d2h_bytes_per_step": hout.numel() * es,
                 "api": "ep.HostPipeline over ExpertParallelMoE.forward (host buffers, copies "
-                       "overlapped across steps)"},
+                       "overlapped across steps)",
+                "host_copies_alone": copy_ceiling},
         "roofline": {"bound": "tensor", "kernel": "expert-parallel layer (all stages, per rank)",
                      "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["tflops"], 4), "traffic": None,
