@@ -102,6 +102,22 @@ bool same_shape(const moe_b200_prepacked& a, const moe_b200_prepacked& b) {
          a.n1 == b.n1 && a.has_fc3 == b.has_fc3 && a.bits == b.bits && a.block == b.block;
 }
 
+// A registered prepack whose key and shape match is shared only if its dequantised copies
+// are, bit for bit, those of the new weights: the 64-bit key is a sum of mixed words, so
+// different weights can collide (deliberately, too); equal dequantised copies are exactly
+// the condition under which sharing gives the same outputs.
+int same_content(const moe_b200_prepacked& e, const moe_b200_problem& p,
+                 const moe_b200_tensors& t, cudaStream_t s, bool* differs) {
+  int* diff = nullptr;
+  cudaError_t ce = cudaMalloc(&diff, sizeof(int));
+  if (ce != cudaSuccess)
+    return set_error(MOE_B200_EP_FAIL, "prepack compare: %s", cudaGetErrorString(ce));
+  const QmoeDequantOut have{e.w1, e.w2, e.w3};
+  const int st = qmoe_dequantized_differs(p, t, have, diff, s, differs);
+  cudaFree(diff);
+  return st;
+}
+
 void free_prepack(moe_b200_prepacked* pk) {
   if (pk->base != nullptr) cudaFree(pk->base);  // waits for work in flight on the device
   delete pk;
@@ -177,6 +193,13 @@ int moe_b200_prepack_create(const moe_b200_problem* problem, const moe_b200_tens
     std::lock_guard<std::mutex> lock(moe::g_registry_mu);
     for (moe_b200_prepacked* e : moe::g_registry) {
       if (e->key == pk->key && moe::same_shape(*e, *pk)) {
+        bool differs = true;
+        st = moe::same_content(*e, p, t, s, &differs);
+        if (st != MOE_B200_OK) {
+          delete pk;
+          return st;
+        }
+        if (differs) continue;  // a hash collision: these weights get their own copy
         e->refs.fetch_add(1);
         delete pk;
         *out = e;
@@ -211,7 +234,9 @@ int moe_b200_prepack_create(const moe_b200_problem* problem, const moe_b200_tens
     std::lock_guard<std::mutex> lock(moe::g_registry_mu);
     // Another thread may have registered the same content meanwhile: keep one copy.
     for (moe_b200_prepacked* e : moe::g_registry) {
-      if (e->key == pk->key && moe::same_shape(*e, *pk)) {
+      bool differs = true;
+      if (e->key == pk->key && moe::same_shape(*e, *pk) &&
+          moe::same_content(*e, p, t, s, &differs) == MOE_B200_OK && !differs) {
         e->refs.fetch_add(1);
         moe::free_prepack(pk);
         *out = e;

@@ -92,6 +92,57 @@ cudaError_t dequant_t(const void* q, const void* scales, int64_t rows, int K, in
   return cudaGetLastError();
 }
 
+// Sets *diff when out[r, c] differs (bitwise) from the dequantisation the kernels above
+// would write for codes q and scales (scales == nullptr: exact codes).
+template <typename T>
+__global__ void __launch_bounds__(256)
+dequant_compare_kernel(const uint8_t* __restrict__ q, const T* __restrict__ scales, int64_t rows,
+                       int K, int bits, int block_size, int num_blocks, const T* __restrict__ out,
+                       int* __restrict__ diff) {
+  const int64_t total = rows * K;
+  const int64_t row_bytes = bits == 4 ? (K + 1) / 2 : K;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / K;
+    const int c = static_cast<int>(i - r * K);
+    int code;
+    if (bits == 4) {
+      const uint8_t b = q[r * row_bytes + c / 2];
+      code = ((c & 1) ? (b >> 4) : (b & 0xF)) - 8;
+    } else {
+      code = static_cast<int>(q[r * row_bytes + c]) - 128;
+    }
+    const float s = scales == nullptr ? 1.f
+                    : block_size == 0  ? to_f(scales[r])
+                                       : to_f(scales[r * num_blocks + c / block_size]);
+    const T v = from_f<T>(static_cast<float>(code) * s);
+    if (*reinterpret_cast<const uint16_t*>(&v) != reinterpret_cast<const uint16_t*>(out)[i])
+      *diff = 1;
+  }
+}
+
+template <typename T>
+cudaError_t dequant_compare_t(const void* q, const void* scales, int64_t rows, int K, int bits,
+                              int block_size, const void* out, int* diff, cudaStream_t s) {
+  const int nb = block_size ? (K + block_size - 1) / block_size : 0;
+  const int blocks = static_cast<int>(std::min<int64_t>((rows * K + 255) / 256, 148 * 16));
+  dequant_compare_kernel<T><<<blocks, 256, 0, s>>>(
+      static_cast<const uint8_t*>(q), static_cast<const T*>(scales), rows, K, bits, block_size,
+      nb, static_cast<const T*>(out), diff);
+  return cudaGetLastError();
+}
+
+cudaError_t dequant_compare(int dtype, const void* q, const void* scales, int64_t rows, int K,
+                            int bits, int block_size, const void* out, int* diff,
+                            cudaStream_t s) {
+  if (rows == 0 || K == 0) return cudaSuccess;
+  if (dtype == kDtF16)
+    return dequant_compare_t<__half>(q, scales, rows, K, bits, block_size, out, diff, s);
+  if (dtype == kDtBF16)
+    return dequant_compare_t<__nv_bfloat16>(q, scales, rows, K, bits, block_size, out, diff, s);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t dequant(int dtype, const void* q, const void* scales, int64_t rows, int K, int bits,
                     int block_size, void* out, cudaStream_t s) {
   if (rows == 0 || K == 0) return cudaSuccess;
@@ -365,6 +416,31 @@ int qmoe_dequantize_into(const moe_b200_problem& p, const moe_b200_tensors& t, u
   out->w1 = w1;
   out->w2 = w2;
   out->w3 = p.has_fc3 ? w3 : nullptr;
+  return MOE_B200_OK;
+}
+
+int qmoe_dequantized_differs(const moe_b200_problem& p, const moe_b200_tensors& t,
+                             const QmoeDequantOut& have, int* diff_dev, cudaStream_t s,
+                             bool* differs) {
+  const int64_t E = p.num_experts, H = p.hidden_size, I = p.inter_size;
+  const int bits = p.attrs.expert_weight_bits, bs = p.attrs.block_size;
+  const bool exact = qmoe_dequantized_exact(p);
+  auto sc = [&](const void* scales) { return exact ? nullptr : scales; };
+  cudaError_t st = cudaMemsetAsync(diff_dev, 0, sizeof(int), s);
+  if (st == cudaSuccess)
+    st = dequant_compare(p.dtype, t.fc1_weights, sc(t.fc1_scales), E * fc1_rows(p),
+                         static_cast<int>(H), bits, bs, have.w1, diff_dev, s);
+  if (st == cudaSuccess)
+    st = dequant_compare(p.dtype, t.fc2_weights, sc(t.fc2_scales), E * H, static_cast<int>(I),
+                         bits, bs, have.w2, diff_dev, s);
+  if (st == cudaSuccess && p.has_fc3)
+    st = dequant_compare(p.dtype, t.fc3_weights, sc(t.fc3_scales), E * I, static_cast<int>(H),
+                         bits, bs, have.w3, diff_dev, s);
+  int h = 0;
+  if (st == cudaSuccess) st = cudaMemcpyAsync(&h, diff_dev, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (st == cudaSuccess) st = cudaStreamSynchronize(s);
+  if (st != cudaSuccess) return set_error(MOE_B200_EP_FAIL, "prepack compare: %s", cudaGetErrorString(st));
+  *differs = h != 0;
   return MOE_B200_OK;
 }
 

@@ -51,6 +51,12 @@ bool qmoe_dequantized_exact(const moe_b200_problem& p);
 int qmoe_dequantize_into(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* dst,
                          QmoeDequantOut* out, cudaStream_t s);
 
+// Compares, bit for bit, the dequantised copies `have` with what qmoe_dequantize_into would
+// write for the weights in `t` (diff_dev: one device int of scratch); synchronises `s`.
+int qmoe_dequantized_differs(const moe_b200_problem& p, const moe_b200_tensors& t,
+                             const QmoeDequantOut& have, int* diff_dev, cudaStream_t s,
+                             bool* differs);
+
 // Dequantises fc1/fc2(/fc3) of every expert into `ws` in element type p.dtype.
 int qmoe_dequantize(const moe_b200_problem& p, const moe_b200_tensors& t, uint8_t* ws,
                     const int32_t* expert_offsets, QmoeDequantOut* out, cudaStream_t s);

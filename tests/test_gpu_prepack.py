@@ -219,3 +219,37 @@ def test_pipeline_with_prepack_and_mixed_sizes(pkg, orc, dev):
     for n, o in zip(sizes, outs):
         ref = _oracle(orc, dict(q, x=q["x"][:n], router_probs=q["router_probs"][:n]), attrs)
         np.testing.assert_allclose(o.numpy(), ref, **TOL["float16"])
+
+
+def test_sharing_refuses_hash_collisions(pkg, orc, dev):
+    """The sharing key is an order-independent sum over 8-byte words, so swapping two
+    different words of the codes gives a colliding key for other weights; the registry
+    compares the dequantised copies and gives the new weights a prepack of their own."""
+    import torch
+    case = (64, 256, 256, 4, 2, 8, 0)
+    q, attrs = _inputs(orc, case, seed=23)
+    T, H, I, E, k, bits, bs = case
+    prob = pkg.make_problem(T, H, I, E, pkg.FLOAT16, has_fc3=True, activation_type="silu", k=k,
+                            normalize_routing_weights=1, expert_weight_bits=bits, block_size=bs)
+
+    def weights(qq):
+        return {n: to_dev(np.ascontiguousarray(qq[m]), dev) for n, m in
+                [("fc1_weights", "fc1_q"), ("fc1_scales", "fc1_scales"), ("fc2_weights", "fc2_q"),
+                 ("fc2_scales", "fc2_scales"), ("fc3_weights", "fc3_q"),
+                 ("fc3_scales", "fc3_scales")]}
+
+    q2 = dict(q)
+    codes = q["fc1_q"].copy()
+    flat = codes.reshape(-1).view(np.uint64)
+    j = int(np.nonzero(flat != flat[0])[0][0])
+    flat[0], flat[j] = flat[j].copy(), flat[0].copy()  # same multiset of words, other weights
+    q2["fc1_q"] = codes
+    a = pkg.Prepacked(prob, weights(q), share=True)
+    b = pkg.Prepacked(prob, weights(q2), share=True)
+    assert b.handle.value != a.handle.value, "colliding weights shared a prepack"
+    assert a.info()[1] == 1 and b.info()[1] == 1
+    c = pkg.Prepacked(prob, weights(q2), share=True)  # equal to b: shared with b
+    assert c.handle.value == b.handle.value and b.info()[1] == 2
+    for x in (c, b, a):
+        x.release()
+    torch.cuda.synchronize()
