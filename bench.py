@@ -531,7 +531,7 @@ def bench_ours(args, cfg, rank, world, dev):
     # copies its inputs from pinned host memory and its output back; the copies of
     # neighbouring steps overlap this step's compute.  Wall clock from the first submit
     # to the completion of the last D2H, max over ranks.
-    with pkg.Pipeline(prob, tens, depth=2) as pl:
+    with pkg.Pipeline(prob, tens, depth=args.pipeline_depth) as pl:
         if wpk is not None:
             pl.set_prepacked(wpk)
         for _ in range(args.warmup):
@@ -814,6 +814,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--prepack", action="store_true",
                     help="QMoE: dequantise the weights once before timing (weight prepack)")
+    ap.add_argument("--pipeline-depth", type=int, default=2,
+                    help="staging slots of the host-buffer pipeline (e2e)")
     ap.add_argument("--ep-chunks", type=int, default=None,
                     help="token chunks pipelined through the expert-parallel exchange "
                          "(default 1)")
