@@ -148,6 +148,29 @@ static void gemm_micro(int64_t kc, const float* const* a, const float* bp, float
   }
 }
 
+/* The same micro-tile on AVX-512 hosts: 12 rows of 16 accumulators, one 16-wide vector
+ * each (selected at run time; the library itself is built for AVX2). */
+typedef float v16 __attribute__((vector_size(64)));
+enum { GEMM_MR16 = 12 };
+
+__attribute__((target("avx512f"))) static void gemm_micro16(int64_t kc, const float* const* a,
+                                                              const float* bp, float* acc) {
+  v16 c[GEMM_MR16];
+  for (int r = 0; r < GEMM_MR16; ++r) c[r] = (v16){0};
+  for (int64_t k = 0; k < kc; ++k) {
+    v16 b;
+    memcpy(&b, bp + k * GEMM_NR, sizeof(v16));
+    for (int r = 0; r < GEMM_MR16; ++r) c[r] += a[r][k] * b;
+  }
+  for (int r = 0; r < GEMM_MR16; ++r) memcpy(acc + r * GEMM_NR, &c[r], sizeof(v16));
+}
+
+static int use_avx512(void) {
+  static int v = -1;
+  if (v < 0) v = __builtin_cpu_supports("avx512f") ? 1 : 0;
+  return v;
+}
+
 static void gemm_range(int64_t p_begin, int64_t p_end, void* p) {
   gemm_ctx* g = (gemm_ctx*)p;
   const float *A = g->A, *B = g->B, *bias = g->bias;
@@ -155,7 +178,9 @@ static void gemm_range(int64_t p_begin, int64_t p_end, void* p) {
   const int64_t M = g->M, N = g->N, K = g->K;
   float* bp = (float*)aligned_alloc(64, sizeof(float) * GEMM_KC * GEMM_NR);
   float* zero = (float*)calloc((size_t)(K > 0 ? K : 1), sizeof(float));
-  float acc[GEMM_MR * GEMM_NR];
+  float acc[GEMM_MR16 * GEMM_NR];
+  const int wide = use_avx512();
+  const int64_t mr = wide ? GEMM_MR16 : GEMM_MR;
   for (int64_t k0 = 0; k0 < K; k0 += GEMM_KC) {
     const int64_t kc = K - k0 < GEMM_KC ? K - k0 : GEMM_KC;
     for (int64_t pn = p_begin; pn < p_end; ++pn) {
@@ -165,11 +190,12 @@ static void gemm_range(int64_t p_begin, int64_t p_end, void* p) {
         const float* b = j < nn ? B + (n0 + j) * K + k0 : zero;
         for (int64_t k = 0; k < kc; ++k) bp[k * GEMM_NR + j] = b[k];
       }
-      for (int64_t m0 = 0; m0 < M; m0 += GEMM_MR) {
-        const float* a[GEMM_MR];
-        const int64_t mm = M - m0 < GEMM_MR ? M - m0 : GEMM_MR;
-        for (int r = 0; r < GEMM_MR; ++r) a[r] = r < mm ? A + (m0 + r) * K + k0 : zero;
-        gemm_micro(kc, a, bp, acc);
+      for (int64_t m0 = 0; m0 < M; m0 += mr) {
+        const float* a[GEMM_MR16];
+        const int64_t mm = M - m0 < mr ? M - m0 : mr;
+        for (int r = 0; r < GEMM_MR16; ++r) a[r] = r < mm ? A + (m0 + r) * K + k0 : zero;
+        if (wide) gemm_micro16(kc, a, bp, acc);
+        else gemm_micro(kc, a, bp, acc);
         for (int64_t r = 0; r < mm; ++r) {
           float* c = C + (m0 + r) * N + n0;
           const float* s = acc + r * GEMM_NR;
