@@ -38,6 +38,7 @@
 // sums [split][row][col] and the combine kernel adds splits in a fixed order, so the
 // result is deterministic.
 #include <algorithm>
+#include <cstdlib>
 #include "qmoe_decode.h"
 
 namespace moe {
@@ -707,8 +708,13 @@ cudaError_t launch_decode_n(const QDecodeArgs& a, cudaStream_t s) {
 // An expert holds at most all routed rows: groups of 8 per pass up to min(4, ceil(rows / 8)).
 template <int BITS, bool GATED, int kScale, bool RAW4>
 cudaError_t launch_decode_t(const QDecodeArgs& a, cudaStream_t s) {
-  if (a.rows <= 8) return launch_decode_n<BITS, GATED, kScale, RAW4, 1>(a, s);
-  if (a.rows <= 16) return launch_decode_n<BITS, GATED, kScale, RAW4, 2>(a, s);
+  // MOE_B200_QDEC_MAXNG=1/2 caps the groups of one pass (measurement runs).
+  static const int max_ng = [] {
+    const char* v = std::getenv("MOE_B200_QDEC_MAXNG");
+    return v != nullptr ? std::atoi(v) : 4;
+  }();
+  if (a.rows <= 8 || max_ng <= 1) return launch_decode_n<BITS, GATED, kScale, RAW4, 1>(a, s);
+  if (a.rows <= 16 || max_ng <= 2) return launch_decode_n<BITS, GATED, kScale, RAW4, 2>(a, s);
   return launch_decode_n<BITS, GATED, kScale, RAW4, 4>(a, s);
 }
 
