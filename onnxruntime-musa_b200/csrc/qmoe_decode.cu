@@ -131,7 +131,7 @@ __device__ __forceinline__ int64_t stored_row(const QOperand& b, int e, int n, i
          b.g;
 }
 
-template <int BITS, int NG, bool GATED, int kScale, bool RAW4, int STAGES>
+template <int BITS, int NG, bool GATED, int kScale, bool RAW4, int STAGES, bool PF>
 __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_begin, int cnt,
                                          int tok0, int n0, int c_begin, int c_end, int split,
                                          uint8_t* ring) {
@@ -224,78 +224,66 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
   // computes: they come from L2, and a load issued just before its use would stall the warp
   // for a full L2 round trip every chunk.
   [[maybe_unused]] const uint32_t bias6400 = opaque_bias();
-  // One-group passes only: wider passes hold too many registers for a second copy.
-  constexpr bool kPf = NG == 1;
+  // One-group passes of one-group kernels only (PF): wider passes, and the kernels that
+  // also hold them, have no registers for a second buffer.
+  constexpr bool kPf = PF && NG == 1;
   constexpr int M = QD_CHUNK / 32;
-  uint4 xnext[M][NG];
-  float onext[NG][2];
-  float fnext0[NT], fnext8[NT];
-  auto load_x = [&](int cc) {
+  // Two register buffers of prefetched values, used in turn by consecutive chunks (no
+  // copies between them).
+  uint4 xbuf[2][M][NG];
+  float obuf[2][NG][2];
+  float fbuf0[2][NT], fbuf8[2][NT];
+  auto load_x = [&](int cc, uint4 (&xd)[M][NG], float (&od)[NG][2]) {
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi)
-        xnext[m][gi] = tok_ok[gi]
-                           ? __ldg(reinterpret_cast<const uint4*>(xrow[gi] + cc * QD_CHUNK + 8 * m))
-                           : make_uint4(0u, 0u, 0u, 0u);
+        xd[m][gi] = tok_ok[gi]
+                        ? __ldg(reinterpret_cast<const uint4*>(xrow[gi] + cc * QD_CHUNK + 8 * m))
+                        : make_uint4(0u, 0u, 0u, 0u);
     if constexpr (kRaw4) {
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) {
-        onext[gi][0] = __ldg(crow[gi][0] + cc);
-        onext[gi][1] = __ldg(crow[gi][1] + cc);
+        od[gi][0] = __ldg(crow[gi][0] + cc);
+        od[gi][1] = __ldg(crow[gi][1] + cc);
       }
     }
   };
-  auto load_scales = [&](int si) {
+  auto load_scales = [&](int si, float (&f0d)[NT], float (&f8d)[NT]) {
     if constexpr (kScale == kScaleChunk) {
 #pragma unroll
       for (int x = 0; x < NT; ++x) {
-        fnext0[x] = __half2float(sc0[x][si]);
-        fnext8[x] = __half2float(sc8[x][si]);
+        f0d[x] = __half2float(sc0[x][si]);
+        f8d[x] = __half2float(sc8[x][si]);
       }
     }
   };
   if (kPf && c_begin < c_end) {
-    load_x(c_begin);
-    load_scales(sblk);
+    load_x(c_begin, xbuf[0], obuf[0]);
+    load_scales(sblk, fbuf0[0], fbuf8[0]);
   }
-  for (int c = c_begin; c < c_end; ++c) {
+  // One chunk: reads the buffer `cur` (prefetched, or loaded now in wider passes) and
+  // prefetches the next chunk into `nxt`.
+  auto chunk = [&](int c, uint4 (&xcur)[M][NG], float (&ocur)[NG][2], float (&fcur0)[NT],
+                   float (&fcur8)[NT], uint4 (&xnxt)[M][NG], float (&onxt)[NG][2],
+                   float (&fnxt0)[NT], float (&fnxt8)[NT]) {
     if (!kPf) {
       if constexpr (kRaw4) {
 #pragma unroll
         for (int gi = 0; gi < NG; ++gi) {
-          onext[gi][0] = __ldg(crow[gi][0] + c);
-          onext[gi][1] = __ldg(crow[gi][1] + c);
+          ocur[gi][0] = __ldg(crow[gi][0] + c);
+          ocur[gi][1] = __ldg(crow[gi][1] + c);
         }
       }
-      load_scales(sblk);
-    }
-    uint4 xcur[M][NG];
-    float ocur[NG][2];
-    float fcur0[NT], fcur8[NT];
-    if constexpr (kPf) {
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int gi = 0; gi < NG; ++gi) xcur[m][gi] = xnext[m][gi];
-    }
-#pragma unroll
-    for (int gi = 0; gi < NG; ++gi) {
-      ocur[gi][0] = onext[gi][0];
-      ocur[gi][1] = onext[gi][1];
-    }
-#pragma unroll
-    for (int x = 0; x < NT; ++x) {
-      fcur0[x] = fnext0[x];
-      fcur8[x] = fnext8[x];
+      load_scales(sblk, fcur0, fcur8);
     }
     if (kScale == kScaleChunk && ++ssub == cpb) {
       ssub = 0;
       ++sblk;
     }
     if (kPf && c + 1 < c_end) {
-      load_x(c + 1);
-      load_scales(sblk);
+      load_x(c + 1, xnxt, onxt);
+      load_scales(sblk, fnxt0, fnxt8);
     }
     cp_async_wait<STAGES - 2>();
     __syncwarp();
@@ -430,6 +418,16 @@ __device__ __forceinline__ void run_pass(const QDecodeArgs& a, int e, int row_be
         }
       }
     }
+    };
+  if constexpr (kPf) {
+    for (int c = c_begin; c < c_end; c += 2) {
+      chunk(c, xbuf[0], obuf[0], fbuf0[0], fbuf8[0], xbuf[1], obuf[1], fbuf0[1], fbuf8[1]);
+      if (c + 1 < c_end)
+        chunk(c + 1, xbuf[1], obuf[1], fbuf0[1], fbuf8[1], xbuf[0], obuf[0], fbuf0[0], fbuf8[0]);
+    }
+  } else {
+    for (int c = c_begin; c < c_end; ++c)
+      chunk(c, xbuf[0], obuf[0], fbuf0[0], fbuf8[0], xbuf[0], obuf[0], fbuf0[0], fbuf8[0]);
   }
   cp_async_wait<0>();
   __syncwarp();
@@ -598,11 +596,11 @@ qmoe_decode_kernel(const QDecodeArgs a) {
   for (int tok0 = 0; tok0 < cnt; tok0 += 8 * NGMAX) {
     const int groups = min(NGMAX, (cnt - tok0 + 7) / 8);
     if (NGMAX == 1 || groups <= 1)
-      run_pass<BITS, 1, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>()>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 1, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>(), NGMAX == 1>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
     else if (NGMAX == 2 || groups <= 2)
-      run_pass<BITS, 2, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>()>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 2, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>(), NGMAX == 1>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
     else
-      run_pass<BITS, 4, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>()>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
+      run_pass<BITS, 4, GATED, kScale, RAW4, qd_stages<BITS, NGMAX>(), NGMAX == 1>(a, e, row_begin, cnt, tok0, n0, c_begin, c_end, split, ring);
   }
 }
 
