@@ -704,8 +704,14 @@ __device__ __forceinline__ bool epilogue_swapped(const TcParams& p, const PairTi
       const int my_tok = c + (lane & 15);
       const unsigned long long my_row =
           my_tok < t.rows ? reinterpret_cast<unsigned long long>(out_row<T>(p, t.r0 + my_tok)) : 0ull;
+      if (p.qepi == 2) {  // biased codes: s_n * (acc - (1024 + zp) * rowsum[row])
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = v[j] * sc + b;
+        for (int j = 0; j < 16; ++j)
+          v[j] = sc * (v[j] - p.qbias * __ldg(p.rowsum + t.r0 + min(c + j, t.rows - 1))) + b;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = v[j] * sc + b;
+      }
       act_chunk<16>(p.ap.act, v);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -1131,7 +1137,8 @@ template <int BITS, int QEPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Q_THREADS, 1)
 tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_q1,
-                     const __grid_constant__ CUtensorMap map_q3, const TcParams p) {
+                     const __grid_constant__ CUtensorMap map_q3,
+                     const __grid_constant__ CUtensorMap map_a_sw, const TcParams p) {
   pdl_wait();  // launched dependent (launch_dependent): predecessors' data after this
   pdl_launch_dependents();
   constexpr int PB = q_packed_bytes<BITS>();
@@ -1218,9 +1225,13 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
       int stage = 0;
       uint32_t phase = 0;
       for (int L = pair; L < total && !*abort_flag && !p.test_stall; L += npairs) {
-        int e, m, n;
-        decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
-        const int row0 = s_offs[e] + m * P_BM + static_cast<int>(rank) * BM;
+        // A swapped tail tile (ungated pass, <= swap_max rows) loads only its rows: nt / 2
+        // per CTA in boxes of SW_TOK_ROWS (the weights then act as the MMA's M side).
+        const PairTile t = pair_tile(L, s_tiles, s_offs, p);
+        const int row0 = t.nt ? t.r0 + static_cast<int>(rank) * (t.nt / 2)
+                              : t.r0 + static_cast<int>(rank) * BM;
+        const int tok_boxes = (t.nt / 2 + SW_TOK_ROWS - 1) / SW_TOK_ROWS;
+        const uint32_t a_tx = t.nt ? 2u * tok_boxes * SW_TOK_ROWS * BK * 2 : 2u * A_BYTES;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&emptyA[stage], phase ^ 1)) {
             atomicExch(p.err, kErrTimeoutProducer);
@@ -1228,8 +1239,14 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
             break;
           }
           const uint32_t full_leader = mapa_shared(smem_u32(&fullA[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&fullA[stage], 2 * A_BYTES);
-          tma_load_2d_pair(sA + stage * A_BYTES, &map_a, full_leader, kb * BK, row0);
+          if (leader) mbar_arrive_expect_tx(&fullA[stage], a_tx);
+          if (t.nt) {
+            for (int j = 0; j < tok_boxes; ++j)
+              tma_load_2d_pair(sA + stage * A_BYTES + j * SW_TOK_ROWS * BK * 2, &map_a_sw,
+                               full_leader, kb * BK, row0 + j * SW_TOK_ROWS);
+          } else {
+            tma_load_2d_pair(sA + stage * A_BYTES, &map_a, full_leader, kb * BK, row0);
+          }
           if (++stage == QA) { stage = 0; phase ^= 1; }
         }
       }
@@ -1275,6 +1292,8 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        const PairTile t = pair_tile(L, s_tiles, s_offs, p);
+        const uint32_t id = t.nt ? idesc_f16(0u, P_BM, t.nt) : idesc;
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&fullA[sa], pa) || !mbar_wait(&cdone[sb], pb)) {
@@ -1284,12 +1303,14 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + sa * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + sb * B_HALF);
+          const uint32_t x_addr = smem_u32(sA + sa * A_BYTES);
+          const uint32_t w_addr = smem_u32(sB + sb * B_HALF);
+          const uint32_t a_addr = t.nt ? w_addr : x_addr;
+          const uint32_t b_addr = t.nt ? x_addr : w_addr;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             tc_mma_f16_pair(d_tmem, smem_desc_k_sw128(a_addr + kk * 32),
-                            smem_desc_k_sw128(b_addr + kk * 32), idesc,
+                            smem_desc_k_sw128(b_addr + kk * 32), id,
                             (kb | kk) != 0 ? 1u : 0u);
           }
           tc_commit_pair(&emptyA[sa], 0x3);
@@ -1391,6 +1412,8 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
     const int r_in_tile = static_cast<int>(rank) * BM + q * 32 + lane;
     int ec0, ec1;
     epi_cols(p, warp, ec0, ec1);
+    const Exchange no_xch{nullptr, nullptr, nullptr};
+    uint32_t xuse = 0;
     int i = 0;
     for (int L = pair; L < total && !*abort_flag; L += npairs, ++i) {
       const int acc = i & 1;
@@ -1401,13 +1424,21 @@ tc_pair_qgemm_kernel(const __grid_constant__ CUtensorMap map_a,
         break;
       }
       tc_fence_after();
-      int e, m, n;
-      decode_tile(L, s_tiles, E, p.n_tiles, e, m, n);
-      const int row = s_offs[e] + m * P_BM + r_in_tile;
-      const bool valid = row < s_offs[e + 1];
+      const PairTile t = pair_tile(L, s_tiles, s_offs, p);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      epilogue_rows<__half>(p, taddr, row, valid, e, p.gated ? n * (BN / 2) : n * BN, ec0, ec1,
-                            epi_stage + (warp - 2) * EPI_STAGE_BYTES, lane);
+      if (t.nt) {  // ungated passes only: the gate/linear exchange is never used
+        if (!epilogue_swapped<__half>(p, t, taddr, static_cast<int>(rank), q, lane,
+                                      warp < 6 ? 0 : 1, no_xch, xuse)) {
+          atomicExch(p.err, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+          break;
+        }
+      } else {
+        const int row = t.r0 + r_in_tile;
+        const bool valid = row < t.r0 + t.rows;
+        epilogue_rows<__half>(p, taddr, row, valid, t.e, p.gated ? t.n * (BN / 2) : t.n * BN,
+                              ec0, ec1, epi_stage + (warp - 2) * EPI_STAGE_BYTES, lane);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
@@ -1683,6 +1714,12 @@ cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.qepi = QEPI;
   p.qbias = 1024.0f + static_cast<float>(1 << (BITS - 1));
   p.rowsum = g.rowsum;
+  // Swapped tail tiles in the ungated pass (fc2): the last m-tile of an expert with at most
+  // swap_max rows runs with the converted weights as M and its rows as N.
+  p.swap_max = g.gated ? 0 : std::max(0, std::min(g.swap_max, kPairSwapLimit)) / 16 * 16;
+  CUtensorMap ma_sw = ma;
+  if (p.swap_max > 0 && !make_map_a(&ma_sw, g.dtype, g.a, g.rows, g.K, SW_TOK_ROWS))
+    return cudaErrorInvalidValue;
   p.seg_start = g.seg_start;
   p.seg_dst = g.seg_dst;
   p.nseg = g.nseg;
@@ -1699,7 +1736,7 @@ cudaError_t launch_q(const GemmArgs& g, int num_sms, cudaStream_t s) {
   const int64_t ub = ((g.rows + P_BM - 1) / P_BM + g.E) * p.n_tiles;
   const int64_t pairs = std::min<int64_t>(ub, num_sms / 2);
   return launch_dependent(pdl_layer_enabled(), tc_pair_qgemm_kernel<BITS, QEPI>, dim3(static_cast<unsigned>(2 * pairs)),
-                          dim3(Q_THREADS), q_smem_bytes<BITS>(), s, ma, mq1, mq3, p);
+                          dim3(Q_THREADS), q_smem_bytes<BITS>(), s, ma, mq1, mq3, ma_sw, p);
 }
 
 }  // namespace
